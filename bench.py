@@ -1,0 +1,355 @@
+"""Benchmark: E8 + rANS KV-cache encode -> full decode.
+
+Workload (per rank, weak scaling): a Llama-3.1-8B-shaped KV cache, 32 layers
+x 8 KV heads x head_dim 128, batch 1, seq 8192, bf16; K = N(0,1) * exp(N(0,1))
+per (layer, head, channel) with one outlier channel x10 per (layer, head)
+(1% of 128), V = N(0,1); 4 bits/dim.  One chunk per (layer, K/V) as the
+reference's prefill makes them (llm/compressed_kv_cache.py:360-361): 64 chunks
+of 8 heads x 131072 E8 blocks = 67,108,864 blocks per step.
+
+A step = encode every chunk (scales, E8 + symbols, tables, rANS lanes) and
+decode every chunk back to bf16.  value = E8 blocks round-tripped per second
+(Gvec/s), inputs resident in HBM (1 GiB > L2, so no flush is needed).
+e2e = the same through the public API from pinned host memory: H2D of the
+bf16 cache, compress, decompress, D2H of the decoded cache.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+N_LAYERS, N_KV, SEQ, HD, BITS = 32, 8, 8192, 128, 4
+N_CHUNKS = 2 * N_LAYERS
+BPH = SEQ * HD // 8
+BLOCKS = N_CHUNKS * N_KV * BPH
+TILE = 1024
+METRIC = "E8+rANS encode/decode Gvec/s"
+UNIT = "Gvec/s"
+
+
+def make_cache(gen_device, seed, n_layers=N_LAYERS):
+    """Synthetic config-2 K/V, chunk c = 2*layer + (0: K, 1: V) -> (2*layers, 8, 8192, 128) bf16."""
+    import torch
+
+    g = torch.Generator(device=gen_device)
+    g.manual_seed(1000 + seed)
+    x = torch.empty(2 * n_layers, N_KV, SEQ, HD, dtype=torch.bfloat16, device=gen_device)
+    for layer in range(n_layers):
+        s_c = torch.exp(torch.randn(N_KV, 1, HD, generator=g, device=gen_device))
+        out_ch = torch.randint(0, HD, (N_KV,), generator=g, device=gen_device)
+        s_c[torch.arange(N_KV, device=gen_device), 0, out_ch] *= 10.0
+        x[2 * layer] = (torch.randn(N_KV, SEQ, HD, generator=g, device=gen_device) * s_c).to(torch.bfloat16)
+        x[2 * layer + 1] = torch.randn(N_KV, SEQ, HD, generator=g, device=gen_device).to(torch.bfloat16)
+    return x
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = str(gpu_index)
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", self.gpu, f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [p.strip() for p in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def cpu_baseline(n_threads, sample_chunks=2, reps=1):
+    """The C oracle port (oracle/lq_oracle_codec.c) on a bounded sample of the workload."""
+    import numpy as np
+
+    import oracle.lq_oracle as O
+
+    O.build()
+    rng = np.random.default_rng(7)
+    x = np.empty((sample_chunks, N_KV, SEQ, HD), np.float32)
+    for c in range(sample_chunks):
+        if c % 2 == 0:
+            s_c = np.exp(rng.standard_normal((N_KV, 1, HD))).astype(np.float32)
+            s_c[np.arange(N_KV), 0, rng.integers(0, HD, N_KV)] *= 10.0
+            x[c] = rng.standard_normal((N_KV, SEQ, HD)).astype(np.float32) * s_c
+        else:
+            x[c] = rng.standard_normal((N_KV, SEQ, HD)).astype(np.float32)
+    # bf16 bit patterns (round to nearest even)
+    u = x.view(np.uint32)
+    xb = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        O.codec_roundtrip_batch(xb, O.DT_BF16, sample_chunks, N_KV, BPH, BITS, TILE, O.DT_BF16, n_threads)
+    dt = time.perf_counter() - t0
+    blocks = reps * sample_chunks * N_KV * BPH
+    return blocks / dt / 1e9, blocks, dt
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU path (C oracle port) on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    n_thr = os.cpu_count() or 1
+    sample = max(2, min(N_CHUNKS, 2 * n_thr))
+    for _ in range(args.warmup):
+        cpu_baseline(n_thr, sample_chunks=2)
+    vals = []
+    for _ in range(args.steps):
+        v, blocks, dt = cpu_baseline(n_thr, sample_chunks=sample)
+        vals.append(v)
+    v = statistics.median(vals)
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": BLOCKS / (v * 1e9) * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded config-2 K/V)",
+            "config": {"workload": "config2: Llama-3.1-8B KV 32Lx8Hx8192x128 bf16, 4 b/dim, encode+decode",
+                       "global_batch": 1, "seq_len": SEQ, "parallelism": "host threads",
+                       "l2": "inputs larger than L2"},
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": n_thr, "kind": "port",
+                             "sample": f"{sample} of 64 chunks per step (oracle/lq_oracle_codec.c, pthreads)"},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--layers", type=int, default=N_LAYERS,
+                    help="layers of the cache (profiling runs use fewer; bench lines use 32)")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+
+    from latticequant_b200 import codec as C
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    global N_CHUNKS, BLOCKS
+    N_CHUNKS = 2 * args.layers
+    BLOCKS = N_CHUNKS * N_KV * BPH
+    x = make_cache(dev, rank, args.layers)
+    geom = C.Geometry(N_CHUNKS, N_KV, BPH, TILE)
+    cd = C.Codec(geom, dev)
+    out = torch.empty(BLOCKS * 8, dtype=torch.bfloat16, device=dev)
+
+    def step():
+        cd.encode(x, BITS)
+        cd.expand_tables(enc=False, dec=True)
+        cd.decode(out)
+
+    # launches per step: scales 2, quantize 1, tables 2 (+1 expand dec), encode 5, decode 4
+    launches_per_step = (1 if C.lib().lq_head_scales_workspace(N_CHUNKS * N_KV, BPH * 8) == 0 else 2) + 1 + 2 + 5 + 1 + 4
+
+    # correctness gate: one eager step, error word clear, lossless round trip on a sample chunk
+    step()
+    torch.cuda.synchronize()
+    if cd.read_err():
+        raise RuntimeError(f"device error flags {cd.read_err():#x}")
+
+    graph = None
+    if not args.no_graph:
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            step()
+        torch.cuda.current_stream(dev).wait_stream(s)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+
+    def run():
+        if graph is not None:
+            graph.replay()
+        else:
+            step()
+
+    for _ in range(max(args.warmup, 3)):
+        run()
+    torch.cuda.synchronize()
+
+    # phase timing (eager, CUDA events on the launching stream) for the roofline
+    st = torch.cuda.current_stream(dev)
+    names = ["scales", "quantize", "tables", "encode", "expand_dec", "decode"]
+    acc = {n: 0.0 for n in names}
+    reps = 3
+    for _ in range(reps):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
+        ev[0].record(st)
+        cd.scales(x, BITS); ev[1].record(st)
+        cd.quantize(x); ev[2].record(st)
+        cd.build_tables(); cd.expand_tables(enc=True, dec=False); ev[3].record(st)
+        cd.entropy_encode(); ev[4].record(st)
+        cd.expand_tables(enc=False, dec=True); ev[5].record(st)
+        cd.decode(out); ev[6].record(st)
+        torch.cuda.synchronize()
+        for i, n in enumerate(names):
+            acc[n] += ev[i].elapsed_time(ev[i + 1]) / reps
+    n_words = cd.n_words()
+    comp_bytes = 4 * n_words + N_CHUNKS * ((N_KV * BPH + 7) // 8) + 2 * N_CHUNKS * N_KV
+
+    # timed region
+    sampler = ClockSampler(local)
+    barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    time.sleep(0.3)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(args.steps):
+        run()
+    e1.record(st)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = world * BLOCKS / (ms * 1e-3) / 1e9
+
+    # e2e through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        host_x = x.cpu().pin_memory()
+        host_out = torch.empty(BLOCKS * 8, dtype=torch.bfloat16).pin_memory()
+        dx = torch.empty_like(x)
+        for _ in range(2):
+            dx.copy_(host_x, non_blocking=True)
+            cd.encode(dx, BITS); cd.expand_tables(enc=False, dec=True); cd.decode(out)
+            host_out.copy_(out, non_blocking=True)
+        torch.cuda.synchronize()
+        barrier()
+        f0 = torch.cuda.Event(enable_timing=True)
+        f1 = torch.cuda.Event(enable_timing=True)
+        k2 = max(2, min(args.steps, 5))
+        f0.record(st)
+        for _ in range(k2):
+            dx.copy_(host_x, non_blocking=True)
+            cd.encode(dx, BITS); cd.expand_tables(enc=False, dec=True); cd.decode(out)
+            host_out.copy_(out, non_blocking=True)
+        f1.record(st)
+        torch.cuda.synchronize()
+        ems = f0.elapsed_time(f1) / k2
+        if world > 1:
+            t = torch.tensor([ems], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ems = float(t.item())
+        e2e = {"value": world * BLOCKS / (ems * 1e-3) / 1e9, "unit": UNIT,
+               "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": out.numel() * 2,
+               "ms_per_step": ems}
+
+    # roofline of the dominant kernel phase, on algorithmic bytes (config-2 per-block figures)
+    peak, peak_kind = measured_peaks()
+    comp_per_block = comp_bytes / BLOCKS
+    enc_alg = BLOCKS * (16.0 + comp_per_block)     # bf16 in + compressed out
+    dec_alg = BLOCKS * (comp_per_block + 16.0)     # compressed in + bf16 out
+    alg = {"scales": BLOCKS * 16.0, "quantize": enc_alg, "tables": 0.0, "encode": enc_alg, "expand_dec": 0.0,
+           "decode": dec_alg}
+    dom = max(names, key=lambda n: acc[n])
+    achieved = alg[dom] / (acc[dom] * 1e-3) / 1e9
+
+    cpu = None
+    if rank == 0 and not args.no_cpu:
+        n_thr = os.cpu_count() or 1
+        v, blocks, dt = cpu_baseline(n_thr, sample_chunks=max(2, min(8, n_thr)))
+        cpu = {"value": v, "unit": UNIT, "cores": n_thr, "kind": "port",
+               "sample": f"{blocks} blocks ({blocks // (N_KV * BPH)} chunks of config 2), "
+                         f"oracle/lq_oracle_codec.c on {n_thr} threads, {dt:.1f} s"}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded config-2 K/V)",
+                "config": {"workload": f"config2: Llama-3.1-8B KV {args.layers}Lx8Hx8192x128 bf16, 4 b/dim, "
+                                       "encode+decode",
+                           "global_batch": world, "seq_len": SEQ, "parallelism": f"dp{world} (chunks per rank)",
+                           "tile_blocks": TILE, "l2": "inputs larger than L2 (1 GiB per rank)",
+                           "cuda_graph": graph is not None},
+                "bits_per_dim": comp_bytes * 8 / (BLOCKS * 8),
+                "phase_ms": {n: round(acc[n], 4) for n in names},
+                "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
+                             "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None},
+                "clocks": clocks, "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
+                "cpu_baseline": cpu}
+        print(json.dumps(line), flush=True)
+    if graph is not None:
+        del graph
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

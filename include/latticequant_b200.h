@@ -1,0 +1,189 @@
+/*
+ * latticequant_b200.h -- C ABI of the B200 (sm_100a) LatticeQuant KV-cache
+ * codec library (latticequant_b200/liblq_b200.so).
+ *
+ * Every entry point is asynchronous on the CUDA stream it is given
+ * (cudaStream_t passed as void*, NULL = legacy default stream), takes device
+ * pointers and plain sizes, allocates nothing, and returns an LQ_* status for
+ * argument / launch errors.  Data-dependent failures (alphabet larger than L,
+ * corrupt bitstream, ...) are raised by the kernels as LQ_EF_* bits OR-ed
+ * into a caller-provided device word `err`, readable after the stream
+ * synchronises.  No kernel traps or asserts.
+ *
+ * Data layout (one "chunk" = one tensor handed to
+ * CompressedKVCache._compress_tensor, reference llm/compressed_kv_cache.py:176):
+ *   x        [n_chunks][n_heads][bph][8] elements, bph = seq*head_dim/8
+ *   block    one 8-element E8 vector; N = n_heads*bph blocks per chunk
+ *   tile     TB consecutive blocks of a chunk (TB multiple of 32); the last
+ *            tile of a chunk may be short
+ *   stream s 8*coset + coord (coord 7 carries coord8_half)
+ *   lane     (chunk, tile, s): the symbols of stream s whose blocks lie in
+ *            the tile, rANS-coded with the chunk's table for s; each lane is
+ *            one reference-format stream (core/gpu_ans.py:105-139)
+ *   words    all lanes of all chunks back to back, lane l at
+ *            [lane_off[l], lane_off[l+1]), ceil(n_bits/32) words each
+ */
+#ifndef LATTICEQUANT_B200_H
+#define LATTICEQUANT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---- */
+#define LQ_OK 0
+#define LQ_ERR_INVALID (-1)  /* bad argument: null pointer, size, dtype, alignment */
+#define LQ_ERR_ALPHABET (-2) /* a stream alphabet exceeds L = 1024 symbols */
+#define LQ_ERR_CAPACITY (-3) /* an output buffer is too small */
+#define LQ_ERR_CUDA (-4)     /* CUDA launch / runtime error */
+#define LQ_ERR_STREAM (-5)   /* corrupt bitstream / metadata */
+
+/* ---- device error flags (OR-ed into *err by kernels) ---- */
+#define LQ_EF_ALPHABET 0x1u   /* table build: alphabet > L (reference hangs here) */
+#define LQ_EF_SYMRANGE 0x2u   /* a lattice coordinate outside [-LQ_SYM_LIMIT, LQ_SYM_LIMIT) */
+#define LQ_EF_CAPACITY 0x4u   /* compressed output larger than the given capacity */
+#define LQ_EF_BITSTREAM 0x8u  /* lane metadata points outside the word buffer */
+#define LQ_EF_NONFINITE 0x10u /* non-finite input or scaled input */
+#define LQ_EF_NOCONVERGE 0x20u /* table normalisation did not converge */
+
+/* ---- dtypes ---- */
+#define LQ_F32 0
+#define LQ_F16 1
+#define LQ_BF16 2
+
+#define LQ_L 1024          /* rANS table size, core/gpu_ans.py:44-45 */
+#define LQ_SYM_LIMIT 512   /* lattice coordinates must lie in [-512, 512) */
+#define LQ_HIST_BINS 1024  /* per-stream histogram bins, value v -> bin v + 512 */
+#define LQ_NSTREAMS 16
+
+/* Library version (major*10000 + minor*100 + patch). */
+int lq_version(void);
+
+/* Human-readable text for an LQ_* status. */
+const char *lq_strerror(int status);
+
+/* ------------------------------------------------------------------------
+ * Per-head variance and scale.
+ * Replaces llm/compressed_kv_cache.py:183-196 (sigma2 = mean(t^2) per head,
+ * scale = sqrt(2*pi*e*sigma2*4^-b), 1.0 where sigma2 < 1e-12, fp16 copy) and
+ * core/e8_quantizer.py:137-148 (compute_scale).  The sum of squares follows
+ * torch's CPU reduction tree bit for bit; sqrt is IEEE.
+ *   x            [n_heads_total][elems_per_head], dtype LQ_F32/F16/BF16
+ *   vol_mult     fp32(4 ** -bits)
+ *   sigma2, scale_f32, scale_f16 [n_heads_total] (each may be NULL)
+ *   workspace    lq_head_scales_workspace() bytes (may be NULL when that is 0)
+ * ---------------------------------------------------------------------- */
+size_t lq_head_scales_workspace(int64_t n_heads_total, int64_t elems_per_head);
+int lq_head_scales(const void *x, int dtype, int64_t n_heads_total, int64_t elems_per_head, float vol_mult,
+                   float *sigma2, float *scale_f32, uint16_t *scale_f16, void *workspace, size_t workspace_bytes,
+                   void *stream);
+
+/* ------------------------------------------------------------------------
+ * E8 quantisation + parity-aware symbolisation + coset packing + histograms.
+ * Replaces the E8 / symbol part of _compress_tensor
+ * (llm/compressed_kv_cache.py:198-228): x / scale -> encode_e8
+ * (core/e8_quantizer.py:61-83) -> e8_to_symbols (core/entropy_coder.py:46-68)
+ * -> pack_coset_bits (llm/compressed_kv_cache.py:46-54), plus the per-stream
+ * counts that feed build_rans_table (:236-253).
+ *   scale_f32    [n_chunks][n_heads]
+ *   sym_rows     [n_chunks][n_tiles][TB][8] int16: in each tile, coset-0
+ *                blocks in block order, then coset-1 blocks in reverse order
+ *   coset_words  [n_chunks][ceil(N/32)] u32, bit i of word w = block 32w+i
+ *   tile_n0      [n_chunks][n_tiles] number of coset-0 blocks per tile
+ *   hist         [n_chunks][16][LQ_HIST_BINS] u32, zeroed by this call
+ *   deq          optional [n_chunks][N][8] in deq_dtype: q * scale_f32 (the
+ *                buffer update() returns, :204); NULL to skip
+ *   q_out        optional [n_chunks][N][8] fp32 lattice points; NULL to skip
+ * ---------------------------------------------------------------------- */
+int lq_e8_quantize(const void *x, int dtype, int64_t n_chunks, int64_t n_heads, int64_t bph, const float *scale_f32,
+                   int64_t tile_blocks, int16_t *sym_rows, uint32_t *coset_words, uint32_t *tile_n0, uint32_t *hist,
+                   void *deq, int deq_dtype, float *q_out, uint32_t *err, void *stream);
+
+/* Plain encode_e8 (core/e8_quantizer.py:61-83) / encode_d8 (:20-58) on (n,8) fp32. */
+int lq_encode_e8(const float *x, int64_t n, float *out, int d8_only, void *stream);
+
+/* ------------------------------------------------------------------------
+ * rANS tables from histograms.
+ * Replaces build_rans_table (core/gpu_ans.py:62-98) with the alphabet rule
+ * of llm/compressed_kv_cache.py:246-250 ([min-2, max+2]).  Ties in the
+ * normalisation are broken by ascending symbol index.
+ *   hist         [n_tables][LQ_HIST_BINS]
+ *   tab_lo       [n_tables] first alphabet value
+ *   tab_nsym     [n_tables] alphabet size (0 = empty stream)
+ *   tab_freq     [n_tables][LQ_L] u16 normalised frequencies
+ * lq_expand_tables turns frequencies into the packed coder tables used by
+ * lq_rans_encode (enc_tab) and lq_rans_decode (dec_tab), [n_tables][LQ_L]
+ * u32 each; either may be NULL.
+ * ---------------------------------------------------------------------- */
+int lq_build_tables(const uint32_t *hist, int64_t n_tables, int32_t *tab_lo, int32_t *tab_nsym, uint16_t *tab_freq,
+                    uint32_t *err, void *stream);
+int lq_expand_tables(const int32_t *tab_nsym, const uint16_t *tab_freq, int64_t n_tables, uint32_t *enc_tab,
+                     uint32_t *dec_tab, uint32_t *err, void *stream);
+
+/* ------------------------------------------------------------------------
+ * Lane encode.  Replaces rans_encode (core/gpu_ans.py:105-139) run over
+ * the 16 streams of each chunk (llm/compressed_kv_cache.py:236-268).
+ *   words        [words_cap] output, lanes back to back
+ *   lane_off     [n_chunks*n_tiles*16 + 1] u32 word offsets (last = total)
+ *   lane_nbits   [n_lanes] u32, lane_state [n_lanes] u32 (final state = the
+ *                decoder's initial state)
+ *   workspace    lq_rans_encode_workspace() bytes
+ * ---------------------------------------------------------------------- */
+size_t lq_rans_encode_workspace(int64_t n_chunks, int64_t n_vectors, int64_t tile_blocks);
+int lq_rans_encode(const int16_t *sym_rows, const uint32_t *tile_n0, int64_t n_chunks, int64_t n_vectors,
+                   int64_t tile_blocks, const int32_t *tab_lo, const int32_t *tab_nsym, const uint32_t *enc_tab,
+                   uint32_t *words, int64_t words_cap, uint32_t *lane_off, uint32_t *lane_nbits,
+                   uint32_t *lane_state, void *workspace, size_t workspace_bytes, uint32_t *err, void *stream);
+
+/* ------------------------------------------------------------------------
+ * Lane decode + dequantisation.  Replaces _decompress_chunk
+ * (llm/compressed_kv_cache.py:289-332): gpu_rans_decode of every stream,
+ * unpack_coset_bits, symbols_to_e8 (core/entropy_coder.py:71-89) and
+ * multiplication by the fp16 per-head scale, output in out_dtype.
+ *   dec_tab      [n_chunks*16][LQ_L] from lq_expand_tables
+ *   out          [n_chunks][N][8] in out_dtype (NULL to skip)
+ *   sym_out      optional [n_chunks][N][8] int32 decoded symbols
+ *   workspace    lq_rans_decode_workspace() bytes
+ * ---------------------------------------------------------------------- */
+size_t lq_rans_decode_workspace(int64_t n_chunks, int64_t n_vectors, int64_t tile_blocks);
+int lq_rans_decode(const uint32_t *words, int64_t n_words, const uint32_t *lane_off, const uint32_t *lane_nbits,
+                   const uint32_t *lane_state, const uint32_t *coset_words, const uint32_t *tile_n0,
+                   int64_t n_chunks, int64_t n_heads, int64_t bph, int64_t tile_blocks, const int32_t *tab_lo,
+                   const int32_t *tab_nsym, const uint16_t *tab_freq, const uint32_t *dec_tab,
+                   const uint16_t *scale_f16, void *out, int out_dtype, int32_t *sym_out, void *workspace,
+                   size_t workspace_bytes, uint32_t *err, void *stream);
+
+/* ------------------------------------------------------------------------
+ * Reference-stream decode: the argument meaning of _rans_decode_kernel
+ * (core/gpu_ans.py:175-235) as prepared by prepare_gpu_decode (:274-342):
+ * bit offsets, n_bits, initial states, symbol counts, per-table lookup /
+ * freqs / cumfreqs / alphabet padded to max_sym, table id per stream, int64
+ * output at out_offsets.  One thread per stream.
+ * ---------------------------------------------------------------------- */
+int lq_rans_decode_streams(const uint32_t *bitstream, int64_t n_words, const int64_t *bit_offsets,
+                           const int64_t *n_bits, const int64_t *init_states, const int64_t *n_decode,
+                           const int32_t *lookup, const int32_t *freqs, const int32_t *cumfreqs,
+                           const int32_t *alphabet, const int32_t *table_id, int64_t max_sym, int64_t n_streams,
+                           int64_t *out, const int64_t *out_offsets, uint32_t *err, void *stream);
+
+/* ------------------------------------------------------------------------
+ * Compact fixed-rate layout (core/compact_storage.py:87-222).
+ * lq_pack_e8: q (n,8) fp32 valid in-range E8 points -> (n,b) bytes; counts
+ * of invalid / out-of-range rows go to n_bad[0] / n_bad[1] (u32, zeroed by
+ * the call) so the host can raise the reference's ValueError.
+ * lq_unpack_e8: (n,b) bytes -> q (n,8) fp32, or, with scales != NULL,
+ * (q * scales[head_idx[i]]) rounded to fp16 -- triton_unpack_e8_4bit
+ * (core/triton_dequant.py:139-177) for b = 4.
+ * ---------------------------------------------------------------------- */
+int lq_pack_e8(const float *q, int64_t n, int bits, uint8_t *out, uint32_t *n_bad, void *stream);
+int lq_unpack_e8(const uint8_t *packed, int64_t n, int bits, const float *scales, const int32_t *head_idx,
+                 float *q_out, uint16_t *f16_out, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LATTICEQUANT_B200_H */

@@ -1,0 +1,216 @@
+// lq_quantize.cu -- E8 quantisation, symbolisation, coset packing, histograms.
+//
+// Reference: llm/compressed_kv_cache.py:198-253
+//   x_scaled = t_heads / scale; all_q = encode_e8(x_scaled)       (core/e8_quantizer.py:61-83)
+//   decompressed_out = (all_q * scale).to(orig_dtype)
+//   coset, free, c8h = e8_to_symbols(all_q)                       (core/entropy_coder.py:46-68)
+//   per (coset, coord) stream: counts over the chunk -> build_rans_table
+//   coset_packed = pack_coset_bits(coset)                         (:46-54)
+//
+// One warp walks one tile of TB blocks, 32 blocks per step, one block per
+// lane: a 16-byte (or 2x16-byte for fp32) load of the block, the E8 search
+// in registers, and per step one ballot that is directly the 32-bit word of
+// the packed coset bitmap.  The ballot also ranks each block inside its
+// coset, which places its 8 symbols as one 16-byte row of the tile's
+// symbol buffer: coset-0 rows from the front in block order, coset-1 rows
+// from the back -- so each rANS lane later reads its symbols contiguously,
+// last symbol first.  Symbol counts go to a shared-memory histogram per CTA
+// (values in [-128, 128)), falling back to global atomics outside that
+// window, and are flushed once per CTA.
+#include "lq_common.cuh"
+
+namespace lq {
+namespace {
+
+constexpr int kQWarps = 8;          // tiles per CTA
+constexpr int kSmemHalf = 128;      // shared histogram window [-128, 128)
+constexpr int kSmemBins = 2 * kSmemHalf;
+
+template <int DT, int DQ>
+__global__ void __launch_bounds__(32 * kQWarps) quantize_kernel(
+    const void *__restrict__ x, int64_t n_heads, int64_t bph, const float *__restrict__ scale_f32, int64_t TB,
+    int64_t n_tiles, int16_t *__restrict__ sym_rows, uint32_t *__restrict__ coset_words, uint32_t *__restrict__ tile_n0,
+    uint32_t *__restrict__ hist, void *__restrict__ deq, float *__restrict__ q_out, uint32_t *__restrict__ err) {
+    __shared__ uint32_t sh_hist[LQ_NSTREAMS * kSmemBins];
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int64_t chunk = blockIdx.y;
+    const int64_t N = n_heads * bph;
+    const int64_t words_per_chunk = ceil_div(N, 32);
+
+    for (int i = threadIdx.x; i < LQ_NSTREAMS * kSmemBins; i += blockDim.x) sh_hist[i] = 0;
+    __syncthreads();
+
+    const int64_t tile = (int64_t)blockIdx.x * kQWarps + warp;
+    uint32_t flags = 0;
+    if (tile < n_tiles) {
+        const int64_t b0 = tile * TB;
+        const int64_t tb = (b0 + TB <= N) ? TB : N - b0;
+        const int64_t cblk0 = chunk * N;  // first block of the chunk in x
+        int16_t *rows = sym_rows + (chunk * n_tiles + tile) * TB * 8;
+        int64_t n0 = 0, n1 = 0;  // running coset counts
+        for (int64_t off = 0; off < tb; off += 32) {
+            const int64_t b = b0 + off + lane;  // block within chunk
+            const bool active = (off + lane) < tb;
+            int sym[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            int coset = 0;
+            if (active) {
+                const int64_t head = b / bph;
+                const float sc = scale_f32[chunk * n_heads + head];
+                float v[8], xs[8], q[8];
+                load_block8<DT>(x, cblk0 + b, v);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    xs[i] = __fdiv_rn(v[i], sc);
+                    if (!isfinite(xs[i])) flags |= LQ_EF_NONFINITE;
+                }
+                e8_nearest(xs, q);
+                if constexpr (DQ >= 0) {
+                    float o[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) o[i] = __fmul_rn(q[i], sc);
+                    store_block8<DQ>(deq, cblk0 + b, o);
+                }
+                if (q_out) {
+                    float4 *qp = reinterpret_cast<float4 *>(q_out) + 2 * (cblk0 + b);
+                    qp[0] = make_float4(q[0], q[1], q[2], q[3]);
+                    qp[1] = make_float4(q[4], q[5], q[6], q[7]);
+                }
+                coset = e8_symbols(q, sym);
+                // symbols must fit the histogram window (float->int saturates, so huge values land outside)
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    if (sym[i] < -LQ_SYM_LIMIT || sym[i] >= LQ_SYM_LIMIT) flags |= LQ_EF_SYMRANGE;
+            }
+            const uint32_t ball = __ballot_sync(0xffffffffu, active && coset);
+            const uint32_t act = __ballot_sync(0xffffffffu, active);
+            if (lane == 0) coset_words[chunk * words_per_chunk + (b0 + off) / 32] = ball;
+            const uint32_t lt = (1u << lane) - 1u;
+            if (active) {
+                int64_t row;
+                if (coset) {
+                    row = tb - 1 - (n1 + __popc(ball & lt));
+                } else {
+                    row = n0 + __popc(act & ~ball & lt);
+                }
+                uint4 packed;
+                packed.x = (uint32_t)(uint16_t)sym[0] | ((uint32_t)(uint16_t)sym[1] << 16);
+                packed.y = (uint32_t)(uint16_t)sym[2] | ((uint32_t)(uint16_t)sym[3] << 16);
+                packed.z = (uint32_t)(uint16_t)sym[4] | ((uint32_t)(uint16_t)sym[5] << 16);
+                packed.w = (uint32_t)(uint16_t)sym[6] | ((uint32_t)(uint16_t)sym[7] << 16);
+                reinterpret_cast<uint4 *>(rows)[row] = packed;
+                uint32_t *gh = hist + (chunk * LQ_NSTREAMS + coset * 8) * LQ_HIST_BINS;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int v = sym[i];
+                    if (v >= -kSmemHalf && v < kSmemHalf) {
+                        atomicAdd(&sh_hist[(coset * 8 + i) * kSmemBins + v + kSmemHalf], 1u);
+                    } else if (v >= -LQ_SYM_LIMIT && v < LQ_SYM_LIMIT) {
+                        atomicAdd(&gh[i * LQ_HIST_BINS + v + LQ_SYM_LIMIT], 1u);
+                    }
+                }
+            }
+            const int c1 = __popc(ball);
+            n1 += c1;
+            n0 += __popc(act) - c1;
+        }
+        if (lane == 0) tile_n0[chunk * n_tiles + tile] = (uint32_t)n0;
+    }
+    if (flags) raise_flag(err, flags);
+    __syncthreads();
+    uint32_t *gh = hist + chunk * LQ_NSTREAMS * LQ_HIST_BINS;
+    for (int i = threadIdx.x; i < LQ_NSTREAMS * kSmemBins; i += blockDim.x) {
+        const uint32_t c = sh_hist[i];
+        if (c) {
+            const int s = i / kSmemBins, v = i % kSmemBins - kSmemHalf;
+            atomicAdd(&gh[s * LQ_HIST_BINS + v + LQ_SYM_LIMIT], c);
+        }
+    }
+}
+
+template <int DT, int DQ>
+int launch_quantize(const void *x, int64_t n_chunks, int64_t n_heads, int64_t bph, const float *scale_f32, int64_t TB,
+                    int16_t *sym_rows, uint32_t *coset_words, uint32_t *tile_n0, uint32_t *hist, void *deq,
+                    float *q_out, uint32_t *err, cudaStream_t st) {
+    const int64_t N = n_heads * bph;
+    const int64_t n_tiles = ceil_div(N, TB);
+    dim3 grid((unsigned)ceil_div(n_tiles, kQWarps), (unsigned)n_chunks);
+    quantize_kernel<DT, DQ><<<grid, 32 * kQWarps, 0, st>>>(x, n_heads, bph, scale_f32, TB, n_tiles, sym_rows,
+                                                            coset_words, tile_n0, hist, deq, q_out, err);
+    return check_launch();
+}
+
+template <int DT>
+int dispatch_deq(int deq_dtype, const void *x, int64_t n_chunks, int64_t n_heads, int64_t bph, const float *sc,
+                 int64_t TB, int16_t *sym_rows, uint32_t *cw, uint32_t *tn0, uint32_t *hist, void *deq, float *q_out,
+                 uint32_t *err, cudaStream_t st) {
+    if (deq == nullptr)
+        return launch_quantize<DT, -1>(x, n_chunks, n_heads, bph, sc, TB, sym_rows, cw, tn0, hist, deq, q_out, err,
+                                       st);
+    switch (deq_dtype) {
+        case LQ_F32:
+            return launch_quantize<DT, LQ_F32>(x, n_chunks, n_heads, bph, sc, TB, sym_rows, cw, tn0, hist, deq, q_out,
+                                               err, st);
+        case LQ_F16:
+            return launch_quantize<DT, LQ_F16>(x, n_chunks, n_heads, bph, sc, TB, sym_rows, cw, tn0, hist, deq, q_out,
+                                               err, st);
+        case LQ_BF16:
+            return launch_quantize<DT, LQ_BF16>(x, n_chunks, n_heads, bph, sc, TB, sym_rows, cw, tn0, hist, deq,
+                                                q_out, err, st);
+        default:
+            return LQ_ERR_INVALID;
+    }
+}
+
+__global__ void encode_e8_kernel(const float *__restrict__ x, int64_t n, float *__restrict__ out, int d8_only) {
+    const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= n) return;
+    float v[8], q[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = x[8 * b + i];
+    if (d8_only) d8_nearest(v, q);
+    else e8_nearest(v, q);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) out[8 * b + i] = q[i];
+}
+
+}  // namespace
+}  // namespace lq
+
+extern "C" int lq_e8_quantize(const void *x, int dtype, int64_t n_chunks, int64_t n_heads, int64_t bph,
+                              const float *scale_f32, int64_t tile_blocks, int16_t *sym_rows, uint32_t *coset_words,
+                              uint32_t *tile_n0, uint32_t *hist, void *deq, int deq_dtype, float *q_out,
+                              uint32_t *err, void *stream) {
+    if (n_chunks < 0 || n_heads < 0 || bph < 0) return LQ_ERR_INVALID;
+    if (tile_blocks <= 0 || (tile_blocks % 32) != 0) return LQ_ERR_INVALID;
+    if (n_chunks == 0 || n_heads * bph == 0) return LQ_OK;
+    if (!x || !scale_f32 || !sym_rows || !coset_words || !tile_n0 || !hist) return LQ_ERR_INVALID;
+    if ((reinterpret_cast<uintptr_t>(x) & 15) || (deq && (reinterpret_cast<uintptr_t>(deq) & 15)) ||
+        (reinterpret_cast<uintptr_t>(sym_rows) & 15) || (q_out && (reinterpret_cast<uintptr_t>(q_out) & 15)))
+        return LQ_ERR_INVALID;
+    if (n_chunks > 65535) return LQ_ERR_INVALID;
+    cudaStream_t st = lq::as_stream(stream);
+    if (cudaMemsetAsync(hist, 0, sizeof(uint32_t) * (size_t)n_chunks * LQ_NSTREAMS * LQ_HIST_BINS, st) != cudaSuccess)
+        return LQ_ERR_CUDA;
+    switch (dtype) {
+        case LQ_F32:
+            return lq::dispatch_deq<LQ_F32>(deq_dtype, x, n_chunks, n_heads, bph, scale_f32, tile_blocks, sym_rows,
+                                            coset_words, tile_n0, hist, deq, q_out, err, st);
+        case LQ_F16:
+            return lq::dispatch_deq<LQ_F16>(deq_dtype, x, n_chunks, n_heads, bph, scale_f32, tile_blocks, sym_rows,
+                                            coset_words, tile_n0, hist, deq, q_out, err, st);
+        case LQ_BF16:
+            return lq::dispatch_deq<LQ_BF16>(deq_dtype, x, n_chunks, n_heads, bph, scale_f32, tile_blocks, sym_rows,
+                                             coset_words, tile_n0, hist, deq, q_out, err, st);
+        default:
+            return LQ_ERR_INVALID;
+    }
+}
+
+extern "C" int lq_encode_e8(const float *x, int64_t n, float *out, int d8_only, void *stream) {
+    if (n < 0) return LQ_ERR_INVALID;
+    if (n == 0) return LQ_OK;
+    if (!x || !out) return LQ_ERR_INVALID;
+    lq::encode_e8_kernel<<<(unsigned)lq::ceil_div(n, 256), 256, 0, lq::as_stream(stream)>>>(x, n, out, d8_only);
+    return lq::check_launch();
+}

@@ -1,0 +1,536 @@
+// lq_rans.cu -- bit-granular rANS (L = 1024) lane encode / decode.
+//
+// Reference coder (core/gpu_ans.py):
+//   encode (:105-139): x = L; for s in reversed(symbols):
+//       while x >= 2f: emit x & 1; x >>= 1
+//       x = L*(x // f) + cf + x % f
+//     bits reversed, packed LSB-first into u32 words; returns (words, x, n_bits)
+//   decode (:146-168): slot = x & (L-1); s = lookup[slot];
+//       x = f*(x >> 10) + slot - cf; while x < L and pos < n_bits: x = 2x | bit[pos++]
+//
+// Encoder, one thread per lane.  With x in [L, 2L) the k emitted bits are
+// k0 or k0+1 (k0 from the table entry), so one compare replaces the shift
+// loop; the k low bits of x are prepended to a 64-bit accumulator and whole
+// 32-bit words leave it toward the FRONT of a per-lane scratch slot, which
+// therefore ends up holding the stream MSB-first, end-aligned.  A scan over
+// lane sizes and a compaction pass (funnel shift + bit reverse) then lay the
+// lanes back to back in the reference's LSB-first word format.
+//
+// Decoder, one thread per lane, table-driven: for x in [L, 2L) the entry for
+// slot gives (symbol, nb, base) and x = base | next nb bits (bit-reversed
+// words read MSB-first from a 64-bit buffer).  Near the end of a lane, or for
+// a state outside [L, 2L), the reference formula runs literally, including
+// its stop at n_bits, so truncated or odd streams decode exactly as the
+// reference decodes them.
+#include "lq_common.cuh"
+
+namespace lq {
+namespace {
+
+// ---------------------------------------------------------------- encode
+__global__ void __launch_bounds__(256) encode_lanes_kernel(
+    const int16_t *__restrict__ sym_rows, const uint32_t *__restrict__ tile_n0, int64_t n_lanes, int64_t n_tiles,
+    int64_t N, int64_t TB, const int32_t *__restrict__ tab_lo, const int32_t *__restrict__ tab_nsym,
+    const uint32_t *__restrict__ enc_tab, uint32_t *__restrict__ scratch, int64_t slot_words,
+    uint32_t *__restrict__ lane_nbits, uint32_t *__restrict__ lane_state, uint32_t *__restrict__ lane_nwords,
+    uint32_t *err) {
+    const int64_t lg = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (lg >= n_lanes) return;
+    const int64_t per_chunk = n_tiles * LQ_NSTREAMS;
+    const int64_t chunk = lg / per_chunk;
+    const int64_t rem = lg - chunk * per_chunk;
+    const int64_t tile = rem >> 4;
+    const int s = (int)(rem & 15), c = s >> 3, idx = s & 7;
+    const int64_t tb = (tile * TB + TB <= N) ? TB : N - tile * TB;
+    const int64_t n0 = tile_n0[chunk * n_tiles + tile];
+    const int64_t n = c ? tb - n0 : n0;
+    const int64_t tabi = chunk * LQ_NSTREAMS + s;
+    uint32_t *out = scratch + lg * slot_words;
+    int64_t wpos = slot_words;
+    uint32_t x = LQ_L;
+    uint64_t nbits = 0;
+    if (n > 0) {
+        const int lo = tab_lo[tabi];
+        const int nsym = tab_nsym[tabi];
+        if (nsym <= 0 || nsym > LQ_L) {
+            raise_flag(err, LQ_EF_ALPHABET);
+            lane_nbits[lg] = 0;
+            lane_state[lg] = LQ_L;
+            lane_nwords[lg] = 0;
+            return;
+        }
+        const uint32_t *enc = enc_tab + tabi * LQ_L;
+        const int16_t *rows = sym_rows + (chunk * n_tiles + tile) * TB * 8 + idx;
+        // symbols in reverse order: coset 0 at rows n0-1 .. 0, coset 1 at rows n0 .. tb-1
+        const int64_t r0 = c ? n0 : n0 - 1;
+        const int64_t dr = c ? 1 : -1;
+        uint64_t acc = 0;
+        int cnt = 0;
+        int64_t row = r0;
+        for (int64_t j = 0; j < n; ++j, row += dr) {
+            int si = (int)rows[row * 8] - lo;
+            si = si < 0 ? 0 : (si >= nsym ? nsym - 1 : si);  // nearest alphabet entry
+            const uint32_t e = __ldg(enc + si);
+            const uint32_t f = e & 0x7ffu, cf = (e >> 11) & 0x3ffu, k0 = e >> 21;
+            const uint32_t k = k0 + (((x >> k0) >= 2 * f) ? 1u : 0u);
+            acc |= (uint64_t)(x & ((1u << k) - 1u)) << cnt;
+            cnt += (int)k;
+            nbits += k;
+            if (cnt >= 32) {
+                out[--wpos] = (uint32_t)acc;
+                acc >>= 32;
+                cnt -= 32;
+            }
+            x = LQ_L + cf + (x >> k) - f;
+        }
+        if (cnt > 0) out[--wpos] = (uint32_t)acc;
+    }
+    lane_nbits[lg] = (uint32_t)nbits;
+    lane_state[lg] = x;
+    lane_nwords[lg] = (uint32_t)(slot_words - wpos);
+}
+
+// ---------------------------------------------------------------- scan
+constexpr int kScanT = 256;
+constexpr int kScanItems = 16;
+constexpr int64_t kScanTile = (int64_t)kScanT * kScanItems;
+
+__device__ inline uint64_t block_incl_scan(uint64_t v, uint64_t *sh_w) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint64_t u = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += u;
+    }
+    if (lane == 31) sh_w[w] = v;
+    __syncthreads();
+    uint64_t base = 0;
+    for (int i = 0; i < w; ++i) base += sh_w[i];
+    __syncthreads();
+    return base + v;
+}
+
+__global__ void __launch_bounds__(kScanT) scan_reduce_kernel(const uint32_t *__restrict__ cnt, int64_t n,
+                                                              uint64_t *__restrict__ block_sums) {
+    __shared__ uint64_t sh[kScanT / 32];
+    const int64_t base = (int64_t)blockIdx.x * kScanTile;
+    uint64_t s = 0;
+    for (int k = 0; k < kScanItems; ++k) {
+        const int64_t i = base + (int64_t)k * kScanT + threadIdx.x;
+        if (i < n) s += cnt[i];
+    }
+    const uint64_t t = block_incl_scan(s, sh);
+    if (threadIdx.x == kScanT - 1) block_sums[blockIdx.x] = t;
+}
+
+// single CTA: exclusive scan of block sums in place
+__global__ void __launch_bounds__(kScanT) scan_blocks_kernel(uint64_t *__restrict__ block_sums, int64_t nb) {
+    __shared__ uint64_t sh[kScanT / 32];
+    __shared__ uint64_t carry;
+    if (threadIdx.x == 0) carry = 0;
+    __syncthreads();
+    for (int64_t b0 = 0; b0 < nb; b0 += kScanT) {
+        const int64_t i = b0 + threadIdx.x;
+        const uint64_t v = i < nb ? block_sums[i] : 0;
+        const uint64_t inc = block_incl_scan(v, sh);
+        const uint64_t c0 = carry;
+        if (i < nb) block_sums[i] = c0 + inc - v;
+        __syncthreads();
+        if (threadIdx.x == kScanT - 1) carry = c0 + inc;
+        __syncthreads();
+    }
+}
+
+__global__ void __launch_bounds__(kScanT) scan_write_kernel(const uint32_t *__restrict__ cnt, int64_t n,
+                                                             const uint64_t *__restrict__ block_off,
+                                                             uint32_t *__restrict__ off, int64_t cap, uint32_t *err) {
+    __shared__ uint64_t sh[kScanT / 32];
+    const int64_t base = (int64_t)blockIdx.x * kScanTile;
+    // each thread owns kScanItems consecutive entries
+    uint32_t v[kScanItems];
+    uint64_t s = 0;
+    for (int k = 0; k < kScanItems; ++k) {
+        const int64_t i = base + (int64_t)threadIdx.x * kScanItems + k;
+        v[k] = i < n ? cnt[i] : 0u;
+        s += v[k];
+    }
+    uint64_t run = block_off[blockIdx.x] + block_incl_scan(s, sh) - s;
+    for (int k = 0; k < kScanItems; ++k) {
+        const int64_t i = base + (int64_t)threadIdx.x * kScanItems + k;
+        if (i < n) off[i] = (uint32_t)run;
+        run += v[k];
+        if (i == n - 1) {
+            off[n] = (uint32_t)run;
+            if ((int64_t)run > cap || run > 0xffffffffull) raise_flag(err, LQ_EF_CAPACITY);
+        }
+    }
+}
+
+// ---------------------------------------------------------------- compaction
+__global__ void __launch_bounds__(256) compact_lanes_kernel(const uint32_t *__restrict__ scratch, int64_t slot_words,
+                                                             int64_t n_lanes, const uint32_t *__restrict__ lane_off,
+                                                             const uint32_t *__restrict__ lane_nbits,
+                                                             const uint32_t *__restrict__ lane_nwords,
+                                                             uint32_t *__restrict__ words, int64_t cap) {
+    const int lane = threadIdx.x & 31;
+    const int64_t lg = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (lg >= n_lanes) return;
+    const int64_t nw = lane_nwords[lg];
+    const int64_t dst0 = lane_off[lg];
+    if (dst0 + nw > cap) return;  // capacity error already flagged by the scan
+    const uint32_t pad = (32u - (lane_nbits[lg] & 31u)) & 31u;
+    const uint32_t *src = scratch + lg * slot_words + (slot_words - nw);
+    for (int64_t i = lane; i < nw; i += 32) {
+        const uint32_t hi = src[i];
+        const uint32_t lo = (i + 1 < nw) ? src[i + 1] : 0u;
+        words[dst0 + i] = __brev(__funnelshift_l(lo, hi, pad));
+    }
+}
+
+// ---------------------------------------------------------------- decode
+// MSB-first reader over a lane's words (reference words bit-reversed).
+struct BitReader {
+    const uint32_t *w;
+    int64_t nw, wi;
+    uint64_t buf;  // next bits at the top
+    int cnt;       // valid bits in buf
+    __device__ void init(const uint32_t *words, int64_t n_words) {
+        w = words;
+        nw = n_words;
+        wi = 0;
+        buf = 0;
+        cnt = 0;
+        refill();
+    }
+    __device__ __forceinline__ void refill() {
+        while (cnt <= 32 && wi < nw) {
+            buf |= (uint64_t)__brev(__ldg(w + wi)) << (32 - cnt);
+            ++wi;
+            cnt += 32;
+        }
+    }
+    // nb in [0, 32]; bits past the end of the words read as 0
+    __device__ __forceinline__ uint32_t read(int nb) {
+        const uint32_t v = nb ? (uint32_t)(buf >> (64 - nb)) : 0u;
+        buf = nb == 64 ? 0 : buf << nb;
+        cnt -= nb;
+        if (cnt < 0) cnt = 0;
+        if (cnt <= 32) refill();
+        return v;
+    }
+};
+
+// Decode n symbols of one lane into out[j*ostride] (alphabet index).
+// dec: fast table (or nullptr), freq/cf source for the literal path.
+struct LaneTables {
+    const uint32_t *dec;    // [L] si | nb << 10 | (base-L) << 14
+    const uint32_t *enc;    // [nsym] f | cf << 11 (literal path), or nullptr
+    const uint16_t *freq;   // [nsym] frequencies (literal path when enc == nullptr)
+};
+
+__device__ inline void literal_step(uint32_t &x, int64_t &pos, int64_t n_bits, uint32_t si, uint32_t f, uint32_t cf,
+                                    uint32_t slot, BitReader &br) {
+    x = f * (x >> LQ_LOG2_L) + slot - cf;
+    while (x < (uint32_t)LQ_L && pos < n_bits) {
+        x = (x << 1) | br.read(1);
+        ++pos;
+    }
+}
+
+template <typename Emit>
+__device__ inline void decode_lane(const uint32_t *words, int64_t n_words, int64_t n_bits, uint32_t state, int64_t n,
+                                   const uint32_t *dec, const uint16_t *freq, Emit emit) {
+    BitReader br;
+    br.init(words, n_words);
+    uint32_t x = state;
+    int64_t pos = 0;
+    for (int64_t j = 0; j < n; ++j) {
+        const uint32_t slot = x & (LQ_L - 1);
+        const uint32_t e = dec[slot];
+        const uint32_t si = e & 0x3ffu;
+        emit(j, si);
+        if ((x >> LQ_LOG2_L) == 1u && pos + 10 <= n_bits) {
+            const int nb = (int)((e >> 10) & 0xfu);
+            x = ((e >> 14) + LQ_L) | br.read(nb);
+            pos += nb;
+        } else {
+            // literal reference semantics (end of lane, or state outside [L, 2L))
+            const uint32_t f = freq[si];
+            const uint32_t xp = ((e >> 14) + LQ_L) >> ((e >> 10) & 0xfu);  // f + slot - cf
+            const uint32_t cf = f + slot - xp;
+            literal_step(x, pos, n_bits, si, f, cf, slot, br);
+        }
+    }
+}
+
+// General path: thread per lane, symbols to the encoder's row layout.
+__global__ void __launch_bounds__(256) decode_lanes_kernel(
+    const uint32_t *__restrict__ words, int64_t n_words, const uint32_t *__restrict__ lane_off,
+    const uint32_t *__restrict__ lane_nbits, const uint32_t *__restrict__ lane_state,
+    const uint32_t *__restrict__ tile_n0, int64_t n_lanes, int64_t n_tiles, int64_t N, int64_t TB,
+    const int32_t *__restrict__ tab_lo, const int32_t *__restrict__ tab_nsym, const uint16_t *__restrict__ tab_freq,
+    const uint32_t *__restrict__ dec_tab, int16_t *__restrict__ sym_rows, uint32_t *err) {
+    const int64_t lg = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (lg >= n_lanes) return;
+    const int64_t per_chunk = n_tiles * LQ_NSTREAMS;
+    const int64_t chunk = lg / per_chunk;
+    const int64_t rem = lg - chunk * per_chunk;
+    const int64_t tile = rem >> 4;
+    const int s = (int)(rem & 15), c = s >> 3, idx = s & 7;
+    const int64_t tb = (tile * TB + TB <= N) ? TB : N - tile * TB;
+    const int64_t n0 = tile_n0[chunk * n_tiles + tile];
+    const int64_t n = c ? tb - n0 : n0;
+    if (n <= 0) return;
+    const int64_t tabi = chunk * LQ_NSTREAMS + s;
+    const int lo = tab_lo[tabi];
+    const int nsym = tab_nsym[tabi];
+    int16_t *rows = sym_rows + (chunk * n_tiles + tile) * TB * 8 + idx;
+    if (nsym <= 0 || nsym > LQ_L) {
+        raise_flag(err, LQ_EF_ALPHABET);
+        return;
+    }
+    const int64_t w0 = lane_off[lg];
+    const int64_t nb = lane_nbits[lg];
+    const int64_t nw = ceil_div(nb, 32);
+    if (w0 + nw > n_words) {
+        raise_flag(err, LQ_EF_BITSTREAM);
+        return;
+    }
+    // rank r of coset 0 -> row r; of coset 1 -> row tb-1-r
+    decode_lane(words + w0, nw, nb, lane_state[lg], n, dec_tab + tabi * LQ_L, tab_freq + tabi * LQ_L,
+                [&](int64_t r, uint32_t si) {
+                    const int64_t row = c ? tb - 1 - r : r;
+                    rows[row * 8] = (int16_t)((int)si + lo);
+                });
+}
+
+// Exclusive count of coset-1 blocks before each coset word, within its tile.
+__global__ void __launch_bounds__(256) coset_rank_kernel(const uint32_t *__restrict__ coset_words, int64_t n_chunks,
+                                                          int64_t words_per_chunk, int64_t words_per_tile,
+                                                          uint32_t *__restrict__ rank1) {
+    // one thread per tile, sequential over the tile's words
+    const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t tiles_per_chunk = ceil_div(words_per_chunk, words_per_tile);
+    if (g >= n_chunks * tiles_per_chunk) return;
+    const int64_t chunk = g / tiles_per_chunk, tile = g % tiles_per_chunk;
+    const int64_t w0 = tile * words_per_tile;
+    const int64_t w1 = (w0 + words_per_tile < words_per_chunk) ? w0 + words_per_tile : words_per_chunk;
+    const uint32_t *cw = coset_words + chunk * words_per_chunk;
+    uint32_t *r = rank1 + chunk * words_per_chunk;
+    uint32_t run = 0;
+    for (int64_t w = w0; w < w1; ++w) {
+        r[w] = run;
+        run += __popc(cw[w]);
+    }
+}
+
+template <int DO>
+__global__ void __launch_bounds__(256) reconstruct_kernel(const int16_t *__restrict__ sym_rows,
+                                                           const uint32_t *__restrict__ coset_words,
+                                                           const uint32_t *__restrict__ rank1, int64_t n_chunks,
+                                                           int64_t n_heads, int64_t bph, int64_t TB, int64_t n_tiles,
+                                                           const uint16_t *__restrict__ scale_f16, void *out,
+                                                           int32_t *sym_out) {
+    const int64_t gb = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t N = n_heads * bph;
+    if (gb >= n_chunks * N) return;
+    const int64_t chunk = gb / N, b = gb - chunk * N;
+    const int64_t tile = b / TB, p = b - tile * TB;
+    const int64_t tb = (tile * TB + TB <= N) ? TB : N - tile * TB;
+    const int64_t wpc = ceil_div(N, 32);
+    const uint32_t word = coset_words[chunk * wpc + (b >> 5)];
+    const int bit = (int)(b & 31);
+    const uint32_t below = __popc(word & ((1u << bit) - 1u));
+    const int64_t r1 = rank1[chunk * wpc + (b >> 5)] + below;  // coset-1 blocks before b in the tile
+    const int c = (word >> bit) & 1u;
+    const int64_t row = c ? tb - 1 - r1 : p - r1;
+    const uint4 u = reinterpret_cast<const uint4 *>(sym_rows + (chunk * n_tiles + tile) * TB * 8)[row];
+    int sym[8];
+    sym[0] = (int16_t)(u.x & 0xffffu); sym[1] = (int16_t)(u.x >> 16);
+    sym[2] = (int16_t)(u.y & 0xffffu); sym[3] = (int16_t)(u.y >> 16);
+    sym[4] = (int16_t)(u.z & 0xffffu); sym[5] = (int16_t)(u.z >> 16);
+    sym[6] = (int16_t)(u.w & 0xffffu); sym[7] = (int16_t)(u.w >> 16);
+    if (sym_out) {
+        int4 *so = reinterpret_cast<int4 *>(sym_out) + 2 * gb;
+        so[0] = make_int4(sym[0], sym[1], sym[2], sym[3]);
+        so[1] = make_int4(sym[4], sym[5], sym[6], sym[7]);
+    }
+    if constexpr (DO >= 0) {
+        float q[8];
+        e8_from_symbols(c, sym, q);
+        const float sc = __half2float(__ushort_as_half(scale_f16[chunk * n_heads + b / bph]));
+#pragma unroll
+        for (int i = 0; i < 8; ++i) q[i] = __fmul_rn(q[i], sc);
+        store_block8<DO>(out, gb, q);
+    }
+}
+
+// ---------------------------------------------------------------- reference streams
+__global__ void __launch_bounds__(128) decode_streams_kernel(
+    const uint32_t *__restrict__ bits, int64_t n_words, const int64_t *__restrict__ bit_offsets,
+    const int64_t *__restrict__ n_bits, const int64_t *__restrict__ init_states, const int64_t *__restrict__ n_decode,
+    const int32_t *__restrict__ lookup, const int32_t *__restrict__ freqs, const int32_t *__restrict__ cumfreqs,
+    const int32_t *__restrict__ alphabet, const int32_t *__restrict__ table_id, int64_t max_sym, int64_t n_streams,
+    int64_t *__restrict__ out, const int64_t *__restrict__ out_offsets, uint32_t *err) {
+    const int64_t sid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (sid >= n_streams) return;
+    const int64_t tid = table_id[sid];
+    const int32_t *lk = lookup + tid * LQ_L;
+    const int32_t *fr = freqs + tid * max_sym;
+    const int32_t *cfr = cumfreqs + tid * max_sym;
+    const int32_t *al = alphabet + tid * max_sym;
+    const int64_t b0 = bit_offsets[sid];
+    const int64_t nb = n_bits[sid];
+    const int64_t nd = n_decode[sid];
+    int64_t *o = out + out_offsets[sid];
+    // the reference reads bit (b0 + pos) of the flat int32 word array
+    if (b0 < 0 || nb < 0 || ((b0 + nb + 31) >> 5) > n_words || init_states[sid] < 0 ||
+        init_states[sid] > 0xffffffffll) {
+        raise_flag(err, LQ_EF_BITSTREAM);
+        return;
+    }
+    uint32_t x = (uint32_t)init_states[sid];
+    int64_t pos = 0;
+    for (int64_t i = 0; i < nd; ++i) {
+        const uint32_t slot = x & (LQ_L - 1);
+        const int32_t si = lk[slot];
+        if (si < 0 || si >= max_sym) {
+            raise_flag(err, LQ_EF_BITSTREAM);
+            return;
+        }
+        o[i] = (int64_t)al[si];
+        x = (uint32_t)fr[si] * (x >> LQ_LOG2_L) + slot - (uint32_t)cfr[si];
+        while (x < (uint32_t)LQ_L && pos < nb) {
+            const int64_t ab = b0 + pos;
+            x = (x << 1) | ((__ldg(bits + (ab >> 5)) >> (ab & 31)) & 1u);
+            ++pos;
+        }
+    }
+}
+
+}  // namespace
+}  // namespace lq
+
+using namespace lq;
+
+static int64_t slot_words_for(int64_t TB) { return ceil_div(10 * TB, 32) + 1; }
+
+extern "C" size_t lq_rans_encode_workspace(int64_t n_chunks, int64_t n_vectors, int64_t tile_blocks) {
+    if (n_chunks <= 0 || n_vectors <= 0 || tile_blocks <= 0) return 0;
+    const int64_t n_tiles = ceil_div(n_vectors, tile_blocks);
+    const int64_t n_lanes = n_chunks * n_tiles * LQ_NSTREAMS;
+    const int64_t nblk = ceil_div(n_lanes, kScanTile);
+    size_t b = sizeof(uint32_t) * (size_t)(n_lanes * slot_words_for(tile_blocks));  // scratch slots
+    b += sizeof(uint32_t) * (size_t)n_lanes;                                        // lane word counts
+    b = (b + 15) & ~(size_t)15;
+    b += sizeof(uint64_t) * (size_t)(nblk + 1);                                     // scan block sums
+    return b;
+}
+
+extern "C" int lq_rans_encode(const int16_t *sym_rows, const uint32_t *tile_n0, int64_t n_chunks, int64_t n_vectors,
+                              int64_t tile_blocks, const int32_t *tab_lo, const int32_t *tab_nsym,
+                              const uint32_t *enc_tab, uint32_t *words, int64_t words_cap, uint32_t *lane_off,
+                              uint32_t *lane_nbits, uint32_t *lane_state, void *workspace, size_t workspace_bytes,
+                              uint32_t *err, void *stream) {
+    if (n_chunks < 0 || n_vectors < 0 || tile_blocks <= 0 || (tile_blocks % 32) != 0 || words_cap < 0)
+        return LQ_ERR_INVALID;
+    if (!lane_off) return LQ_ERR_INVALID;
+    cudaStream_t st = as_stream(stream);
+    if (n_chunks == 0 || n_vectors == 0) {
+        if (cudaMemsetAsync(lane_off, 0, sizeof(uint32_t), st) != cudaSuccess) return LQ_ERR_CUDA;
+        return LQ_OK;
+    }
+    if (!sym_rows || !tile_n0 || !tab_lo || !tab_nsym || !enc_tab || !words || !lane_nbits || !lane_state ||
+        !workspace)
+        return LQ_ERR_INVALID;
+    if (workspace_bytes < lq_rans_encode_workspace(n_chunks, n_vectors, tile_blocks)) return LQ_ERR_CAPACITY;
+    const int64_t n_tiles = ceil_div(n_vectors, tile_blocks);
+    const int64_t n_lanes = n_chunks * n_tiles * LQ_NSTREAMS;
+    const int64_t sw = slot_words_for(tile_blocks);
+    uint32_t *scratch = static_cast<uint32_t *>(workspace);
+    uint32_t *nwords = scratch + n_lanes * sw;
+    size_t off = ((sizeof(uint32_t) * (size_t)(n_lanes * sw + n_lanes)) + 15) & ~(size_t)15;
+    uint64_t *bsum = reinterpret_cast<uint64_t *>(static_cast<char *>(workspace) + off);
+    const int64_t nblk = ceil_div(n_lanes, kScanTile);
+    encode_lanes_kernel<<<(unsigned)ceil_div(n_lanes, 256), 256, 0, st>>>(
+        sym_rows, tile_n0, n_lanes, n_tiles, n_vectors, tile_blocks, tab_lo, tab_nsym, enc_tab, scratch, sw,
+        lane_nbits, lane_state, nwords, err);
+    scan_reduce_kernel<<<(unsigned)nblk, kScanT, 0, st>>>(nwords, n_lanes, bsum);
+    scan_blocks_kernel<<<1, kScanT, 0, st>>>(bsum, nblk);
+    scan_write_kernel<<<(unsigned)nblk, kScanT, 0, st>>>(nwords, n_lanes, bsum, lane_off, words_cap, err);
+    compact_lanes_kernel<<<(unsigned)ceil_div(n_lanes, 8), 256, 0, st>>>(scratch, sw, n_lanes, lane_off, lane_nbits,
+                                                                          nwords, words, words_cap);
+    return check_launch();
+}
+
+extern "C" size_t lq_rans_decode_workspace(int64_t n_chunks, int64_t n_vectors, int64_t tile_blocks) {
+    if (n_chunks <= 0 || n_vectors <= 0 || tile_blocks <= 0) return 0;
+    const int64_t n_tiles = ceil_div(n_vectors, tile_blocks);
+    size_t b = sizeof(int16_t) * 8 * (size_t)(n_chunks * n_tiles * tile_blocks);  // symbol rows
+    b += sizeof(uint32_t) * (size_t)(n_chunks * ceil_div(n_vectors, 32));         // coset ranks
+    return (b + 15) & ~(size_t)15;
+}
+
+extern "C" int lq_rans_decode(const uint32_t *words, int64_t n_words, const uint32_t *lane_off,
+                                 const uint32_t *lane_nbits, const uint32_t *lane_state, const uint32_t *coset_words,
+                                 const uint32_t *tile_n0, int64_t n_chunks, int64_t n_heads, int64_t bph,
+                                 int64_t tile_blocks, const int32_t *tab_lo, const int32_t *tab_nsym,
+                                 const uint16_t *tab_freq, const uint32_t *dec_tab, const uint16_t *scale_f16,
+                                 void *out, int out_dtype, int32_t *sym_out, void *workspace, size_t workspace_bytes,
+                                 uint32_t *err, void *stream) {
+    if (n_chunks < 0 || n_heads < 0 || bph < 0 || tile_blocks <= 0 || (tile_blocks % 32) != 0 || n_words < 0)
+        return LQ_ERR_INVALID;
+    const int64_t N = n_heads * bph;
+    if (n_chunks == 0 || N == 0) return LQ_OK;
+    if (!lane_off || !lane_nbits || !lane_state || !coset_words || !tile_n0 || !tab_lo || !tab_nsym || !tab_freq ||
+        !dec_tab || !workspace || (!out && !sym_out) || (n_words > 0 && !words))
+        return LQ_ERR_INVALID;
+    if (out && (reinterpret_cast<uintptr_t>(out) & 15)) return LQ_ERR_INVALID;
+    if (out && !scale_f16) return LQ_ERR_INVALID;
+    if (workspace_bytes < lq_rans_decode_workspace(n_chunks, N, tile_blocks)) return LQ_ERR_CAPACITY;
+    cudaStream_t st = as_stream(stream);
+    const int64_t n_tiles = ceil_div(N, tile_blocks);
+    const int64_t n_lanes = n_chunks * n_tiles * LQ_NSTREAMS;
+    int16_t *rows = static_cast<int16_t *>(workspace);
+    uint32_t *rank1 = reinterpret_cast<uint32_t *>(rows + 8 * n_chunks * n_tiles * tile_blocks);
+    decode_lanes_kernel<<<(unsigned)ceil_div(n_lanes, 256), 256, 0, st>>>(
+        words, n_words, lane_off, lane_nbits, lane_state, tile_n0, n_lanes, n_tiles, N, tile_blocks, tab_lo, tab_nsym,
+        tab_freq, dec_tab, rows, err);
+    const int64_t wpc = ceil_div(N, 32);
+    const int64_t wpt = tile_blocks / 32;
+    coset_rank_kernel<<<(unsigned)ceil_div(n_chunks * n_tiles, 256), 256, 0, st>>>(coset_words, n_chunks, wpc, wpt,
+                                                                                   rank1);
+    const unsigned g = (unsigned)ceil_div(n_chunks * N, 256);
+    if (!out) {
+        reconstruct_kernel<-1><<<g, 256, 0, st>>>(rows, coset_words, rank1, n_chunks, n_heads, bph, tile_blocks,
+                                                  n_tiles, scale_f16, out, sym_out);
+    } else if (out_dtype == LQ_F32) {
+        reconstruct_kernel<LQ_F32><<<g, 256, 0, st>>>(rows, coset_words, rank1, n_chunks, n_heads, bph, tile_blocks,
+                                                      n_tiles, scale_f16, out, sym_out);
+    } else if (out_dtype == LQ_F16) {
+        reconstruct_kernel<LQ_F16><<<g, 256, 0, st>>>(rows, coset_words, rank1, n_chunks, n_heads, bph, tile_blocks,
+                                                      n_tiles, scale_f16, out, sym_out);
+    } else if (out_dtype == LQ_BF16) {
+        reconstruct_kernel<LQ_BF16><<<g, 256, 0, st>>>(rows, coset_words, rank1, n_chunks, n_heads, bph, tile_blocks,
+                                                       n_tiles, scale_f16, out, sym_out);
+    } else {
+        return LQ_ERR_INVALID;
+    }
+    return check_launch();
+}
+
+extern "C" int lq_rans_decode_streams(const uint32_t *bitstream, int64_t n_words, const int64_t *bit_offsets,
+                                      const int64_t *n_bits, const int64_t *init_states, const int64_t *n_decode,
+                                      const int32_t *lookup, const int32_t *freqs, const int32_t *cumfreqs,
+                                      const int32_t *alphabet, const int32_t *table_id, int64_t max_sym,
+                                      int64_t n_streams, int64_t *out, const int64_t *out_offsets, uint32_t *err,
+                                      void *stream) {
+    if (n_streams < 0 || max_sym < 0 || n_words < 0) return LQ_ERR_INVALID;
+    if (n_streams == 0) return LQ_OK;
+    if (!bitstream || !bit_offsets || !n_bits || !init_states || !n_decode || !lookup || !freqs || !cumfreqs ||
+        !alphabet || !table_id || !out || !out_offsets)
+        return LQ_ERR_INVALID;
+    decode_streams_kernel<<<(unsigned)ceil_div(n_streams, 128), 128, 0, as_stream(stream)>>>(
+        bitstream, n_words, bit_offsets, n_bits, init_states, n_decode, lookup, freqs, cumfreqs, alphabet, table_id,
+        max_sym, n_streams, out, out_offsets, err);
+    return check_launch();
+}

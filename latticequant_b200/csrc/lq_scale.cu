@@ -1,0 +1,239 @@
+// lq_scale.cu -- per-head sigma^2 and lattice scale.
+//
+// Reference: llm/compressed_kv_cache.py:183-196
+//   sigma2 = (t_heads ** 2).mean(dim=(1, 2)); scale = sqrt(2*pi*e*sigma2*4^-b)
+//   scale = 1 where sigma2 < 1e-12; per_head_scale = scale.to(float16)
+//
+// torch sums a contiguous row on the CPU with a fixed tree, and the sum is
+// reproduced here bit for bit so that the scales (and with them every
+// lattice point) agree with the reference.  The tree, for a row of E
+// elements read as vec_size = E/8 vectors of 8 lanes:
+//   * 32 chains: chain t = 8k + l sums elements 32*i + t, i in [0, S),
+//     S = vec_size / 4 (k = interleaved accumulator row, l = vector lane);
+//   * each chain is a 4-level cascade with fan-out G = 2^max(4, ceil_log2(S)/4):
+//     level-0 sums G consecutive elements left to right, level-1 sums G
+//     level-0 sums, level-2 sums G level-1 sums, level-3 sums all level-2
+//     sums; leftovers: chain = ((tail + part1) + part2) + acc3;
+//   * vectors 4S..vec_size-1 are added to row k = 0, then row 0 += rows 1..3
+//     lane by lane; finally a zero accumulates the E%8 scalar tail and then
+//     lanes 0..7, left to right.
+// One warp evaluates one (head, level-1 block): lane t owns chain t, so every
+// warp-wide load reads 32 consecutive elements.  A second pass folds the
+// level-1 sums of each head.  Heads whose chain fits in one level-1 block
+// (S < G^2) are finished by a single pass.
+#include "lq_common.cuh"
+
+namespace lq {
+namespace {
+
+__host__ __device__ inline int64_t ceil_log2_i64(int64_t x) {
+    if (x <= 2) return 1;
+#ifdef __CUDA_ARCH__
+    return 64 - __clzll((long long)(x - 1));
+#else
+    return 64 - __builtin_clzll((unsigned long long)(x - 1));
+#endif
+}
+
+struct Cascade {
+    int64_t E, vec_size, S, G, n_l1;
+    __host__ __device__ explicit Cascade(int64_t e) : E(e) {
+        vec_size = E / 8;
+        S = vec_size / 4;
+        int64_t lp = ceil_log2_i64(S) / 4;
+        if (lp < 4) lp = 4;
+        G = (int64_t)1 << lp;
+        n_l1 = ceil_div(S, G * G);
+        if (n_l1 < 1) n_l1 = 1;
+    }
+};
+
+template <int DT>
+__device__ __forceinline__ float sq(const void *x, int64_t i) {
+    const float t = Elem<DT>::load(x, i);
+    return __fmul_rn(t, t);
+}
+
+// Sum of chain `lane` over i in [i0, i1) as complete level-0 groups, plus the
+// trailing partial group separately.  Returns the level-1 partial; *tail gets
+// the partial group's sum.
+template <int DT>
+__device__ __forceinline__ float chain_block(const void *xh, int64_t i0, int64_t i1, int64_t G, int lane,
+                                             float *tail) {
+    float acc1 = 0.0f;
+    const int64_t full = (i1 - i0) / G;
+    int64_t i = i0;
+    for (int64_t g = 0; g < full; ++g) {
+        float a0 = 0.0f;
+        // 16 loads in flight before the dependent adds
+        for (int64_t j = 0; j < G; j += 16) {
+            float v[16];
+#pragma unroll
+            for (int u = 0; u < 16; ++u) v[u] = sq<DT>(xh, 32 * (i + j + u) + lane);
+#pragma unroll
+            for (int u = 0; u < 16; ++u) a0 = __fadd_rn(a0, v[u]);
+        }
+        acc1 = __fadd_rn(acc1, a0);
+        i += G;
+    }
+    float t = 0.0f;
+    for (; i < i1; ++i) t = __fadd_rn(t, sq<DT>(xh, 32 * i + lane));
+    *tail = t;
+    return acc1;
+}
+
+// Final fold of one head, given per-chain (tail, part1, part2, acc3) in lane t.
+template <int DT>
+__device__ __forceinline__ float fold_head(const void *xh, const Cascade &c, float chain, int lane) {
+    // extra vectors 4S .. vec_size-1 go into row 0 (lanes 0..7)
+    float r = chain;
+    if (lane < 8)
+        for (int64_t v = c.S * 4; v < c.vec_size; ++v) r = __fadd_rn(r, sq<DT>(xh, v * 8 + lane));
+    // row 0 += row 1, += row 2, += row 3 (lane-wise)
+    const float r1 = __shfl_sync(0xffffffffu, r, lane + 8);
+    const float r2 = __shfl_sync(0xffffffffu, r, lane + 16);
+    const float r3 = __shfl_sync(0xffffffffu, r, lane + 24);
+    r = __fadd_rn(__fadd_rn(__fadd_rn(r, r1), r2), r3);
+    // scalar tail then lanes 0..7, left to right, from zero
+    float fa = 0.0f;
+    if (lane == 0)
+        for (int64_t e = c.vec_size * 8; e < c.E; ++e) fa = __fadd_rn(fa, sq<DT>(xh, e));
+#pragma unroll
+    for (int l = 0; l < 8; ++l) {
+        const float rl = __shfl_sync(0xffffffffu, r, l);
+        fa = __fadd_rn(fa, rl);
+    }
+    return fa;  // valid in every lane
+}
+
+__device__ __forceinline__ void write_scale(int64_t h, float sum, int64_t E, float vol_mult, float *sigma2,
+                                            float *scale_f32, uint16_t *scale_f16) {
+    // 2*pi*e as a Python double, cast to fp32 by torch
+    constexpr float kTwoPiE = 17.079468445347132f;
+    const float s2 = __fdiv_rn(sum, (float)E);
+    float sc = __fsqrt_rn(__fmul_rn(__fmul_rn(s2, kTwoPiE), vol_mult));
+    if (s2 < 1e-12f) sc = 1.0f;
+    if (sigma2) sigma2[h] = s2;
+    if (scale_f32) scale_f32[h] = sc;
+    if (scale_f16) scale_f16[h] = __half_as_ushort(__float2half_rn(sc));
+}
+
+// Heads with a single level-1 block: one warp does everything.
+template <int DT>
+__global__ void __launch_bounds__(256) scale_small_kernel(const void *x, int64_t n_heads, int64_t E, float vol_mult,
+                                                           float *sigma2, float *scale_f32, uint16_t *scale_f16) {
+    const int lane = threadIdx.x & 31;
+    const int64_t h = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (h >= n_heads) return;
+    const Cascade c(E);
+    const char *xh = static_cast<const char *>(x) + h * E * (DT == LQ_F32 ? 4 : 2);
+    float tail;
+    const float part1 = chain_block<DT>(xh, 0, c.S, c.G, lane, &tail);
+    // single block: complete level-1 block goes to level 2, else it is part1
+    float chain;
+    if (c.S == c.G * c.G) {
+        chain = __fadd_rn(__fadd_rn(__fadd_rn(tail, 0.0f), part1), 0.0f);
+    } else {
+        chain = __fadd_rn(__fadd_rn(__fadd_rn(tail, part1), 0.0f), 0.0f);
+    }
+    const float sum = fold_head<DT>(xh, c, chain, lane);
+    if (lane == 0) write_scale(h, sum, E, vol_mult, sigma2, scale_f32, scale_f16);
+}
+
+// Pass 1 (large heads): one warp per (head, level-1 block).
+template <int DT>
+__global__ void __launch_bounds__(256) scale_l1_kernel(const void *x, int64_t n_heads, int64_t E, float *l1,
+                                                        float *tails) {
+    const int lane = threadIdx.x & 31;
+    const Cascade c(E);
+    const int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (w >= n_heads * c.n_l1) return;
+    const int64_t h = w / c.n_l1, j = w % c.n_l1;
+    const char *xh = static_cast<const char *>(x) + h * E * (DT == LQ_F32 ? 4 : 2);
+    const int64_t i0 = j * c.G * c.G;
+    const int64_t i1 = (i0 + c.G * c.G < c.S) ? i0 + c.G * c.G : c.S;
+    float tail;
+    const float part = chain_block<DT>(xh, i0, i1, c.G, lane, &tail);
+    l1[w * 32 + lane] = part;
+    if (j == c.n_l1 - 1) tails[h * 32 + lane] = tail;
+}
+
+// Pass 2: fold level-1 sums into levels 2 and 3, then the head.
+template <int DT>
+__global__ void __launch_bounds__(256) scale_fold_kernel(const void *x, int64_t n_heads, int64_t E, float vol_mult,
+                                                          const float *l1, const float *tails, float *sigma2,
+                                                          float *scale_f32, uint16_t *scale_f16) {
+    const int lane = threadIdx.x & 31;
+    const int64_t h = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (h >= n_heads) return;
+    const Cascade c(E);
+    const char *xh = static_cast<const char *>(x) + h * E * (DT == LQ_F32 ? 4 : 2);
+    const int64_t n_full = c.S / (c.G * c.G);  // complete level-1 blocks
+    float acc2 = 0.0f, acc3 = 0.0f;
+    const float *hl = l1 + h * c.n_l1 * 32;
+    for (int64_t j = 0; j < n_full; ++j) {
+        acc2 = __fadd_rn(acc2, hl[j * 32 + lane]);
+        if (((j + 1) % c.G) == 0) {
+            acc3 = __fadd_rn(acc3, acc2);
+            acc2 = 0.0f;
+        }
+    }
+    const float part1 = (n_full < c.n_l1) ? hl[n_full * 32 + lane] : 0.0f;
+    const float tail = tails[h * 32 + lane];
+    const float chain = __fadd_rn(__fadd_rn(__fadd_rn(tail, part1), acc2), acc3);
+    const float sum = fold_head<DT>(xh, c, chain, lane);
+    if (lane == 0) write_scale(h, sum, E, vol_mult, sigma2, scale_f32, scale_f16);
+}
+
+template <int DT>
+int launch_scales(const void *x, int64_t n_heads, int64_t E, float vol_mult, float *sigma2, float *scale_f32,
+                  uint16_t *scale_f16, void *ws, size_t ws_bytes, cudaStream_t st) {
+    const Cascade c(E);
+    const int wpb = 8;
+    if (c.n_l1 == 1) {
+        const int64_t blocks = ceil_div(n_heads, wpb);
+        scale_small_kernel<DT><<<(unsigned)blocks, 32 * wpb, 0, st>>>(x, n_heads, E, vol_mult, sigma2, scale_f32,
+                                                                        scale_f16);
+        return check_launch();
+    }
+    const size_t need = sizeof(float) * 32 * (size_t)(n_heads * c.n_l1 + n_heads);
+    if (ws == nullptr || ws_bytes < need) return LQ_ERR_CAPACITY;
+    float *l1 = static_cast<float *>(ws);
+    float *tails = l1 + 32 * n_heads * c.n_l1;
+    const int64_t warps = n_heads * c.n_l1;
+    scale_l1_kernel<DT><<<(unsigned)ceil_div(warps, wpb), 32 * wpb, 0, st>>>(x, n_heads, E, l1, tails);
+    scale_fold_kernel<DT><<<(unsigned)ceil_div(n_heads, wpb), 32 * wpb, 0, st>>>(x, n_heads, E, vol_mult, l1, tails,
+                                                                                 sigma2, scale_f32, scale_f16);
+    return check_launch();
+}
+
+}  // namespace
+}  // namespace lq
+
+extern "C" size_t lq_head_scales_workspace(int64_t n_heads_total, int64_t elems_per_head) {
+    const lq::Cascade c(elems_per_head);
+    if (c.n_l1 == 1) return 0;
+    return sizeof(float) * 32 * (size_t)(n_heads_total * c.n_l1 + n_heads_total);
+}
+
+extern "C" int lq_head_scales(const void *x, int dtype, int64_t n_heads_total, int64_t elems_per_head,
+                              float vol_mult, float *sigma2, float *scale_f32, uint16_t *scale_f16, void *workspace,
+                              size_t workspace_bytes, void *stream) {
+    if (n_heads_total < 0 || elems_per_head < 0) return LQ_ERR_INVALID;
+    if (n_heads_total == 0) return LQ_OK;
+    if (x == nullptr || elems_per_head == 0) return LQ_ERR_INVALID;
+    cudaStream_t st = lq::as_stream(stream);
+    switch (dtype) {
+        case LQ_F32:
+            return lq::launch_scales<LQ_F32>(x, n_heads_total, elems_per_head, vol_mult, sigma2, scale_f32, scale_f16,
+                                             workspace, workspace_bytes, st);
+        case LQ_F16:
+            return lq::launch_scales<LQ_F16>(x, n_heads_total, elems_per_head, vol_mult, sigma2, scale_f32, scale_f16,
+                                             workspace, workspace_bytes, st);
+        case LQ_BF16:
+            return lq::launch_scales<LQ_BF16>(x, n_heads_total, elems_per_head, vol_mult, sigma2, scale_f32,
+                                              scale_f16, workspace, workspace_bytes, st);
+        default:
+            return LQ_ERR_INVALID;
+    }
+}
