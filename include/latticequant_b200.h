@@ -82,6 +82,33 @@ int lq_head_scales(const void *x, int dtype, int64_t n_heads_total, int64_t elem
                    void *stream);
 
 /* ------------------------------------------------------------------------
+ * lq_head_scales without a workspace argument.  It has no counterpart in
+ * the reference, which computes the scales with torch on whatever device the
+ * tensor lives on.  It is for callers that cannot allocate device memory: a
+ * host that owns all GPU memory and hands out no allocator (a serving engine
+ * with a pre-reserved pool, a foreign-language plugin without torch), or a
+ * latency-critical decode step that must not pay the device-wide
+ * synchronisation a cudaMalloc/cudaFree can cause.  Results are identical to
+ * lq_head_scales.
+ *   limit     the partial sums use a scratch array inside the library of
+ *             LQ_HEAD_SCALES_STATIC_FLOATS floats (4 MiB) that every GPU which
+ *             loads the library holds until the process exits; a problem with
+ *             lq_head_scales_workspace(n, e) > 4 MiB returns LQ_ERR_CAPACITY
+ *             before anything is launched (e.g. heads of 2^20 elements: at
+ *             most 254 heads per call)
+ *   set-up    the first call on a device (with that device current) looks up
+ *             the array's device address; make that first call before any
+ *             CUDA stream capture
+ *   sharing   all calls use the same array, which keeps the last call's
+ *             contents (nothing needs to start at zero); calls that can
+ *             overlap on the GPU -- different streams without ordering, or
+ *             several host threads -- race on it and must be serialised
+ * ---------------------------------------------------------------------- */
+#define LQ_HEAD_SCALES_STATIC_FLOATS (1 << 20)
+int lq_head_scales_static(const void *x, int dtype, int64_t n_heads_total, int64_t elems_per_head, float vol_mult,
+                          float *sigma2, float *scale_f32, uint16_t *scale_f16, void *stream);
+
+/* ------------------------------------------------------------------------
  * E8 quantisation + parity-aware symbolisation + coset packing + histograms.
  * Replaces the E8 / symbol part of _compress_tensor
  * (llm/compressed_kv_cache.py:198-228): x / scale -> encode_e8

@@ -21,6 +21,8 @@
 // warp-wide load reads 32 consecutive elements.  A second pass folds the
 // level-1 sums of each head.  Heads whose chain fits in one level-1 block
 // (S < G^2) are finished by a single pass.
+#include <mutex>
+
 #include "lq_common.cuh"
 
 namespace lq {
@@ -235,5 +237,62 @@ extern "C" int lq_head_scales(const void *x, int dtype, int64_t n_heads_total, i
                                               scale_f16, workspace, workspace_bytes, st);
         default:
             return LQ_ERR_INVALID;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant.  The level-1 partial sums go to a scratch array
+// that is part of this library's own device image, so the caller passes no
+// workspace and nothing is allocated per call.  Host code cannot use the
+// array's name as a device address: the address is looked up once per device
+// with cudaGetSymbolAddress and cached here.  Every call on a device shares
+// the array; nothing in it needs to start at zero (each call writes every
+// entry it later reads).
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) float lq_scales_static_scratch[LQ_HEAD_SCALES_STATIC_FLOATS];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_static_mu;
+float *g_static_scratch[kMaxDevices] = {};
+
+int static_scratch_for_current_device(float **out) {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess) return LQ_ERR_CUDA;
+    if (dev < 0 || dev >= kMaxDevices) return LQ_ERR_INVALID;
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    if (g_static_scratch[dev] == nullptr) {
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, lq_scales_static_scratch) != cudaSuccess || p == nullptr) return LQ_ERR_CUDA;
+        g_static_scratch[dev] = static_cast<float *>(p);
+    }
+    *out = g_static_scratch[dev];
+    return LQ_OK;
+}
+}  // namespace
+
+extern "C" int lq_head_scales_static(const void *x, int dtype, int64_t n_heads_total, int64_t elems_per_head,
+                                     float vol_mult, float *sigma2, float *scale_f32, uint16_t *scale_f16,
+                                     void *stream) {
+    if (n_heads_total < 0 || elems_per_head < 0) return LQ_ERR_INVALID;
+    if (n_heads_total == 0) return LQ_OK;
+    if (x == nullptr || elems_per_head == 0) return LQ_ERR_INVALID;
+    if (dtype != LQ_F32 && dtype != LQ_F16 && dtype != LQ_BF16) return LQ_ERR_INVALID;
+    const size_t cap = sizeof(float) * (size_t)LQ_HEAD_SCALES_STATIC_FLOATS;
+    if (lq_head_scales_workspace(n_heads_total, elems_per_head) > cap) return LQ_ERR_CAPACITY;
+    float *ws = nullptr;
+    const int rc = static_scratch_for_current_device(&ws);
+    if (rc != LQ_OK) return rc;
+    cudaStream_t st = lq::as_stream(stream);
+    switch (dtype) {
+        case LQ_F32:
+            return lq::launch_scales<LQ_F32>(x, n_heads_total, elems_per_head, vol_mult, sigma2, scale_f32, scale_f16,
+                                             ws, cap, st);
+        case LQ_F16:
+            return lq::launch_scales<LQ_F16>(x, n_heads_total, elems_per_head, vol_mult, sigma2, scale_f32, scale_f16,
+                                             ws, cap, st);
+        default:
+            return lq::launch_scales<LQ_BF16>(x, n_heads_total, elems_per_head, vol_mult, sigma2, scale_f32,
+                                              scale_f16, ws, cap, st);
     }
 }
