@@ -209,6 +209,17 @@ int lq_pack_e8(const float *q, int64_t n, int bits, uint8_t *out, uint32_t *n_ba
 int lq_unpack_e8(const uint8_t *packed, int64_t n, int bits, const float *scales, const int32_t *head_idx,
                  float *q_out, uint16_t *f16_out, void *stream);
 
+/* ------------------------------------------------------------------------
+ * Diagnostics for tests: run one internal device helper over arrays.
+ *   LQ_SELFTEST_DIV      out[i] = a[i] / b[i] (fp32) through the quantiser's
+ *                        division (reciprocal + FMA correction); must equal IEEE
+ *   LQ_SELFTEST_FASTDIV  out[i] = a[i] / d (u32, a[i] < 2^31, 1 <= d < 2^31)
+ *                        through the invariant-divisor multiply-shift
+ * ---------------------------------------------------------------------- */
+#define LQ_SELFTEST_DIV 1
+#define LQ_SELFTEST_FASTDIV 2
+int lq_selftest(int which, const void *a, const void *b, int64_t n, uint32_t d, void *out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -61,6 +61,8 @@ def _declare(lib):
         "lq_rans_decode_streams": ([vp, i64, vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, vp, vp, vp, vp], i32),
         "lq_pack_e8": ([vp, i64, i32, vp, vp, vp], i32),
         "lq_unpack_e8": ([vp, i64, i32, vp, vp, vp, vp, vp], i32),
+        "lq_head_scales_static": ([vp, i32, i64, i64, f32, vp, vp, vp, vp], i32),
+        "lq_selftest": ([i32, vp, vp, i64, ctypes.c_uint32, vp, vp], i32),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)

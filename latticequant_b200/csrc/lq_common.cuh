@@ -107,6 +107,49 @@ __device__ inline void store_block8(void *y, int64_t blk, const float v[8]) {
     }
 }
 
+// ---- division by a loop-invariant divisor ---------------------------------
+// Round-up multiply-shift method for unsigned division (Granlund & Montgomery,
+// "Division by invariant integers using multiplication", PLDI 1994, Fig. 4.1):
+// l = ceil(log2 d), m = floor(2^32 (2^l - d) / d) + 1, t = umulhi(m, n),
+// n / d = (t + ((n - t) >> min(l, 1))) >> max(l - 1, 0), for d in [1, 2^31).
+struct FastDiv {
+    uint32_t d, m, sh1, sh2;
+    __host__ __device__ FastDiv() : d(1), m(1), sh1(0), sh2(0) {}
+    __host__ __device__ explicit FastDiv(uint32_t div) : d(div) {
+        uint32_t l = 0;
+        while ((1ull << l) < (uint64_t)div) ++l;
+        m = (uint32_t)(((1ull << 32) * ((1ull << l) - div)) / div + 1);
+        sh1 = l < 1 ? l : 1;
+        sh2 = l > 1 ? l - 1 : 0;
+    }
+    __device__ __forceinline__ uint32_t div(uint32_t n) const {
+        const uint32_t t = __umulhi(m, n);
+        return (t + ((n - t) >> sh1)) >> sh2;
+    }
+};
+
+// ---- IEEE division by a per-head scale -----------------------------------
+// Markstein's theorem (P. Markstein, "Computation of elementary functions on
+// the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990; also
+// Muller et al., Handbook of Floating-Point Arithmetic, FMA-based division):
+// with y = RN(1/b), q0 = RN(a*y) and the exact FMA residual r = a - b*q0,
+// RN(q0 + r*y) == RN(a/b) in round-to-nearest when nothing over- or
+// underflows.  Both |a| (unless 0) and |b| must lie in [2^-40, 2^40], which
+// keeps every intermediate normal; anything else takes the IEEE divide.  When
+// r == 0, q0 is the exact quotient (this also keeps the sign of zero).
+__device__ __forceinline__ bool scale_ok_for_fast_div(float b) {
+    const float ab = fabsf(b);
+    return ab >= 9.094947e-13f && ab <= 1.0995116e12f;
+}
+
+__device__ __forceinline__ float div_by_scale(float a, float b, float y, bool b_ok) {
+    const float aa = fabsf(a);
+    if (!b_ok || !(aa <= 1.0995116e12f && (aa >= 9.094947e-13f || aa == 0.0f))) return __fdiv_rn(a, b);
+    const float q0 = __fmul_rn(a, y);
+    const float r = __fmaf_rn(-b, q0, a);
+    return r == 0.0f ? q0 : __fmaf_rn(r, y, q0);
+}
+
 // ---- E8 nearest point ---------------------------------------------------
 // Bit-exact restatement of core/e8_quantizer.py:20-83 as torch evaluates it
 // on the CPU: every operation below is one rounded binary32 op (explicit
@@ -121,53 +164,115 @@ __device__ __forceinline__ float e8_tie(int i) {
     return __uint_as_float(bits[i]);
 }
 
+// packed fp32x2 ops (sm_100): two independent IEEE binary32 operations, each
+// rounded to nearest, in one instruction
+__device__ __forceinline__ unsigned long long f2_pack(float a, float b) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void f2_unpack(unsigned long long r, float &a, float &b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ unsigned long long f2_mul(unsigned long long a, unsigned long long b) {
+    unsigned long long r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsigned long long b) {
+    unsigned long long r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+
+// D8 nearest point (core/e8_quantizer.py:20-58).  Flip cost RN(1 - 2|res|)
+// is one FMA because 2|res| is exact; the first-index argmin runs as a
+// tree in which the right operand wins only when strictly smaller, which
+// selects the same index as a left-to-right scan.
 __device__ __forceinline__ void d8_nearest(const float x[8], float r[8]) {
-    float res[8];
+    float res[8], c[8];
     float s = 0.0f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         r[i] = rintf(x[i]);
         s = __fadd_rn(s, r[i]);
         res[i] = __fsub_rn(x[i], r[i]);
+        c[i] = __fmaf_rn(-2.0f, fabsf(res[i]), 1.0f);
+        if (i) c[i] = __fadd_rn(c[i], e8_tie(i));
     }
     // parity = s % 2 != 0; s is integer valued, and even once |s| >= 2^24
     const bool odd = (fabsf(s) < 16777216.0f) && (((int)s) & 1);
-    if (odd) {
-        int best = 0;
-        float bestc = __fsub_rn(1.0f, __fmul_rn(2.0f, fabsf(res[0])));  // + tie(0) == + 0
+    float c01 = c[0], c23 = c[2], c45 = c[4], c67 = c[6];
+    int i01 = 0, i23 = 2, i45 = 4, i67 = 6;
+    if (c[1] < c01) { c01 = c[1]; i01 = 1; }
+    if (c[3] < c23) { c23 = c[3]; i23 = 3; }
+    if (c[5] < c45) { c45 = c[5]; i45 = 5; }
+    if (c[7] < c67) { c67 = c[7]; i67 = 7; }
+    if (c23 < c01) { c01 = c23; i01 = i23; }
+    if (c67 < c45) { c45 = c67; i45 = i67; }
+    const int best = (c45 < c01) ? i45 : i01;
 #pragma unroll
-        for (int i = 1; i < 8; ++i) {
-            const float c = __fadd_rn(__fsub_rn(1.0f, __fmul_rn(2.0f, fabsf(res[i]))), e8_tie(i));
-            if (c < bestc) {
-                bestc = c;
-                best = i;
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            if (i == best) r[i] = __fadd_rn(r[i], res[i] < 0.0f ? -1.0f : 1.0f);
-        }
+    for (int i = 0; i < 8; ++i) {
+        const float sg = res[i] < 0.0f ? -1.0f : 1.0f;  // sign(0) -> +1
+        if (odd && i == best) r[i] = __fadd_rn(r[i], sg);
     }
 }
 
+// E8 nearest point (core/e8_quantizer.py:61-83).  The two squared-distance
+// sums run left to right as the two halves of packed fp32x2 operations.
 __device__ __forceinline__ void e8_nearest(const float x[8], float q[8]) {
     float c1[8], y[8], c2[8];
     d8_nearest(x, c1);
 #pragma unroll
     for (int i = 0; i < 8; ++i) y[i] = __fsub_rn(x[i], 0.5f);
     d8_nearest(y, c2);
-    float d1 = 0.0f, d2 = 0.0f;
+    unsigned long long d = 0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         c2[i] = __fadd_rn(c2[i], 0.5f);
-        const float e1 = __fsub_rn(x[i], c1[i]);
-        const float e2 = __fsub_rn(x[i], c2[i]);
-        d1 = __fadd_rn(d1, __fmul_rn(e1, e1));
-        d2 = __fadd_rn(d2, __fmul_rn(e2, e2));
+        const unsigned long long e = f2_pack(__fsub_rn(x[i], c1[i]), __fsub_rn(x[i], c2[i]));
+        const unsigned long long e2 = f2_mul(e, e);
+        d = i ? f2_add(d, e2) : e2;  // 0 + v == v exactly
     }
+    float d1, d2;
+    f2_unpack(d, d1, d2);
     const bool use1 = d1 <= d2;
 #pragma unroll
     for (int i = 0; i < 8; ++i) q[i] = use1 ? c1[i] : c2[i];
+}
+
+// E8 nearest point fused with e8_to_symbols (core/entropy_coder.py:46-68).
+// The winning candidate's D8 coordinates are the symbols directly: for the
+// integer coset q = c1 and round(q) = c1; for the half coset q = c2 + 1/2 and
+// round(q - 1/2) = c2 (exact while |q| < 2^22, far beyond the symbol range).
+// Returns the coset bit; *finite is false when any distance is NaN/inf
+// (a non-finite input).
+__device__ __forceinline__ int e8_nearest_symbols(const float x[8], float q[8], int sym[8], bool *finite) {
+    float c1[8], y[8], c2[8];
+    d8_nearest(x, c1);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) y[i] = __fsub_rn(x[i], 0.5f);
+    d8_nearest(y, c2);
+    unsigned long long d = 0;
+    float h[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        h[i] = __fadd_rn(c2[i], 0.5f);
+        const unsigned long long e = f2_pack(__fsub_rn(x[i], c1[i]), __fsub_rn(x[i], h[i]));
+        const unsigned long long e2 = f2_mul(e, e);
+        d = i ? f2_add(d, e2) : e2;
+    }
+    float d1, d2;
+    f2_unpack(d, d1, d2);
+    *finite = isfinite(d1) && isfinite(d2);
+    const bool use1 = d1 <= d2;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        q[i] = use1 ? c1[i] : h[i];
+        sym[i] = __float2int_rn(use1 ? c1[i] : c2[i]);
+    }
+    sym[7] = sym[7] >> 1;  // floor(coord8 / 2)
+    return use1 ? 0 : 1;
 }
 
 // e8_to_symbols (core/entropy_coder.py:46-68): coset = |q0 - round(q0)| > 0.25,

@@ -101,8 +101,41 @@ __global__ void unpack_kernel(const uint8_t *__restrict__ in, int64_t n, int b, 
     }
 }
 
+__global__ void selftest_div_kernel(const float *__restrict__ a, const float *__restrict__ b, int64_t n,
+                                    float *__restrict__ out) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float bb = b[i];
+    out[i] = div_by_scale(a[i], bb, __frcp_rn(bb), scale_ok_for_fast_div(bb));
+}
+
+__global__ void selftest_fastdiv_kernel(const uint32_t *__restrict__ num, int64_t n, FastDiv d,
+                                        uint32_t *__restrict__ out) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = d.div(num[i]);
+}
+
 }  // namespace
 }  // namespace lq
+
+extern "C" int lq_selftest(int which, const void *a, const void *b, int64_t n, uint32_t d, void *out, void *stream) {
+    if (n < 0 || !out || !a) return LQ_ERR_INVALID;
+    if (n == 0) return LQ_OK;
+    const unsigned g = (unsigned)lq::ceil_div(n, 256);
+    cudaStream_t st = lq::as_stream(stream);
+    if (which == LQ_SELFTEST_DIV) {
+        if (!b) return LQ_ERR_INVALID;
+        lq::selftest_div_kernel<<<g, 256, 0, st>>>(static_cast<const float *>(a), static_cast<const float *>(b), n,
+                                                    static_cast<float *>(out));
+    } else if (which == LQ_SELFTEST_FASTDIV) {
+        if (d == 0 || d >= 0x80000000u) return LQ_ERR_INVALID;
+        lq::selftest_fastdiv_kernel<<<g, 256, 0, st>>>(static_cast<const uint32_t *>(a), n, lq::FastDiv(d),
+                                                        static_cast<uint32_t *>(out));
+    } else {
+        return LQ_ERR_INVALID;
+    }
+    return lq::check_launch();
+}
 
 extern "C" int lq_version(void) { return 100; }
 

@@ -27,98 +27,114 @@ constexpr int kSmemHalf = 128;      // shared histogram window [-128, 128)
 constexpr int kSmemBins = 2 * kSmemHalf;
 
 template <int DT, int DQ>
-__global__ void __launch_bounds__(32 * kQWarps) quantize_kernel(
-    const void *__restrict__ x, int64_t n_heads, int64_t bph, const float *__restrict__ scale_f32, int64_t TB,
-    int64_t n_tiles, int16_t *__restrict__ sym_rows, uint32_t *__restrict__ coset_words, uint32_t *__restrict__ tile_n0,
-    uint32_t *__restrict__ hist, void *__restrict__ deq, float *__restrict__ q_out, uint32_t *__restrict__ err) {
+__global__ void __launch_bounds__(32 * kQWarps, 4) quantize_kernel(
+    const void *__restrict__ x, uint32_t n_heads, uint32_t bph, FastDiv bph_div, const float *__restrict__ scale_f32,
+    uint32_t TB, uint32_t n_tiles, int16_t *__restrict__ sym_rows, uint32_t *__restrict__ coset_words,
+    uint32_t *__restrict__ tile_n0, uint32_t *__restrict__ hist, void *__restrict__ deq, float *__restrict__ q_out,
+    uint32_t *__restrict__ err) {
     __shared__ uint32_t sh_hist[LQ_NSTREAMS * kSmemBins];
-    const int lane = threadIdx.x & 31;
-    const int warp = threadIdx.x >> 5;
-    const int64_t chunk = blockIdx.y;
-    const int64_t N = n_heads * bph;
-    const int64_t words_per_chunk = ceil_div(N, 32);
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t warp = threadIdx.x >> 5;
+    const uint32_t chunk = blockIdx.y;
+    const uint32_t N = n_heads * bph;
+    const uint32_t words_per_chunk = (N + 31) / 32;
 
     for (int i = threadIdx.x; i < LQ_NSTREAMS * kSmemBins; i += blockDim.x) sh_hist[i] = 0;
     __syncthreads();
 
-    const int64_t tile = (int64_t)blockIdx.x * kQWarps + warp;
+    const uint32_t tile = blockIdx.x * kQWarps + warp;
     uint32_t flags = 0;
     if (tile < n_tiles) {
-        const int64_t b0 = tile * TB;
-        const int64_t tb = (b0 + TB <= N) ? TB : N - b0;
-        const int64_t cblk0 = chunk * N;  // first block of the chunk in x
-        int16_t *rows = sym_rows + (chunk * n_tiles + tile) * TB * 8;
-        int64_t n0 = 0, n1 = 0;  // running coset counts
-        for (int64_t off = 0; off < tb; off += 32) {
-            const int64_t b = b0 + off + lane;  // block within chunk
+        const uint32_t b0 = tile * TB;
+        const uint32_t tb = (b0 + TB <= N) ? TB : N - b0;
+        const int64_t cblk0 = (int64_t)chunk * N;  // first block of the chunk
+        int16_t *rows = sym_rows + ((int64_t)chunk * n_tiles + tile) * TB * 8;
+        const float *sc_chunk = scale_f32 + (int64_t)chunk * n_heads;
+        uint32_t *cw = coset_words + (int64_t)chunk * words_per_chunk + b0 / 32;
+        // per-thread position: block b = b0 + off + lane lives in head `head`, at `rem` within it
+        uint32_t head = bph_div.div(b0 + lane);
+        uint32_t rem = b0 + lane - head * bph;
+        uint32_t cur_head = 0xffffffffu;
+        float sc = 1.0f, rcp = 1.0f;
+        bool fast = false;
+        uint32_t n0 = 0, n1 = 0;  // running coset counts
+        for (uint32_t off = 0; off < tb; off += 32) {
             const bool active = (off + lane) < tb;
             int sym[8] = {0, 0, 0, 0, 0, 0, 0, 0};
             int coset = 0;
             if (active) {
-                const int64_t head = b / bph;
-                const float sc = scale_f32[chunk * n_heads + head];
-                float v[8], xs[8], q[8];
-                load_block8<DT>(x, cblk0 + b, v);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    xs[i] = __fdiv_rn(v[i], sc);
-                    if (!isfinite(xs[i])) flags |= LQ_EF_NONFINITE;
+                if (head != cur_head) {
+                    cur_head = head;
+                    sc = sc_chunk[head];
+                    rcp = __frcp_rn(sc);
+                    fast = scale_ok_for_fast_div(sc);
                 }
-                e8_nearest(xs, q);
+                const int64_t blk = cblk0 + b0 + off + lane;
+                float v[8], xs[8], q[8];
+                load_block8<DT>(x, blk, v);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) xs[i] = div_by_scale(v[i], sc, rcp, fast);
+                bool finite;
+                coset = e8_nearest_symbols(xs, q, sym, &finite);
+                if (!finite) flags |= LQ_EF_NONFINITE;
                 if constexpr (DQ >= 0) {
                     float o[8];
 #pragma unroll
                     for (int i = 0; i < 8; ++i) o[i] = __fmul_rn(q[i], sc);
-                    store_block8<DQ>(deq, cblk0 + b, o);
+                    store_block8<DQ>(deq, blk, o);
                 }
                 if (q_out) {
-                    float4 *qp = reinterpret_cast<float4 *>(q_out) + 2 * (cblk0 + b);
+                    float4 *qp = reinterpret_cast<float4 *>(q_out) + 2 * blk;
                     qp[0] = make_float4(q[0], q[1], q[2], q[3]);
                     qp[1] = make_float4(q[4], q[5], q[6], q[7]);
                 }
-                coset = e8_symbols(q, sym);
                 // symbols must fit the histogram window (float->int saturates, so huge values land outside)
+                int lo = sym[0], hi = sym[0];
 #pragma unroll
-                for (int i = 0; i < 8; ++i)
-                    if (sym[i] < -LQ_SYM_LIMIT || sym[i] >= LQ_SYM_LIMIT) flags |= LQ_EF_SYMRANGE;
+                for (int i = 1; i < 8; ++i) {
+                    lo = min(lo, sym[i]);
+                    hi = max(hi, sym[i]);
+                }
+                if (lo < -LQ_SYM_LIMIT || hi >= LQ_SYM_LIMIT) flags |= LQ_EF_SYMRANGE;
             }
             const uint32_t ball = __ballot_sync(0xffffffffu, active && coset);
             const uint32_t act = __ballot_sync(0xffffffffu, active);
-            if (lane == 0) coset_words[chunk * words_per_chunk + (b0 + off) / 32] = ball;
+            if (lane == 0) cw[off / 32] = ball;
             const uint32_t lt = (1u << lane) - 1u;
             if (active) {
-                int64_t row;
-                if (coset) {
-                    row = tb - 1 - (n1 + __popc(ball & lt));
-                } else {
-                    row = n0 + __popc(act & ~ball & lt);
-                }
+                const uint32_t row = coset ? tb - 1 - (n1 + __popc(ball & lt)) : n0 + __popc(act & ~ball & lt);
                 uint4 packed;
                 packed.x = (uint32_t)(uint16_t)sym[0] | ((uint32_t)(uint16_t)sym[1] << 16);
                 packed.y = (uint32_t)(uint16_t)sym[2] | ((uint32_t)(uint16_t)sym[3] << 16);
                 packed.z = (uint32_t)(uint16_t)sym[4] | ((uint32_t)(uint16_t)sym[5] << 16);
                 packed.w = (uint32_t)(uint16_t)sym[6] | ((uint32_t)(uint16_t)sym[7] << 16);
                 reinterpret_cast<uint4 *>(rows)[row] = packed;
-                uint32_t *gh = hist + (chunk * LQ_NSTREAMS + coset * 8) * LQ_HIST_BINS;
+                uint32_t *sh = sh_hist + coset * 8 * kSmemBins + kSmemHalf;
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
                     const int v = sym[i];
                     if (v >= -kSmemHalf && v < kSmemHalf) {
-                        atomicAdd(&sh_hist[(coset * 8 + i) * kSmemBins + v + kSmemHalf], 1u);
+                        atomicAdd(&sh[i * kSmemBins + v], 1u);
                     } else if (v >= -LQ_SYM_LIMIT && v < LQ_SYM_LIMIT) {
-                        atomicAdd(&gh[i * LQ_HIST_BINS + v + LQ_SYM_LIMIT], 1u);
+                        uint32_t *gh = hist + ((int64_t)chunk * LQ_NSTREAMS + coset * 8 + i) * LQ_HIST_BINS;
+                        atomicAdd(&gh[v + LQ_SYM_LIMIT], 1u);
                     }
                 }
             }
-            const int c1 = __popc(ball);
+            const uint32_t c1 = __popc(ball);
             n1 += c1;
             n0 += __popc(act) - c1;
+            rem += 32;
+            while (rem >= bph) {
+                rem -= bph;
+                ++head;
+            }
         }
-        if (lane == 0) tile_n0[chunk * n_tiles + tile] = (uint32_t)n0;
+        if (lane == 0) tile_n0[(int64_t)chunk * n_tiles + tile] = n0;
     }
     if (flags) raise_flag(err, flags);
     __syncthreads();
-    uint32_t *gh = hist + chunk * LQ_NSTREAMS * LQ_HIST_BINS;
+    uint32_t *gh = hist + (int64_t)chunk * LQ_NSTREAMS * LQ_HIST_BINS;
     for (int i = threadIdx.x; i < LQ_NSTREAMS * kSmemBins; i += blockDim.x) {
         const uint32_t c = sh_hist[i];
         if (c) {
@@ -135,7 +151,8 @@ int launch_quantize(const void *x, int64_t n_chunks, int64_t n_heads, int64_t bp
     const int64_t N = n_heads * bph;
     const int64_t n_tiles = ceil_div(N, TB);
     dim3 grid((unsigned)ceil_div(n_tiles, kQWarps), (unsigned)n_chunks);
-    quantize_kernel<DT, DQ><<<grid, 32 * kQWarps, 0, st>>>(x, n_heads, bph, scale_f32, TB, n_tiles, sym_rows,
+    quantize_kernel<DT, DQ><<<grid, 32 * kQWarps, 0, st>>>(x, (uint32_t)n_heads, (uint32_t)bph, FastDiv((uint32_t)bph),
+                                                            scale_f32, (uint32_t)TB, (uint32_t)n_tiles, sym_rows,
                                                             coset_words, tile_n0, hist, deq, q_out, err);
     return check_launch();
 }
@@ -189,6 +206,7 @@ extern "C" int lq_e8_quantize(const void *x, int dtype, int64_t n_chunks, int64_
         (reinterpret_cast<uintptr_t>(sym_rows) & 15) || (q_out && (reinterpret_cast<uintptr_t>(q_out) & 15)))
         return LQ_ERR_INVALID;
     if (n_chunks > 65535) return LQ_ERR_INVALID;
+    if (n_heads * bph >= (int64_t)1 << 31) return LQ_ERR_INVALID;  // blocks per chunk are indexed in 32 bits
     cudaStream_t st = lq::as_stream(stream);
     if (cudaMemsetAsync(hist, 0, sizeof(uint32_t) * (size_t)n_chunks * LQ_NSTREAMS * LQ_HIST_BINS, st) != cudaSuccess)
         return LQ_ERR_CUDA;

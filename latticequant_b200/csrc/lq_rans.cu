@@ -28,27 +28,29 @@ namespace lq {
 namespace {
 
 // ---------------------------------------------------------------- encode
+// Table entry (lq_expand_tables): 2f | k0 << 12 | (L + cf - f) << 16.
+// From x in [L, 2L): k = k0 + (x >> k0 >= 2f) bits leave (the k low bits of
+// x), then x' = (x >> k) + L + cf - f.  The k bits are prepended to a 32-bit
+// accumulator; full words are written toward the front of the lane's slot.
 __global__ void __launch_bounds__(256) encode_lanes_kernel(
-    const int16_t *__restrict__ sym_rows, const uint32_t *__restrict__ tile_n0, int64_t n_lanes, int64_t n_tiles,
-    int64_t N, int64_t TB, const int32_t *__restrict__ tab_lo, const int32_t *__restrict__ tab_nsym,
-    const uint32_t *__restrict__ enc_tab, uint32_t *__restrict__ scratch, int64_t slot_words,
+    const int16_t *__restrict__ sym_rows, const uint32_t *__restrict__ tile_n0, uint32_t n_lanes, uint32_t n_tiles,
+    uint32_t N, uint32_t TB, const int32_t *__restrict__ tab_lo, const int32_t *__restrict__ tab_nsym,
+    const uint32_t *__restrict__ enc_tab, uint32_t *__restrict__ scratch, uint32_t slot_words,
     uint32_t *__restrict__ lane_nbits, uint32_t *__restrict__ lane_state, uint32_t *__restrict__ lane_nwords,
     uint32_t *err) {
-    const int64_t lg = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const uint32_t lg = blockIdx.x * blockDim.x + threadIdx.x;
     if (lg >= n_lanes) return;
-    const int64_t per_chunk = n_tiles * LQ_NSTREAMS;
-    const int64_t chunk = lg / per_chunk;
-    const int64_t rem = lg - chunk * per_chunk;
-    const int64_t tile = rem >> 4;
-    const int s = (int)(rem & 15), c = s >> 3, idx = s & 7;
-    const int64_t tb = (tile * TB + TB <= N) ? TB : N - tile * TB;
-    const int64_t n0 = tile_n0[chunk * n_tiles + tile];
-    const int64_t n = c ? tb - n0 : n0;
-    const int64_t tabi = chunk * LQ_NSTREAMS + s;
-    uint32_t *out = scratch + lg * slot_words;
-    int64_t wpos = slot_words;
-    uint32_t x = LQ_L;
-    uint64_t nbits = 0;
+    const uint32_t per_chunk = n_tiles * LQ_NSTREAMS;
+    const uint32_t chunk = lg / per_chunk;
+    const uint32_t rem = lg - chunk * per_chunk;
+    const uint32_t tile = rem >> 4;
+    const uint32_t s = rem & 15u, c = s >> 3, idx = s & 7u;
+    const uint32_t tb = (tile * TB + TB <= N) ? TB : N - tile * TB;
+    const uint32_t n0 = tile_n0[chunk * n_tiles + tile];
+    const int n = (int)(c ? tb - n0 : n0);
+    const uint32_t tabi = chunk * LQ_NSTREAMS + s;
+    uint32_t *out = scratch + (size_t)lg * slot_words + slot_words;  // written backward
+    uint32_t x = LQ_L, nbits = 0;
     if (n > 0) {
         const int lo = tab_lo[tabi];
         const int nsym = tab_nsym[tabi];
@@ -59,35 +61,62 @@ __global__ void __launch_bounds__(256) encode_lanes_kernel(
             lane_nwords[lg] = 0;
             return;
         }
-        const uint32_t *enc = enc_tab + tabi * LQ_L;
-        const int16_t *rows = sym_rows + (chunk * n_tiles + tile) * TB * 8 + idx;
-        // symbols in reverse order: coset 0 at rows n0-1 .. 0, coset 1 at rows n0 .. tb-1
-        const int64_t r0 = c ? n0 : n0 - 1;
-        const int64_t dr = c ? 1 : -1;
-        uint64_t acc = 0;
-        int cnt = 0;
-        int64_t row = r0;
-        for (int64_t j = 0; j < n; ++j, row += dr) {
-            int si = (int)rows[row * 8] - lo;
-            si = si < 0 ? 0 : (si >= nsym ? nsym - 1 : si);  // nearest alphabet entry
-            const uint32_t e = __ldg(enc + si);
-            const uint32_t f = e & 0x7ffu, cf = (e >> 11) & 0x3ffu, k0 = e >> 21;
-            const uint32_t k = k0 + (((x >> k0) >= 2 * f) ? 1u : 0u);
-            acc |= (uint64_t)(x & ((1u << k) - 1u)) << cnt;
-            cnt += (int)k;
-            nbits += k;
-            if (cnt >= 32) {
-                out[--wpos] = (uint32_t)acc;
-                acc >>= 32;
-                cnt -= 32;
+        const uint32_t *enc = enc_tab + (size_t)tabi * LQ_L;
+        // symbols in reverse order: coset 0 at rows n0-1 .. 0, coset 1 at rows n0 .. tb-1.
+        // Batches of 8: the next batch's 8 row loads are in flight while this one is coded;
+        // prefetch rows past the lane's end are clamped into the tile.
+        const int16_t *rows = sym_rows + ((size_t)chunk * n_tiles + tile) * TB * 8 + idx;
+        const int r0 = c ? (int)n0 : (int)n0 - 1;
+        const int dr = c ? 1 : -1;
+        const int rlo = 0, rhi = (int)tb - 1;
+        auto row_at = [&](int j) {
+            const int r = r0 + dr * j;
+            return (int)rows[8 * (r < rlo ? rlo : (r > rhi ? rhi : r))];
+        };
+        int sv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sv[i] = row_at(i);
+        uint32_t acc = 0, cnt = 0;
+        uint32_t *const out_end = out;
+        auto code = [&](uint32_t e) {
+            const uint32_t twof = e & 0xfffu, k0 = (e >> 12) & 0xfu;
+            const uint32_t k = k0 + ((x >> k0) >= twof ? 1u : 0u);
+            const uint32_t v = x & ~(0xffffffffu << k);
+            acc |= v << cnt;
+            const uint32_t t = cnt + k;
+            if (t >= 32u) {
+                *--out = acc;
+                acc = v >> (32u - cnt);
             }
-            x = LQ_L + cf + (x >> k) - f;
+            cnt = t & 31u;
+            x = (x >> k) + (e >> 16);
+        };
+        auto entry = [&](int v) {
+            const int si = min(max(v - lo, 0), nsym - 1);  // nearest alphabet entry
+            return __ldg(enc + si);
+        };
+        int j0 = 0;
+        for (; j0 + 8 <= n; j0 += 8) {
+            int sn[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) sn[i] = row_at(j0 + 8 + i);
+            uint32_t e[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) e[i] = entry(sv[i]);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) code(e[i]);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) sv[i] = sn[i];
         }
-        if (cnt > 0) out[--wpos] = (uint32_t)acc;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            if (j0 + i < n) code(entry(sv[i]));
+        nbits = 32u * (uint32_t)(out_end - out) + cnt;
+        if (cnt) *--out = acc;
     }
-    lane_nbits[lg] = (uint32_t)nbits;
+    lane_nbits[lg] = nbits;
     lane_state[lg] = x;
-    lane_nwords[lg] = (uint32_t)(slot_words - wpos);
+    lane_nwords[lg] = (nbits + 31u) >> 5;
 }
 
 // ---------------------------------------------------------------- scan
@@ -222,7 +251,7 @@ struct BitReader {
 // Decode n symbols of one lane into out[j*ostride] (alphabet index).
 // dec: fast table (or nullptr), freq/cf source for the literal path.
 struct LaneTables {
-    const uint32_t *dec;    // [L] si | nb << 10 | (base-L) << 14
+    const uint32_t *dec;    // [L] si | nb << 10 | base << 14
     const uint32_t *enc;    // [nsym] f | cf << 11 (literal path), or nullptr
     const uint16_t *freq;   // [nsym] frequencies (literal path when enc == nullptr)
 };
@@ -250,12 +279,12 @@ __device__ inline void decode_lane(const uint32_t *words, int64_t n_words, int64
         emit(j, si);
         if ((x >> LQ_LOG2_L) == 1u && pos + 10 <= n_bits) {
             const int nb = (int)((e >> 10) & 0xfu);
-            x = ((e >> 14) + LQ_L) | br.read(nb);
+            x = (e >> 14) | br.read(nb);
             pos += nb;
         } else {
             // literal reference semantics (end of lane, or state outside [L, 2L))
             const uint32_t f = freq[si];
-            const uint32_t xp = ((e >> 14) + LQ_L) >> ((e >> 10) & 0xfu);  // f + slot - cf
+            const uint32_t xp = (e >> 14) >> ((e >> 10) & 0xfu);  // f + slot - cf
             const uint32_t cf = f + slot - xp;
             literal_step(x, pos, n_bits, si, f, cf, slot, br);
         }
@@ -329,12 +358,15 @@ __global__ void __launch_bounds__(256) reconstruct_kernel(const int16_t *__restr
                                                            const uint32_t *__restrict__ rank1, int64_t n_chunks,
                                                            int64_t n_heads, int64_t bph, int64_t TB, int64_t n_tiles,
                                                            const uint16_t *__restrict__ scale_f16, void *out,
-                                                           int32_t *sym_out) {
+                                                           int32_t *sym_out, FastDiv n_div, FastDiv tb_div,
+                                                           FastDiv bph_div) {
     const int64_t gb = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t N = n_heads * bph;
     if (gb >= n_chunks * N) return;
-    const int64_t chunk = gb / N, b = gb - chunk * N;
-    const int64_t tile = b / TB, p = b - tile * TB;
+    // gb < 2^31 * 65535: split into chunk and block with 32-bit divisions
+    const int64_t chunk = (gb >> 31) == 0 ? (int64_t)n_div.div((uint32_t)gb) : gb / N;
+    const int64_t b = gb - chunk * N;
+    const int64_t tile = tb_div.div((uint32_t)b), p = b - tile * TB;
     const int64_t tb = (tile * TB + TB <= N) ? TB : N - tile * TB;
     const int64_t wpc = ceil_div(N, 32);
     const uint32_t word = coset_words[chunk * wpc + (b >> 5)];
@@ -357,10 +389,222 @@ __global__ void __launch_bounds__(256) reconstruct_kernel(const int16_t *__restr
     if constexpr (DO >= 0) {
         float q[8];
         e8_from_symbols(c, sym, q);
-        const float sc = __half2float(__ushort_as_half(scale_f16[chunk * n_heads + b / bph]));
+        const float sc = __half2float(__ushort_as_half(scale_f16[chunk * n_heads + bph_div.div((uint32_t)b)]));
 #pragma unroll
         for (int i = 0; i < 8; ++i) q[i] = __fmul_rn(q[i], sc);
         store_block8<DO>(out, gb, q);
+    }
+}
+
+// ---------------------------------------------------------------- fused decode
+// One warp decodes two tiles (32 lanes).  Per round each lane decodes up to
+// kRing symbols of its lane into a shared ring; the warp then rebuilds the
+// blocks whose symbols just arrived (rank r of coset c in tile t -> block
+// position via a rank->position list built from the coset bits) and writes
+// them scaled by the fp16 head scale.  The chunk's 16 decode tables live in
+// shared memory.
+constexpr int kRing = 32;
+constexpr int kRingStride = 40;  // int16 per ring row: 80 B, keeps 8-symbol groups 16-B aligned and conflict-free
+
+__host__ __device__ inline size_t fused_smem_bytes(int nwarps, uint32_t TB) {
+    return (size_t)LQ_NSTREAMS * LQ_L * 4 + (size_t)nwarps * (2 * TB * 2 + kRing * kRingStride * 2);
+}
+
+template <int DO>
+__global__ void __launch_bounds__(512) decode_fused_kernel(
+    const uint32_t *__restrict__ words, uint32_t n_words, const uint32_t *__restrict__ lane_off,
+    const uint32_t *__restrict__ lane_nbits, const uint32_t *__restrict__ lane_state,
+    const uint32_t *__restrict__ coset_words, const uint32_t *__restrict__ tile_n0, uint32_t n_heads, uint32_t bph,
+    FastDiv bph_div, uint32_t TB, uint32_t n_tiles, const int32_t *__restrict__ tab_lo,
+    const int32_t *__restrict__ tab_nsym, const uint16_t *__restrict__ tab_freq, const uint32_t *__restrict__ dec_tab,
+    const uint16_t *__restrict__ scale_f16, void *__restrict__ out, int32_t *__restrict__ sym_out, uint32_t *err) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    uint32_t *dtab = reinterpret_cast<uint32_t *>(smem);
+    const int nwarps = blockDim.x >> 5;
+    uint16_t *rows_all = reinterpret_cast<uint16_t *>(smem + (size_t)LQ_NSTREAMS * LQ_L * 4);
+    int16_t *ring_all = reinterpret_cast<int16_t *>(rows_all + (size_t)nwarps * 2 * TB);
+
+    const uint32_t chunk = blockIdx.y;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    {
+        const uint4 *src = reinterpret_cast<const uint4 *>(dec_tab + (size_t)chunk * LQ_NSTREAMS * LQ_L);
+        uint4 *dst = reinterpret_cast<uint4 *>(dtab);
+        for (int i = threadIdx.x; i < LQ_NSTREAMS * LQ_L / 4; i += blockDim.x) dst[i] = __ldg(src + i);
+    }
+    __syncthreads();
+
+    const uint32_t N = n_heads * bph;
+    const uint32_t wpc = (N + 31) >> 5;
+    const uint32_t tile0 = (blockIdx.x * nwarps + warp) * 2;
+    if (tile0 >= n_tiles) return;
+    uint16_t *rows = rows_all + (size_t)warp * 2 * TB;
+    int16_t *ring = ring_all + (size_t)warp * kRing * kRingStride;
+    const uint32_t lt = (1u << lane) - 1u;
+
+    uint32_t tbv[2], n0v[2];
+    bool tact[2];
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+        const uint32_t tile = tile0 + t;
+        tact[t] = tile < n_tiles;
+        tbv[t] = tact[t] ? ((tile * TB + TB <= N) ? TB : N - tile * TB) : 0u;
+        n0v[t] = tact[t] ? tile_n0[chunk * n_tiles + tile] : 0u;
+        if (!tact[t]) continue;
+        // rank -> position lists: coset-0 rank r at r, coset-1 rank r at tb-1-r
+        const uint32_t *cw = coset_words + (size_t)chunk * wpc + (size_t)tile * (TB >> 5);
+        uint32_t c0 = 0, c1 = 0;
+        const uint32_t tb = tbv[t];
+        for (uint32_t off = 0; off < tb; off += 32) {
+            const uint32_t word = __ldg(cw + (off >> 5));
+            const uint32_t left = tb - off;
+            const uint32_t actm = left >= 32 ? 0xffffffffu : ((1u << left) - 1u);
+            const uint32_t w1 = word & actm, w0 = ~word & actm;
+            if (lane < left) {
+                const uint32_t pos = ((word >> lane) & 1u) ? tb - 1 - (c1 + __popc(w1 & lt)) : c0 + __popc(w0 & lt);
+                rows[t * TB + pos] = (uint16_t)(off + lane);
+            }
+            c1 += __popc(w1);
+            c0 += __popc(w0);
+        }
+    }
+
+    // lane setup: lanes 0-15 -> tile0, 16-31 -> tile0+1; stream s = lane & 15
+    const uint32_t lt_tile = lane >> 4, s = lane & 15u, c = s >> 3;
+    const uint32_t tile = tile0 + lt_tile;
+    const bool my_act = lt_tile ? tact[1] : tact[0];
+    const uint32_t my_tb = lt_tile ? tbv[1] : tbv[0], my_n0 = lt_tile ? n0v[1] : n0v[0];
+    int n = my_act ? (int)(c ? my_tb - my_n0 : my_n0) : 0;
+    const uint32_t tabi = chunk * LQ_NSTREAMS + s;
+    int lo = 0;
+    uint32_t x = LQ_L, nb = 0, nw = 0;
+    const uint32_t *wp = words;
+    if (n > 0) {
+        const int nsym = tab_nsym[tabi];
+        lo = tab_lo[tabi];
+        const uint32_t lg = (chunk * n_tiles + tile) * LQ_NSTREAMS + s;
+        const uint32_t w0 = lane_off[lg];
+        nb = lane_nbits[lg];
+        nw = (nb + 31u) >> 5;
+        x = lane_state[lg];
+        if (nsym <= 0 || nsym > LQ_L) {
+            raise_flag(err, LQ_EF_ALPHABET);
+            n = 0;
+        } else if ((uint64_t)w0 + nw > n_words) {
+            raise_flag(err, LQ_EF_BITSTREAM);
+            n = 0;
+        }
+        wp = words + w0;
+    }
+    const uint32_t *dt = dtab + s * LQ_L;
+    const uint16_t *fr = tab_freq + (size_t)tabi * LQ_L;
+    // 64-bit MSB-first bit buffer over the lane's words (bit-reversed reference
+    // words).  `avail` counts valid bits; a step takes at most 10, so after a
+    // refill (avail >= 33) three table-driven steps can run before the next
+    // refill, which is predicated rather than branched.
+    uint64_t bb = 0;
+    int avail = 0;
+    uint32_t wi = 0;
+    auto refill = [&]() {
+        const bool need = avail <= 32;
+        const uint32_t w = (need && wi < nw) ? __brev(__ldg(wp + wi)) : 0u;
+        if (need) {
+            bb |= (uint64_t)w << (32 - avail);
+            avail += 32;
+            ++wi;
+        }
+    };
+    refill();
+    refill();
+    // bits consumed so far = 32*wi - avail (words past the end read as zeros)
+    // the table-driven step is exact while x is in [L, 2L) and 10 more bits exist
+    int budget = (int)nb - 10;
+    bool fast_ok = (x >> LQ_LOG2_L) == 1u;
+    const int maxn = (int)__reduce_max_sync(0xffffffffu, (unsigned)n);
+
+    auto fast_step = [&](int j) {
+        const uint32_t slot = x & (LQ_L - 1);
+        const uint32_t e = dt[slot];
+        ring[j * kRingStride + lane] = (int16_t)((int)(e & 0x3ffu) + lo);
+        const uint32_t k = (e >> 10) & 0xfu;
+        x = (e >> 14) | __funnelshift_lc((uint32_t)(bb >> 32), 0u, k);
+        bb <<= k;
+        avail -= (int)k;
+        budget -= (int)k;
+    };
+    auto slow_step = [&](int j) {
+        const uint32_t slot = x & (LQ_L - 1);
+        const uint32_t e = dt[slot];
+        const uint32_t si = e & 0x3ffu;
+        ring[j * kRingStride + lane] = (int16_t)((int)si + lo);
+        const uint32_t k = (e >> 10) & 0xfu;
+        if (fast_ok && budget >= 0) {
+            x = (e >> 14) | __funnelshift_lc((uint32_t)(bb >> 32), 0u, k);
+            bb <<= k;
+            avail -= (int)k;
+            budget -= (int)k;
+        } else {
+            // literal reference step (end of lane, or a state outside [L, 2L))
+            uint32_t pos = (uint32_t)((int)nb - 10 - budget);
+            const uint32_t f = fr[si];
+            const uint32_t cf = f + slot - ((e >> 14) >> k);  // (e >> 14) >> k == f + slot - cf
+            x = f * (x >> LQ_LOG2_L) + slot - cf;
+            while (x < (uint32_t)LQ_L && pos < nb) {
+                x = (x << 1) | (uint32_t)(bb >> 63);
+                bb <<= 1;
+                --avail;
+                ++pos;
+                refill();
+            }
+            budget = (int)nb - 10 - (int)pos;
+            fast_ok = (x >> LQ_LOG2_L) == 1u;
+        }
+        refill();
+    };
+
+    for (int base = 0; base < maxn; base += kRing) {
+        const int cnt = min(kRing, n - base);
+        int j = 0;
+        // groups of three table-driven steps while every step of the group is exact
+        for (; j + 3 <= cnt && fast_ok && budget >= 20; j += 3) {
+            fast_step(j);
+            fast_step(j + 1);
+            fast_step(j + 2);
+            refill();
+        }
+        for (; j < cnt; ++j) slow_step(j);
+        __syncwarp();
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+            const int t = g >> 1, cc = g & 1;
+            if (!tact[t]) continue;
+            const int nc = (int)(cc ? tbv[t] - n0v[t] : n0v[t]);
+            const int r = base + (int)lane;
+            if (r < nc) {
+                const uint32_t p = rows[t * TB + (cc ? tbv[t] - 1 - r : r)];
+                const uint4 u = *reinterpret_cast<const uint4 *>(ring + lane * kRingStride + t * 16 + cc * 8);
+                int sym[8];
+                sym[0] = (int16_t)(u.x & 0xffffu); sym[1] = (int16_t)(u.x >> 16);
+                sym[2] = (int16_t)(u.y & 0xffffu); sym[3] = (int16_t)(u.y >> 16);
+                sym[4] = (int16_t)(u.z & 0xffffu); sym[5] = (int16_t)(u.z >> 16);
+                sym[6] = (int16_t)(u.w & 0xffffu); sym[7] = (int16_t)(u.w >> 16);
+                const uint32_t b = (tile0 + t) * TB + p;
+                const size_t gb = (size_t)chunk * N + b;
+                if (sym_out) {
+                    int4 *so = reinterpret_cast<int4 *>(sym_out) + 2 * gb;
+                    so[0] = make_int4(sym[0], sym[1], sym[2], sym[3]);
+                    so[1] = make_int4(sym[4], sym[5], sym[6], sym[7]);
+                }
+                if constexpr (DO >= 0) {
+                    float q[8];
+                    e8_from_symbols(cc, sym, q);
+                    const float sc = __half2float(__ushort_as_half(scale_f16[chunk * n_heads + bph_div.div(b)]));
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) q[i] = __fmul_rn(q[i], sc);
+                    store_block8<DO>(out, gb, q);
+                }
+            }
+        }
+        __syncwarp();
     }
 }
 
@@ -452,8 +696,8 @@ extern "C" int lq_rans_encode(const int16_t *sym_rows, const uint32_t *tile_n0, 
     uint64_t *bsum = reinterpret_cast<uint64_t *>(static_cast<char *>(workspace) + off);
     const int64_t nblk = ceil_div(n_lanes, kScanTile);
     encode_lanes_kernel<<<(unsigned)ceil_div(n_lanes, 256), 256, 0, st>>>(
-        sym_rows, tile_n0, n_lanes, n_tiles, n_vectors, tile_blocks, tab_lo, tab_nsym, enc_tab, scratch, sw,
-        lane_nbits, lane_state, nwords, err);
+        sym_rows, tile_n0, (uint32_t)n_lanes, (uint32_t)n_tiles, (uint32_t)n_vectors, (uint32_t)tile_blocks, tab_lo,
+        tab_nsym, enc_tab, scratch, (uint32_t)sw, lane_nbits, lane_state, nwords, err);
     scan_reduce_kernel<<<(unsigned)nblk, kScanT, 0, st>>>(nwords, n_lanes, bsum);
     scan_blocks_kernel<<<1, kScanT, 0, st>>>(bsum, nblk);
     scan_write_kernel<<<(unsigned)nblk, kScanT, 0, st>>>(nwords, n_lanes, bsum, lane_off, words_cap, err);
@@ -490,6 +734,31 @@ extern "C" int lq_rans_decode(const uint32_t *words, int64_t n_words, const uint
     cudaStream_t st = as_stream(stream);
     const int64_t n_tiles = ceil_div(N, tile_blocks);
     const int64_t n_lanes = n_chunks * n_tiles * LQ_NSTREAMS;
+    // fused path: tables + per-warp rank lists + rings fit in shared memory
+    int nwarps = 16;
+    while (nwarps >= 4 && fused_smem_bytes(nwarps, (uint32_t)tile_blocks) > 227 * 1024) nwarps -= 1;
+    if (nwarps >= 4 && n_chunks <= 65535 && n_lanes < ((int64_t)1 << 32)) {
+        const size_t sm = fused_smem_bytes(nwarps, (uint32_t)tile_blocks);
+        dim3 grid((unsigned)ceil_div(n_tiles, 2 * nwarps), (unsigned)n_chunks);
+        const FastDiv bd((uint32_t)bph);
+#define LQ_LAUNCH_FUSED(DOV)                                                                                    \
+    do {                                                                                                        \
+        if (cudaFuncSetAttribute(decode_fused_kernel<DOV>, cudaFuncAttributeMaxDynamicSharedMemorySize,        \
+                                 (int)sm) != cudaSuccess)                                                       \
+            return LQ_ERR_CUDA;                                                                                 \
+        decode_fused_kernel<DOV><<<grid, 32 * nwarps, sm, st>>>(                                                \
+            words, (uint32_t)n_words, lane_off, lane_nbits, lane_state, coset_words, tile_n0, (uint32_t)n_heads, \
+            (uint32_t)bph, bd, (uint32_t)tile_blocks, (uint32_t)n_tiles, tab_lo, tab_nsym, tab_freq, dec_tab,     \
+            scale_f16, out, sym_out, err);                                                                      \
+    } while (0)
+        if (!out) LQ_LAUNCH_FUSED(-1);
+        else if (out_dtype == LQ_F32) LQ_LAUNCH_FUSED(LQ_F32);
+        else if (out_dtype == LQ_F16) LQ_LAUNCH_FUSED(LQ_F16);
+        else if (out_dtype == LQ_BF16) LQ_LAUNCH_FUSED(LQ_BF16);
+        else return LQ_ERR_INVALID;
+#undef LQ_LAUNCH_FUSED
+        return check_launch();
+    }
     int16_t *rows = static_cast<int16_t *>(workspace);
     uint32_t *rank1 = reinterpret_cast<uint32_t *>(rows + 8 * n_chunks * n_tiles * tile_blocks);
     decode_lanes_kernel<<<(unsigned)ceil_div(n_lanes, 256), 256, 0, st>>>(
@@ -500,18 +769,19 @@ extern "C" int lq_rans_decode(const uint32_t *words, int64_t n_words, const uint
     coset_rank_kernel<<<(unsigned)ceil_div(n_chunks * n_tiles, 256), 256, 0, st>>>(coset_words, n_chunks, wpc, wpt,
                                                                                    rank1);
     const unsigned g = (unsigned)ceil_div(n_chunks * N, 256);
+    const FastDiv nd((uint32_t)N), td((uint32_t)tile_blocks), bd((uint32_t)bph);
     if (!out) {
         reconstruct_kernel<-1><<<g, 256, 0, st>>>(rows, coset_words, rank1, n_chunks, n_heads, bph, tile_blocks,
-                                                  n_tiles, scale_f16, out, sym_out);
+                                                  n_tiles, scale_f16, out, sym_out, nd, td, bd);
     } else if (out_dtype == LQ_F32) {
         reconstruct_kernel<LQ_F32><<<g, 256, 0, st>>>(rows, coset_words, rank1, n_chunks, n_heads, bph, tile_blocks,
-                                                      n_tiles, scale_f16, out, sym_out);
+                                                      n_tiles, scale_f16, out, sym_out, nd, td, bd);
     } else if (out_dtype == LQ_F16) {
         reconstruct_kernel<LQ_F16><<<g, 256, 0, st>>>(rows, coset_words, rank1, n_chunks, n_heads, bph, tile_blocks,
-                                                      n_tiles, scale_f16, out, sym_out);
+                                                      n_tiles, scale_f16, out, sym_out, nd, td, bd);
     } else if (out_dtype == LQ_BF16) {
         reconstruct_kernel<LQ_BF16><<<g, 256, 0, st>>>(rows, coset_words, rank1, n_chunks, n_heads, bph, tile_blocks,
-                                                       n_tiles, scale_f16, out, sym_out);
+                                                       n_tiles, scale_f16, out, sym_out, nd, td, bd);
     } else {
         return LQ_ERR_INVALID;
     }

@@ -65,7 +65,23 @@ __device__ __forceinline__ float chain_block(const void *xh, int64_t i0, int64_t
     float acc1 = 0.0f;
     const int64_t full = (i1 - i0) / G;
     int64_t i = i0;
-    for (int64_t g = 0; g < full; ++g) {
+    int64_t g = 0;
+    if (G == 16) {
+        // two level-0 groups per batch: 32 loads in flight, adds still in order
+        for (; g + 1 < full; g += 2) {
+            float v[32];
+#pragma unroll
+            for (int u = 0; u < 32; ++u) v[u] = sq<DT>(xh, 32 * (i + u) + lane);
+            float a = 0.0f, b = 0.0f;
+#pragma unroll
+            for (int u = 0; u < 16; ++u) a = __fadd_rn(a, v[u]);
+#pragma unroll
+            for (int u = 16; u < 32; ++u) b = __fadd_rn(b, v[u]);
+            acc1 = __fadd_rn(__fadd_rn(acc1, a), b);
+            i += 32;
+        }
+    }
+    for (; g < full; ++g) {
         float a0 = 0.0f;
         // 16 loads in flight before the dependent adds
         for (int64_t j = 0; j < G; j += 16) {
@@ -142,10 +158,47 @@ __global__ void __launch_bounds__(256) scale_small_kernel(const void *x, int64_t
     if (lane == 0) write_scale(h, sum, E, vol_mult, sigma2, scale_f32, scale_f16);
 }
 
+// 16-bit input, complete level-1 block with G = 16 (256 rows of 32 chains):
+// 64-row batches arrive as 16-byte loads (4 KB per warp in flight), are
+// transposed through shared memory, and each lane sums its chain in order.
+template <int DT>
+__device__ __forceinline__ float chain_block_vec16(const char *xh, int64_t i0, int lane, uint4 *stage) {
+    const uint4 *src = reinterpret_cast<const uint4 *>(xh + i0 * 64);  // 32 chains x 2 B per row
+    const uint16_t *st16 = reinterpret_cast<const uint16_t *>(stage);
+    uint4 buf[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) buf[k] = __ldg(src + k * 32 + lane);
+    float acc1 = 0.0f;
+#pragma unroll 1
+    for (int b = 0; b < 4; ++b) {
+        __syncwarp();
+#pragma unroll
+        for (int k = 0; k < 8; ++k) stage[k * 32 + lane] = buf[k];
+        __syncwarp();
+        if (b < 3) {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) buf[k] = __ldg(src + (b + 1) * 256 + k * 32 + lane);
+        }
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+            float a0 = 0.0f;
+#pragma unroll
+            for (int r = 0; r < 16; ++r) {
+                const uint16_t u = st16[(g * 16 + r) * 32 + lane];
+                const float t = DT == LQ_F16 ? __half2float(__ushort_as_half(u)) : __bfloat162float(__ushort_as_bfloat16(u));
+                a0 = __fadd_rn(a0, __fmul_rn(t, t));
+            }
+            acc1 = __fadd_rn(acc1, a0);
+        }
+    }
+    return acc1;
+}
+
 // Pass 1 (large heads): one warp per (head, level-1 block).
 template <int DT>
 __global__ void __launch_bounds__(256) scale_l1_kernel(const void *x, int64_t n_heads, int64_t E, float *l1,
                                                         float *tails) {
+    __shared__ uint4 stage_all[8][256];  // 4 KB per warp
     const int lane = threadIdx.x & 31;
     const Cascade c(E);
     const int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -155,7 +208,14 @@ __global__ void __launch_bounds__(256) scale_l1_kernel(const void *x, int64_t n_
     const int64_t i0 = j * c.G * c.G;
     const int64_t i1 = (i0 + c.G * c.G < c.S) ? i0 + c.G * c.G : c.S;
     float tail;
-    const float part = chain_block<DT>(xh, i0, i1, c.G, lane, &tail);
+    float part;
+    const bool aligned = (reinterpret_cast<uintptr_t>(xh) & 15) == 0;
+    if (DT != LQ_F32 && c.G == 16 && i1 - i0 == 256 && aligned) {
+        part = chain_block_vec16<DT>(xh, i0, lane, stage_all[threadIdx.x >> 5]);
+        tail = 0.0f;
+    } else {
+        part = chain_block<DT>(xh, i0, i1, c.G, lane, &tail);
+    }
     l1[w * 32 + lane] = part;
     if (j == c.n_l1 - 1) tails[h * 32 + lane] = tail;
 }

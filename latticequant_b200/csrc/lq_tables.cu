@@ -53,12 +53,40 @@ __device__ inline int block_max_i(int v, int *sh) {
     return t;
 }
 
+// Rank of every entry under (key descending, index ascending): bitonic sort
+// of (~key << 32 | index) over the next power of two >= n, in shared memory.
+__device__ void stable_desc_ranks(const int32_t *key, int n, uint64_t *sk, int32_t *rnk) {
+    int n2 = 1;
+    while (n2 < n) n2 <<= 1;
+    for (int i = threadIdx.x; i < n2; i += blockDim.x)
+        sk[i] = i < n ? (((uint64_t)(0xffffffffu - (uint32_t)key[i]) << 32) | (uint32_t)i) : ~0ull;
+    __syncthreads();
+    for (int k = 2; k <= n2; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < n2; i += blockDim.x) {
+                const int ixj = i ^ j;
+                if (ixj > i) {
+                    const uint64_t a = sk[i], b = sk[ixj];
+                    if (((i & k) == 0) == (a > b)) {
+                        sk[i] = b;
+                        sk[ixj] = a;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    for (int p = threadIdx.x; p < n; p += blockDim.x) rnk[(uint32_t)(sk[p] & 0xffffffffu)] = p;
+    __syncthreads();
+}
+
 __global__ void __launch_bounds__(kTT) build_tables_kernel(const uint32_t *__restrict__ hist, int64_t n_tables,
                                                             int32_t *__restrict__ tab_lo, int32_t *__restrict__ tab_nsym,
                                                             uint16_t *__restrict__ tab_freq, uint32_t *err) {
-    __shared__ uint32_t cnt[LQ_L + 4];
+    __shared__ int32_t cnt[LQ_L];
     __shared__ int32_t freq[LQ_L];
     __shared__ int32_t rnk[LQ_L];
+    __shared__ uint64_t sk[LQ_L];
     __shared__ uint64_t red64[kTT / 32];
     __shared__ int redi[kTT / 32];
     const int64_t t = blockIdx.x;
@@ -101,68 +129,102 @@ __global__ void __launch_bounds__(kTT) build_tables_kernel(const uint32_t *__res
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         const int b = lo_bin + i;
         const uint32_t c = (b >= 0 && b < LQ_HIST_BINS) ? h[b] : 0u;
-        cnt[i] = c;
+        cnt[i] = (int32_t)c;  // counts per stream stay below 2^31 (blocks per chunk < 2^31)
         // numpy: (counts / total * L).astype(int32), then max(., 1)
         const int f = (int)__dmul_rn(__ddiv_rn((double)c, dtotal), (double)LQ_L);
         freq[i] = f < 1 ? 1 : f;
     }
     __syncthreads();
-    // ranks by (counts desc, index asc): fixed across the loop
+    __shared__ int32_t cand[LQ_L];
+    __shared__ int n_cand;
     bool have_count_rank = false;
-    for (int iter = 0; iter < 64; ++iter) {
+    // Each pass of the reference loop either fixes the sum (diff > 0: one
+    // increment pass) or removes at least one from a frequency > 1, so at most
+    // L + 1 passes run; the bound only guards against a corrupt histogram.
+    for (int iter = 0; iter <= LQ_L + 1; ++iter) {
         uint64_t part = 0;
         for (int i = threadIdx.x; i < n; i += blockDim.x) part += (uint64_t)freq[i];
         const int64_t sum = (int64_t)block_sum_u64(part, red64);
         if (sum == LQ_L) break;
+        if (iter == LQ_L + 1) {
+            if (threadIdx.x == 0) raise_flag(err, LQ_EF_NOCONVERGE);
+            break;
+        }
         const int64_t diff = LQ_L - sum;
         if (diff > 0) {
+            // argsort(-counts): fixed across iterations
             if (!have_count_rank) {
-                for (int i = threadIdx.x; i < n; i += blockDim.x) {
-                    const uint32_t ki = cnt[i];
-                    int r = 0;
-                    for (int j = 0; j < n; ++j) {
-                        const uint32_t kj = cnt[j];
-                        r += (kj > ki) || (kj == ki && j < i);
-                    }
-                    rnk[i] = r;
-                }
+                stable_desc_ranks(cnt, n, sk, rnk);
                 have_count_rank = true;
-                __syncthreads();
             }
             for (int i = threadIdx.x; i < n; i += blockDim.x) {
                 const int p = rnk[i];
                 freq[i] += (int)(diff / n) + (p < (int)(diff % n) ? 1 : 0);
             }
-        } else {
-            have_count_rank = false;  // rnk is reused for the freq order
             __syncthreads();
-            for (int i = threadIdx.x; i < n; i += blockDim.x) {
-                const int ki = freq[i];
-                int r = 0;
-                for (int j = 0; j < n; ++j) {
-                    const int kj = freq[j];
-                    r += (kj > ki) || (kj == ki && j < i);
+            continue;
+        }
+        // diff < 0: argsort(-freqs).  Entries at 1 are never decremented and
+        // sort after every entry > 1, so only the m entries > 1 matter, at
+        // positions 0..m-1 of the order.
+        have_count_rank = false;
+        if (threadIdx.x == 0) n_cand = 0;
+        __syncthreads();
+        for (int i = threadIdx.x; i < n; i += blockDim.x)
+            if (freq[i] > 1) cand[atomicAdd(&n_cand, 1)] = i;
+        __syncthreads();
+        const int m = n_cand;
+        if (m <= 32) {
+            // warp 0 finishes every remaining pass in registers
+            if (threadIdx.x < 32) {
+                const int lane = threadIdx.x;
+                // one candidate per lane (lane order is irrelevant: positions
+                // compare frequencies and symbol indices)
+                const int my = lane < m ? cand[lane] : 0x7fffffff;
+                const bool act = lane < m;
+                int f = act ? freq[my] : 1;
+                int64_t d = -diff;
+                for (int pass = 0; pass <= LQ_L + 1 && d > 0; ++pass) {
+                    // position among entries > 1: (f desc, index asc)
+                    int pos = 0;
+                    for (int q = 0; q < 32; ++q) {
+                        const int fq = __shfl_sync(0xffffffffu, f, q);
+                        const int iq = __shfl_sync(0xffffffffu, my, q);
+                        pos += (fq > 1 && (fq > f || (fq == f && iq < my))) ? 1 : 0;
+                    }
+                    int dec = 0;
+                    if (act && f > 1) {
+                        const int visits = (int)(d / n) + (pos < (int)(d % n) ? 1 : 0);
+                        dec = min(visits, f - 1);
+                        f -= dec;
+                    }
+                    int tot = dec;
+                    for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+                    d -= tot;
+                    if (tot == 0) break;  // cannot happen while sum > L: some entry is > 1
                 }
-                rnk[i] = r;
+                if (act) freq[my] = f;
             }
             __syncthreads();
-            const int64_t d = -diff;
-            for (int i = threadIdx.x; i < n; i += blockDim.x) {
-                const int p = rnk[i];
-                const int visits = (int)(d / n) + (p < (int)(d % n) ? 1 : 0);
-                const int f = freq[i];
-                freq[i] = f - min(visits, f - 1);
-            }
+            continue;
+        }
+        stable_desc_ranks(freq, n, sk, rnk);
+        const int64_t d = -diff;
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+            const int p = rnk[i];
+            const int visits = (int)(d / n) + (p < (int)(d % n) ? 1 : 0);
+            const int f = freq[i];
+            freq[i] = f - min(visits, f - 1);
         }
         __syncthreads();
-        if (iter == 63 && threadIdx.x == 0) raise_flag(err, LQ_EF_NOCONVERGE);
     }
     for (int i = threadIdx.x; i < LQ_L; i += blockDim.x) fo[i] = (uint16_t)(i < n ? freq[i] : 0);
 }
 
-// enc entry: f | cf << 11 | k0 << 21, k0 = max(0, 9 - floor(log2 f)): the
-// encoder emits k0 or k0+1 bits from a state in [L, 2L).
-// dec entry: si | nb << 10 | (base - L) << 14 for slot in [cf, cf+f):
+// enc entry: 2f | k0 << 12 | (L + cf - f) << 16, k0 = max(0, 9 - floor(log2 f)):
+// from a state x in [L, 2L) the encoder emits k = k0 + (x >> k0 >= 2f) bits and
+// moves to (x >> k) + L + cf - f.
+// dec entry: si | nb << 10 | base << 14 for slot in [cf, cf+f):
 //   x' = f + slot - cf; nb = bits the decoder reads; base = x' << nb.
 __global__ void __launch_bounds__(kTT) expand_tables_kernel(const int32_t *__restrict__ tab_nsym,
                                                              const uint16_t *__restrict__ tab_freq,
@@ -217,7 +279,7 @@ __global__ void __launch_bounds__(kTT) expand_tables_kernel(const int32_t *__res
                 const int fi = f[i];
                 const int g = 31 - __clz(fi > 0 ? fi : 1);
                 const int k0 = max(0, 9 - g);
-                e = (uint32_t)fi | ((uint32_t)cf[i] << 11) | ((uint32_t)k0 << 21);
+                e = (uint32_t)(2 * fi) | ((uint32_t)k0 << 12) | ((uint32_t)(LQ_L + cf[i] - fi) << 16);
             }
             enc[i] = e;
         }
@@ -228,8 +290,8 @@ __global__ void __launch_bounds__(kTT) expand_tables_kernel(const int32_t *__res
             for (int slot = c0; slot < c0 + fi && slot < LQ_L; ++slot) {
                 const uint32_t xp = (uint32_t)(fi + slot - c0);
                 const uint32_t nb = xp >= (uint32_t)LQ_L ? 0u : (uint32_t)(__clz(xp) - 21);
-                const uint32_t b = xp << nb;
-                dec[slot] = (uint32_t)si | (nb << 10) | ((b - LQ_L) << 14);
+                const uint32_t b = xp << nb;  // in [L, 2L)
+                dec[slot] = (uint32_t)si | (nb << 10) | (b << 14);
             }
         }
     }

@@ -293,3 +293,39 @@ def test_full_size_roundtrip_property(lq):
     assert torch.equal(out.view(torch.int32), want.view(torch.int32))
     bits_per_dim = (4 * cd.n_words() * 8) / (q.numel())
     assert 3.8 < bits_per_dim < 4.3
+
+
+@pytest.mark.parametrize("case", ["rare_tail", "two_big_many_ones", "flat", "gaussian_large"])
+def test_device_tables_match_oracle_rule(lq, case):
+    """lq_build_tables == the oracle's stable-tie normalisation, including many-pass fix-ups."""
+    _lib, codec = lq
+    rng = np.random.default_rng(5)
+    hist = np.zeros(1024, np.int64)
+    if case == "rare_tail":
+        hist[512] = 10 ** 6
+        hist[512 - 300:512 + 300:1] += 1
+    elif case == "two_big_many_ones":
+        hist[100] = 500
+        hist[101] = 400
+        hist[102:1015] = 1
+    elif case == "flat":
+        hist[200:260] = 13
+    else:
+        v = np.clip(np.round(rng.standard_normal(2_000_000) * 40), -500, 500).astype(np.int64) + 512
+        hist = np.bincount(v, minlength=1024).astype(np.int64)
+    h = torch.from_numpy(hist.astype(np.int32)).cuda()
+    lo = torch.empty(1, dtype=torch.int32, device="cuda")
+    ns = torch.empty(1, dtype=torch.int32, device="cuda")
+    fr = torch.empty(1, 1024, dtype=torch.int16, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    P = _lib.ptr
+    _lib.check(_lib.lib().lq_build_tables(P(h), 1, P(lo), P(ns), P(fr), P(err), _lib.stream_handle()), "tables")
+    nz = np.nonzero(hist)[0]
+    a, b = nz.min() - 2, nz.max() + 2
+    counts = np.zeros(b - a + 1, np.int64)
+    counts[:] = [hist[i] if 0 <= i < 1024 else 0 for i in range(a, b + 1)]
+    want = O.normalize_freqs_stable(counts)
+    assert int(err.item()) == 0
+    assert int(lo.item()) == a - 512 and int(ns.item()) == len(counts)
+    got = fr[0].cpu().numpy().view(np.uint16).astype(np.int32)[: len(counts)]
+    assert np.array_equal(got, want)

@@ -215,3 +215,14 @@ def test_compact_pack_unpack_bit_exact():
         assert np.array_equal(O.unpack_e8(g[f"gauss_b{b}_packed"], b), g[f"gauss_b{b}_unpacked"])
     out = O.unpack_e8_4bit_f16(g["gauss_b4_packed"], g["u4_scales"], g["u4_head"])
     assert np.array_equal(out.view(np.uint16), _bits16(g["u4_out"]))
+
+
+def test_normalisation_needing_many_passes():
+    """Many rare symbols: the reference's fix-up loop needs hundreds of passes (no early cap)."""
+    counts = np.array([10 ** 6] + [1] * 600 + [3, 5, 9], dtype=np.int64)
+    a = O.normalize_freqs_numpy(counts)
+    b = O.normalize_freqs_stable(counts)
+    assert a.sum() == O.L and np.array_equal(a, b)  # entries at 1 never move, so ties cannot matter
+    counts = np.array([500, 400] + [1] * 1000 + [0, 0], dtype=np.int64)
+    a = O.normalize_freqs_numpy(counts)
+    assert a.sum() == O.L and np.array_equal(a, O.normalize_freqs_stable(counts))
