@@ -210,6 +210,44 @@ int lq_unpack_e8(const uint8_t *packed, int64_t n, int bits, const float *scales
                  float *q_out, uint16_t *f16_out, void *stream);
 
 /* ------------------------------------------------------------------------
+ * Element-wise entry points of the reference's core modules.
+ *   lq_quantize_e8     quantize_e8 (core/e8_quantizer.py:90-110): n blocks of x
+ *                      (fp32) -> q = encode_e8(x / scale), xhat = q * scale
+ *   lq_e8_to_symbols   e8_to_symbols (core/entropy_coder.py:46-68): coset[n],
+ *                      sym[n][8] (coords 0..6, coord8_half)
+ *   lq_symbols_to_e8   symbols_to_e8 (core/entropy_coder.py:71-89)
+ *   lq_check_e8        validate_e8 (core/compact_storage.py:39-80) and, for
+ *                      bits > 0, check_representable (:235-249); each output
+ *                      may be NULL
+ *   lq_pack_bits / lq_unpack_bits
+ *                      pack_coset_bits / unpack_coset_bits
+ *                      (llm/compressed_kv_cache.py:46-63): bit i <-> byte i/8, bit i%8
+ *   lq_map_symbols     symbol values -> table indices, nearest alphabet entry
+ *                      and first index on ties (core/gpu_ans.py:115-119)
+ *   lq_rans_encode_streams / lq_rans_finish_streams
+ *                      rans_encode (core/gpu_ans.py:105-139) of independent
+ *                      streams: symbol indices, one thread per stream, into
+ *                      slots [slot_off[i], slot_off[i+1]) of at least
+ *                      ceil(10*n/32) words; then reference words
+ *                      (ceil(n_bits/32) + 1, the last one zero) at dst_off[i]
+ * ---------------------------------------------------------------------- */
+int lq_quantize_e8(const float *x, int64_t n, float scale, float *q_out, float *xhat, void *stream);
+int lq_e8_to_symbols(const float *q, int64_t n, int32_t *coset, int32_t *sym, void *stream);
+int lq_symbols_to_e8(const int32_t *coset, const int32_t *sym, int64_t n, float *q, void *stream);
+int lq_check_e8(const float *q, int64_t n, float atol, int bits, uint8_t *valid, uint8_t *coset, uint8_t *in_range,
+                void *stream);
+int lq_pack_bits(const uint8_t *in, int64_t n, uint8_t *out, void *stream);
+int lq_unpack_bits(const uint8_t *in, int64_t n, uint8_t *out, void *stream);
+int lq_map_symbols(const int64_t *sym, int64_t n, const int64_t *alphabet, int32_t n_alpha, int contiguous,
+                   int32_t *out, void *stream);
+int lq_rans_encode_streams(const int32_t *sym_idx, const int64_t *sym_off, const int64_t *n_sym,
+                           const int32_t *table_id, const int32_t *tab_nsym, const uint32_t *enc_tab,
+                           int64_t n_streams, const int64_t *slot_off, uint32_t *slots, int64_t *nbits,
+                           uint32_t *state, uint32_t *err, void *stream);
+int lq_rans_finish_streams(const uint32_t *slots, const int64_t *slot_off, const int64_t *nbits, int64_t n_streams,
+                           const int64_t *dst_off, uint32_t *dst, void *stream);
+
+/* ------------------------------------------------------------------------
  * Diagnostics for tests: run one internal device helper over arrays.
  *   LQ_SELFTEST_DIV      out[i] = a[i] / b[i] (fp32) through the quantiser's
  *                        division (reciprocal + FMA correction); must equal IEEE

@@ -63,6 +63,15 @@ def _declare(lib):
         "lq_unpack_e8": ([vp, i64, i32, vp, vp, vp, vp, vp], i32),
         "lq_head_scales_static": ([vp, i32, i64, i64, f32, vp, vp, vp, vp], i32),
         "lq_selftest": ([i32, vp, vp, i64, ctypes.c_uint32, vp, vp], i32),
+        "lq_quantize_e8": ([vp, i64, f32, vp, vp, vp], i32),
+        "lq_e8_to_symbols": ([vp, i64, vp, vp, vp], i32),
+        "lq_symbols_to_e8": ([vp, vp, i64, vp, vp], i32),
+        "lq_check_e8": ([vp, i64, f32, i32, vp, vp, vp, vp], i32),
+        "lq_pack_bits": ([vp, i64, vp, vp], i32),
+        "lq_unpack_bits": ([vp, i64, vp, vp], i32),
+        "lq_map_symbols": ([vp, i64, vp, ctypes.c_int32, i32, vp, vp], i32),
+        "lq_rans_encode_streams": ([vp, vp, vp, vp, vp, vp, i64, vp, vp, vp, vp, vp, vp], i32),
+        "lq_rans_finish_streams": ([vp, vp, vp, i64, vp, vp, vp], i32),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)

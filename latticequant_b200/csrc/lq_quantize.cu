@@ -88,14 +88,6 @@ __global__ void __launch_bounds__(32 * kQWarps, 4) quantize_kernel(
                     qp[0] = make_float4(q[0], q[1], q[2], q[3]);
                     qp[1] = make_float4(q[4], q[5], q[6], q[7]);
                 }
-                // symbols must fit the histogram window (float->int saturates, so huge values land outside)
-                int lo = sym[0], hi = sym[0];
-#pragma unroll
-                for (int i = 1; i < 8; ++i) {
-                    lo = min(lo, sym[i]);
-                    hi = max(hi, sym[i]);
-                }
-                if (lo < -LQ_SYM_LIMIT || hi >= LQ_SYM_LIMIT) flags |= LQ_EF_SYMRANGE;
             }
             const uint32_t ball = __ballot_sync(0xffffffffu, active && coset);
             const uint32_t act = __ballot_sync(0xffffffffu, active);
@@ -113,11 +105,14 @@ __global__ void __launch_bounds__(32 * kQWarps, 4) quantize_kernel(
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
                     const int v = sym[i];
-                    if (v >= -kSmemHalf && v < kSmemHalf) {
+                    if ((uint32_t)(v + kSmemHalf) < (uint32_t)kSmemBins) {
                         atomicAdd(&sh[i * kSmemBins + v], 1u);
-                    } else if (v >= -LQ_SYM_LIMIT && v < LQ_SYM_LIMIT) {
+                    } else if ((uint32_t)(v + LQ_SYM_LIMIT) < (uint32_t)(2 * LQ_SYM_LIMIT)) {
                         uint32_t *gh = hist + ((int64_t)chunk * LQ_NSTREAMS + coset * 8 + i) * LQ_HIST_BINS;
                         atomicAdd(&gh[v + LQ_SYM_LIMIT], 1u);
+                    } else {
+                        // outside the histogram window (float->int saturates, so huge values land here)
+                        flags |= LQ_EF_SYMRANGE;
                     }
                 }
             }

@@ -411,7 +411,7 @@ __host__ __device__ inline size_t fused_smem_bytes(int nwarps, uint32_t TB) {
 }
 
 template <int DO>
-__global__ void __launch_bounds__(512) decode_fused_kernel(
+__global__ void __launch_bounds__(768) decode_fused_kernel(
     const uint32_t *__restrict__ words, uint32_t n_words, const uint32_t *__restrict__ lane_off,
     const uint32_t *__restrict__ lane_nbits, const uint32_t *__restrict__ lane_state,
     const uint32_t *__restrict__ coset_words, const uint32_t *__restrict__ tile_n0, uint32_t n_heads, uint32_t bph,
@@ -735,7 +735,7 @@ extern "C" int lq_rans_decode(const uint32_t *words, int64_t n_words, const uint
     const int64_t n_tiles = ceil_div(N, tile_blocks);
     const int64_t n_lanes = n_chunks * n_tiles * LQ_NSTREAMS;
     // fused path: tables + per-warp rank lists + rings fit in shared memory
-    int nwarps = 16;
+    int nwarps = 24;  // one CTA per SM; as many warps as shared memory allows
     while (nwarps >= 4 && fused_smem_bytes(nwarps, (uint32_t)tile_blocks) > 227 * 1024) nwarps -= 1;
     if (nwarps >= 4 && n_chunks <= 65535 && n_lanes < ((int64_t)1 << 32)) {
         const size_t sm = fused_smem_bytes(nwarps, (uint32_t)tile_blocks);

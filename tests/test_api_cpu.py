@@ -1,0 +1,105 @@
+"""Host-side logic of the reference-facing API and the C ABI surface (no GPU).
+
+The library is loaded and its exports are checked against the header; no
+compute entry point is called here.
+"""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+from conftest import ROOT, golden
+
+LIB = os.path.join(ROOT, "latticequant_b200", "liblq_b200.so")
+HDR = os.path.join(ROOT, "include", "latticequant_b200.h")
+
+
+def _declared():
+    text = open(HDR).read()
+    return sorted(set(re.findall(r"^\s*(?:int|size_t|const char \*)\s*\*?\s*(lq_\w+)\s*\(", text, re.M)))
+
+
+@pytest.fixture(scope="module")
+def cabi():
+    if not os.path.exists(LIB):
+        from latticequant_b200 import _build
+
+        _build.build()
+    return ctypes.CDLL(LIB)
+
+
+def test_library_exports_every_declared_symbol(cabi):
+    names = _declared()
+    assert len(names) >= 20
+    for n in names:
+        assert hasattr(cabi, n), n
+
+
+def test_host_only_entry_points(cabi):
+    cabi.lq_version.restype = ctypes.c_int
+    cabi.lq_strerror.restype = ctypes.c_char_p
+    cabi.lq_strerror.argtypes = [ctypes.c_int]
+    assert cabi.lq_version() >= 100
+    for code in (0, -1, -2, -3, -4, -5):
+        assert cabi.lq_strerror(code)
+    cabi.lq_rans_encode_workspace.restype = ctypes.c_size_t
+    cabi.lq_rans_encode_workspace.argtypes = [ctypes.c_int64] * 3
+    cabi.lq_head_scales_workspace.restype = ctypes.c_size_t
+    cabi.lq_head_scales_workspace.argtypes = [ctypes.c_int64] * 2
+    assert cabi.lq_rans_encode_workspace(64, 8 * 131072, 1024) > 0
+    assert cabi.lq_head_scales_workspace(16, 128) == 0          # small heads fold in one pass
+    assert cabi.lq_head_scales_workspace(16, 1 << 20) > 0
+
+
+def test_build_rans_table_matches_reference_fixtures():
+    from latticequant_b200.core.gpu_ans import L, build_rans_table
+
+    g = golden("rans.npz")
+    for i in range(int(g["n_cases"])):
+        t = build_rans_table(g[f"c{i}_counts"], list(g[f"c{i}_alphabet"]))
+        assert np.array_equal(t.freqs, g[f"c{i}_freqs"]), i
+        assert np.array_equal(t.cumfreqs, g[f"c{i}_cumfreqs"]), i
+        assert np.array_equal(t.lookup, g[f"c{i}_lookup"]), i
+        assert t.cumfreqs[-1] == L
+
+
+def test_build_rans_table_rejects_alphabet_over_L():
+    from latticequant_b200.core.gpu_ans import build_rans_table
+
+    with pytest.raises(ValueError):
+        build_rans_table(np.ones(1025, np.int64), list(range(1025)))
+
+
+def test_host_formulas_match_reference():
+    from latticequant_b200.core import compact_storage as cs
+    from latticequant_b200.core import e8_quantizer as e8
+
+    assert e8.G_E8 == 0.0717
+    for b in (3, 4, 5):
+        assert e8.compute_scale(1.0, b) == np.sqrt(2 * np.pi * np.e * 4.0 ** (-b))
+        assert cs.representable_range(b) == (-(2 ** (b - 1)), 2 ** (b - 1) - 1)
+
+
+def test_compact_tensor_accounting():
+    import torch
+
+    from latticequant_b200.core.compact_storage import CompactE8Tensor
+
+    ct = CompactE8Tensor(packed=torch.zeros(1000, 4, dtype=torch.uint8), scales=torch.zeros(3, dtype=torch.float32),
+                         bits_per_dim=4, orig_shape=(1, 3, 1000, 8), group_size=1000, num_vectors=1000)
+    assert ct.total_bytes == 4000 + 12
+    assert ct.fp16_bytes == 16000
+    assert abs(ct.effective_bits_per_dim - (4012 * 8) / 8000) < 1e-12
+    assert "CompactE8Tensor" in ct.summary()
+
+
+def test_geometry_and_capacity():
+    from latticequant_b200 import codec
+
+    g = codec.Geometry(3, 8, 8192 * 16, 1024)
+    assert g.n_tiles == 1024 and g.n_lanes == 3 * 1024 * 16
+    assert g.words_capacity >= 3 * (8 * g.n_vectors * 10) // 32
+    assert codec.round_tile(None, 1000) == 1024 and codec.round_tile(33, 1) == 64
+    assert codec.vol_mult(4) == 4.0 ** -4
