@@ -184,6 +184,47 @@ int lq_rans_decode(const uint32_t *words, int64_t n_words, const uint32_t *lane_
                    size_t workspace_bytes, uint32_t *err, void *stream);
 
 /* ------------------------------------------------------------------------
+ * Fused dequant + decode attention over one compressed K chunk and one V
+ * chunk of the same geometry (a (B, Hkv, S, D) cache tensor each, as
+ * CompressedKVCache._compress_tensor stores them,
+ * llm/compressed_kv_cache.py:176-287).  Replaces _decompress_chunk (:289-332)
+ * + the concatenated bf16 buffer update() returns (:385-395) + transformers'
+ * SDPA with repeat_kv: for every batch b and query head h,
+ *   o[b][h] = softmax(q[b][h] . K[b][h/G]^T * sm_scale) V[b][h/G]
+ * with K, V = symbols_to_e8 * fp16 head scale, never materialised.
+ *   q          [B][Hkv*group][head_dim] in q_dtype (16-byte aligned)
+ *   out        [B][Hkv*group][head_dim] in out_dtype
+ *   lse        optional [B][Hkv*group] fp32 ln(sum_t exp(s_t)), the form
+ *              lq_attn_merge combines across key sets (sequence shards)
+ *   workspace  lq_attn_decode_workspace() bytes (per-CTA partials)
+ * Needs head_dim 64 or 128, group 1..8, tile_blocks dividing bph.
+ * ---------------------------------------------------------------------- */
+typedef struct lq_chunk_view {
+    const uint32_t *words;
+    int64_t n_words;
+    const uint32_t *lane_off, *lane_nbits, *lane_state;
+    const uint32_t *coset_words, *tile_n0;
+    const int32_t *tab_lo, *tab_nsym;
+    const uint16_t *tab_freq;
+    const uint32_t *dec_tab;
+    const uint16_t *scale_f16;
+    int64_t n_heads, bph, tile_blocks;
+} lq_chunk_view;
+
+size_t lq_attn_decode_workspace(int64_t n_heads, int64_t bph, int64_t tile_blocks, int group, int head_dim);
+int lq_attn_decode(const lq_chunk_view *k, const lq_chunk_view *v, const void *q, int q_dtype, int64_t n_kv_heads,
+                   int group, int head_dim, float sm_scale, void *out, int out_dtype, float *lse, void *workspace,
+                   size_t workspace_bytes, uint32_t *err, void *stream);
+
+/* Merge attention parts over disjoint key sets (the all-gathered sequence
+ * shards, or several chunks of one layer): o = sum_i o_i exp(lse_i - lse),
+ * lse = ln sum_i exp(lse_i).
+ *   o_parts [n_parts][rows][head_dim] fp32, lse_parts [n_parts][rows] fp32
+ *   out     [rows][head_dim] in out_dtype; lse optional [rows] */
+int lq_attn_merge(const float *o_parts, const float *lse_parts, int64_t n_parts, int64_t rows, int head_dim,
+                  void *out, int out_dtype, float *lse, void *stream);
+
+/* ------------------------------------------------------------------------
  * Reference-stream decode: the argument meaning of _rans_decode_kernel
  * (core/gpu_ans.py:175-235) as prepared by prepare_gpu_decode (:274-342):
  * bit offsets, n_bits, initial states, symbol counts, per-table lookup /

@@ -42,6 +42,17 @@ class LatticeQuantError(RuntimeError):
     """Raised for device-side data errors reported through the error word."""
 
 
+class ChunkView(ctypes.Structure):
+    """struct lq_chunk_view: device pointers + geometry of one compressed chunk."""
+
+    _fields_ = [("words", ctypes.c_void_p), ("n_words", ctypes.c_int64),
+                ("lane_off", ctypes.c_void_p), ("lane_nbits", ctypes.c_void_p), ("lane_state", ctypes.c_void_p),
+                ("coset_words", ctypes.c_void_p), ("tile_n0", ctypes.c_void_p),
+                ("tab_lo", ctypes.c_void_p), ("tab_nsym", ctypes.c_void_p), ("tab_freq", ctypes.c_void_p),
+                ("dec_tab", ctypes.c_void_p), ("scale_f16", ctypes.c_void_p),
+                ("n_heads", ctypes.c_int64), ("bph", ctypes.c_int64), ("tile_blocks", ctypes.c_int64)]
+
+
 def _declare(lib):
     vp, i64, i32, f32, sz = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_size_t
     sig = {
@@ -63,6 +74,10 @@ def _declare(lib):
         "lq_unpack_e8": ([vp, i64, i32, vp, vp, vp, vp, vp], i32),
         "lq_head_scales_static": ([vp, i32, i64, i64, f32, vp, vp, vp, vp], i32),
         "lq_selftest": ([i32, vp, vp, i64, ctypes.c_uint32, vp, vp], i32),
+        "lq_attn_decode_workspace": ([i64, i64, i64, i32, i32], sz),
+        "lq_attn_decode": ([ctypes.POINTER(ChunkView), ctypes.POINTER(ChunkView), vp, i32, i64, i32, i32, f32, vp,
+                            i32, vp, vp, sz, vp, vp], i32),
+        "lq_attn_merge": ([vp, vp, i64, i64, i32, vp, i32, vp, vp], i32),
         "lq_quantize_e8": ([vp, i64, f32, vp, vp, vp], i32),
         "lq_e8_to_symbols": ([vp, i64, vp, vp, vp], i32),
         "lq_symbols_to_e8": ([vp, vp, i64, vp, vp], i32),

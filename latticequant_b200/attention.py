@@ -1,0 +1,136 @@
+"""Fused dequant + decode attention over compressed K/V chunks (CUDA, sm_100a).
+
+The reference serves decode attention from the dequantised buffer that
+CompressedKVCache.update() returns (llm/compressed_kv_cache.py:342-395),
+which transformers' SDPA reads after repeat_kv.  ``decode_attention`` reads
+the compressed K and V chunks instead: lq_attn_decode rebuilds every E8
+block in registers (symbols_to_e8, core/entropy_coder.py:71-89, times the
+fp16 head scale, llm/compressed_kv_cache.py:330) and folds it into the
+softmax of the query heads that share its KV head.  ``merge_attention``
+combines results over disjoint key sets (the chunks of one layer, or the
+sequence shards of several GPUs) from their log-sum-exp.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from typing import Optional, Sequence, Tuple
+
+import torch
+
+from . import _lib
+from ._lib import ChunkView, check, lib, ptr, raise_flags, stream_handle
+from .codec import LaneChunk, expand_dec_tables
+
+
+def chunk_view(chunk: LaneChunk) -> ChunkView:
+    """The C view (struct lq_chunk_view) of a single-chunk LaneChunk."""
+    g = chunk.geom
+    if g.n_chunks != 1:
+        raise ValueError("attention reads one chunk per K/V tensor")
+    dec = expand_dec_tables(chunk)
+    v = ChunkView()
+    v.words = chunk.words.data_ptr()
+    v.n_words = chunk.n_words
+    v.lane_off = chunk.lane_off.data_ptr()
+    v.lane_nbits = chunk.lane_nbits.data_ptr()
+    v.lane_state = chunk.lane_state.data_ptr()
+    v.coset_words = chunk.coset_words.data_ptr()
+    v.tile_n0 = chunk.tile_n0.data_ptr()
+    v.tab_lo = chunk.tab_lo.data_ptr()
+    v.tab_nsym = chunk.tab_nsym.data_ptr()
+    v.tab_freq = chunk.tab_freq.data_ptr()
+    v.dec_tab = dec.data_ptr()
+    v.scale_f16 = chunk.scale_f16.data_ptr()
+    v.n_heads = g.n_heads
+    v.bph = g.bph
+    v.tile_blocks = g.tile_blocks
+    return v
+
+
+def attention_workspace_bytes(k_chunk: LaneChunk, group: int) -> int:
+    g = k_chunk.geom
+    d = k_chunk.orig_shape[-1]
+    return int(lib().lq_attn_decode_workspace(g.n_heads, g.bph, g.tile_blocks, group, d))
+
+
+def supports(k_chunk: LaneChunk, group: int) -> bool:
+    """Whether the fused kernel takes this chunk geometry (head_dim 64/128,
+    group 1..8, tiles that do not straddle heads)."""
+    return attention_workspace_bytes(k_chunk, group) > 0
+
+
+def decode_attention(q: torch.Tensor, k_chunk: LaneChunk, v_chunk: LaneChunk, sm_scale: Optional[float] = None,
+                     out_dtype: Optional[torch.dtype] = None, return_lse: bool = False,
+                     out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None,
+                     workspace: Optional[torch.Tensor] = None):
+    """softmax(q K^T * sm_scale) V for one decode step, K/V read compressed.
+
+    q: (B, Hq, D) or (B, Hq, 1, D) on the device; K/V chunks of a (B, Hkv, S, D)
+    tensor each with Hq a multiple of Hkv (GQA as repeat_kv).  Returns o with
+    q's shape (and the fp32 (B, Hq) log-sum-exp of the scores if return_lse).
+    """
+    _lib.require_cuda(q)
+    kshape, vshape = tuple(k_chunk.orig_shape), tuple(v_chunk.orig_shape)
+    if len(kshape) != 4 or kshape != vshape:
+        raise ValueError("K and V chunks must hold (B, Hkv, S, D) tensors of one shape")
+    B, Hkv, S, D = kshape
+    qshape = tuple(q.shape)
+    if q.dim() == 4:
+        if q.shape[2] != 1:
+            raise ValueError("decode attention takes one query position")
+        q3 = q.reshape(q.shape[0], q.shape[1], q.shape[3])
+    elif q.dim() == 3:
+        q3 = q
+    else:
+        raise ValueError("q must be (B, Hq, D) or (B, Hq, 1, D)")
+    if q3.shape[0] != B or q3.shape[2] != D or q3.shape[1] % Hkv != 0:
+        raise ValueError(f"q {qshape} does not match K/V {kshape}")
+    group = q3.shape[1] // Hkv
+    q3 = q3.contiguous()
+    od = out_dtype or q.dtype
+    dev = q.device
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    kv, vv = chunk_view(k_chunk), chunk_view(v_chunk)
+    ws_need = attention_workspace_bytes(k_chunk, group)
+    if ws_need == 0:
+        raise ValueError(f"fused attention does not take head_dim={D}, group={group}, "
+                         f"tile_blocks={k_chunk.geom.tile_blocks} with {k_chunk.geom.bph} blocks per head")
+    if workspace is None or workspace.numel() < ws_need:
+        workspace = torch.empty(ws_need, dtype=torch.uint8, device=dev)
+    if out is None:
+        out = torch.empty(q3.shape, dtype=od, device=dev)
+    if return_lse and lse is None:
+        lse = torch.empty(q3.shape[:2], dtype=torch.float32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    check(lib().lq_attn_decode(ctypes.byref(kv), ctypes.byref(vv), ptr(q3), _lib.dtype_code(q3.dtype), Hkv, group,
+                               D, float(sm_scale), ptr(out), _lib.dtype_code(out.dtype),
+                               ptr(lse) if return_lse else None, ptr(workspace), workspace.numel(), ptr(err),
+                               stream_handle(dev)), "lq_attn_decode")
+    raise_flags(int(err.item()) & 0xFFFFFFFF, "decode_attention")
+    o = out.view(qshape[:-1] + (D,)) if q.dim() == 4 else out
+    return (o, lse) if return_lse else o
+
+
+def merge_attention(o_parts: Sequence[torch.Tensor] | torch.Tensor, lse_parts: Sequence[torch.Tensor] | torch.Tensor,
+                    out_dtype: Optional[torch.dtype] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Combine attention over disjoint key sets: o = sum_i o_i exp(lse_i - lse).
+
+    o_parts: n tensors (or one stacked tensor) of shape (..., D); lse_parts the
+    matching (...) log-sum-exps.  Returns (o, lse)."""
+    o = torch.stack(list(o_parts)) if not torch.is_tensor(o_parts) else o_parts
+    ls = torch.stack(list(lse_parts)) if not torch.is_tensor(lse_parts) else lse_parts
+    _lib.require_cuda(o)
+    n, D = o.shape[0], o.shape[-1]
+    rows = o[0].numel() // D
+    if ls.numel() != n * rows:
+        raise ValueError("lse parts do not match the o parts")
+    of = o.reshape(n, rows, D).to(torch.float32).contiguous()
+    lf = ls.reshape(n, rows).to(torch.float32).contiguous()
+    od = out_dtype or o.dtype
+    out = torch.empty((rows, D), dtype=od, device=o.device)
+    lse = torch.empty(rows, dtype=torch.float32, device=o.device)
+    check(lib().lq_attn_merge(ptr(of), ptr(lf), n, rows, D, ptr(out), _lib.dtype_code(od), ptr(lse),
+                              stream_handle(o.device)), "lq_attn_merge")
+    return out.view(o.shape[1:]), lse.view(ls.shape[1:])

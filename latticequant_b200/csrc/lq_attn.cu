@@ -1,0 +1,458 @@
+// lq_attn.cu -- fused dequant + decode attention over compressed K/V chunks.
+//
+// The reference serves attention from a decompressed bf16 buffer: update()
+// (llm/compressed_kv_cache.py:342-395) returns the dequantised K/V and
+// transformers runs SDPA over it with repeat_kv; its fused analogue
+// (llm/fused_triton_merge.py) only merges the compact 4-bit layout into that
+// buffer.  Here one kernel streams the entropy-coded K and V tiles straight
+// from HBM, rebuilds each E8 block in registers (symbols_to_e8,
+// core/entropy_coder.py:71-89, times the fp16 head scale of
+// llm/compressed_kv_cache.py:330) and folds it into the attention of the
+// GQA query group that reads that KV head, so no dequantised tensor exists.
+//
+// Work split: a CTA owns a range of tile pairs of one (batch, kv-head) head;
+// a warp owns one tile pair (tokens of two consecutive tiles).
+//   phase K  the chunk's K tables in shared memory; the warp decodes its K
+//            tiles in position order (lq_tiledec.cuh) and each lane, which
+//            always holds the same 8 channels of a token, multiplies them
+//            with the same 8 channels of the G query heads; a butterfly over
+//            the token's lanes gives the G scores of the token (shared memory)
+//   softmax  per warp: m = max score, p = 2^(s - m), l = sum p (base 2)
+//   phase V  V tables replace the K tables; the warp decodes its V tiles
+//            and each lane accumulates p * v for its 8 channels in registers
+//   merge    warps merge (m, l, o) in a fixed order -> one partial per CTA;
+//            a second kernel merges a head's partials into o and lse.
+// Every sum runs in a fixed order, so results are deterministic.
+#include <algorithm>
+
+#include "lq_tiledec.cuh"
+
+namespace lq {
+namespace {
+
+constexpr int kAttnRing = 48;  // ring rows: rounds take 3-6 token groups of 16 blocks
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+struct AttnArgs {
+    ChunkDev k, v;
+    const void *q;        // [B][Hkv*G][D] in q dtype
+    uint32_t n_kv_heads;  // heads of the chunk = B * n_kv_heads
+    uint32_t tph;         // tiles per head
+    uint32_t n_pairs;     // tile pairs per head
+    uint32_t nct;         // CTAs per head
+    uint32_t tpt;         // tokens per tile
+    uint32_t region0;     // bytes of the table / merge region
+    uint32_t warp_bytes;  // bytes of per-warp shared memory
+    float qk_log2;        // sm_scale * log2(e)
+    float *part;          // [heads][nct][G][D + 2]: o (unnormalised), m, l
+    uint32_t *err;
+};
+
+template <int G>
+__host__ __device__ constexpr int padded_g() {
+    return (G + 3) & ~3;
+}
+
+template <int G, int BPT>
+__host__ __device__ constexpr int attn_threads() {
+    return G <= 4 ? 768 : 512;
+}
+
+// Fused attention partials.  BPT = blocks per token = head_dim / 8.
+template <int G, int BPT, int QDT>
+__global__ void __launch_bounds__(attn_threads<G, BPT>()) attn_partial_kernel(AttnArgs a) {
+    static_assert(BPT == 8 || BPT == 16, "head_dim 64 or 128");
+    static_assert(G >= 1 && G <= 8, "query group 1..8");
+    constexpr int D = 8 * BPT, GP = padded_g<G>(), TPG = 16 / BPT;
+    extern __shared__ __align__(16) unsigned char smem[];
+    uint32_t *dtab = reinterpret_cast<uint32_t *>(smem);
+    const int warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const uint32_t lane = threadIdx.x & 31, dc = lane % BPT;
+    unsigned char *wb = smem + a.region0 + (size_t)warp * a.warp_bytes;
+    int16_t *ring = reinterpret_cast<int16_t *>(wb);
+    float *sc = reinterpret_cast<float *>(wb + kAttnRing * kRingStride * 2);
+
+    const uint32_t head = blockIdx.y;
+    const uint32_t pb = (uint32_t)(((uint64_t)blockIdx.x * a.n_pairs) / a.nct);
+    const uint32_t pe = (uint32_t)(((uint64_t)(blockIdx.x + 1) * a.n_pairs) / a.nct);
+    const uint32_t pair = pb + (uint32_t)warp;
+    const bool wact = pair < pe;
+    const bool act0 = wact, act1 = wact && 2 * pair + 1 < a.tph;
+    const uint32_t tile0 = head * a.tph + 2 * pair;
+
+    // query channels 8*dc .. 8*dc+7 of the G heads reading this kv head
+    const uint32_t b = head / a.n_kv_heads, kvh = head % a.n_kv_heads;
+    float qr[G][8];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const int64_t row = (int64_t)b * a.n_kv_heads * G + (int64_t)kvh * G + g;
+        load_block8<QDT>(a.q, row * BPT + dc, qr[g]);
+    }
+
+    // ---- phase K: scores
+    stage_tables(a.k, 0, dtab);
+    __syncthreads();
+    if (wact) {
+        decode_two_tiles_ordered<kAttnRing>(
+            a.k, 0, tile0, act0, act1, dtab, ring,
+            [&](bool ok, int t, uint32_t grp, uint32_t j, uint32_t cc, const int *sym) {
+                float kq[8];
+                e8_from_symbols((int)cc, sym, kq);
+                float dot[G];
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    float s = 0.f;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) s = fmaf(qr[g][i], kq[i], s);
+                    dot[g] = ok ? s : 0.f;
+                }
+#pragma unroll
+                for (int off = BPT / 2; off >= 1; off >>= 1) {
+#pragma unroll
+                    for (int g = 0; g < G; ++g) dot[g] += __shfl_xor_sync(0xffffffffu, dot[g], off);
+                }
+                const uint32_t jc = j % BPT;
+                if (ok && jc < (uint32_t)G) {
+                    float v = dot[0];
+#pragma unroll
+                    for (int g = 1; g < G; ++g) v = (jc == (uint32_t)g) ? dot[g] : v;
+                    const uint32_t tok = grp * TPG + j / BPT;
+                    sc[((uint32_t)t * a.tpt + tok) * GP + jc] = v;
+                }
+            },
+            a.err);
+    }
+    __syncwarp();
+
+    // ---- softmax statistics of this warp's tokens (base 2)
+    const float ck = __half2float(__ushort_as_half(a.k.scale_f16[head])) * a.qk_log2;
+    const uint32_t ntok = 2 * a.tpt;
+    float m[G], l[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        m[g] = -INFINITY;
+        l[g] = 0.f;
+    }
+    for (uint32_t i = lane; i < ntok; i += 32) {
+        const bool v = i < a.tpt ? act0 : act1;
+        if (!v) continue;
+#pragma unroll
+        for (int g = 0; g < G; ++g) m[g] = fmaxf(m[g], sc[i * GP + g] * ck);
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) m[g] = fmaxf(m[g], __shfl_xor_sync(0xffffffffu, m[g], off));
+    }
+    for (uint32_t i = lane; i < ntok; i += 32) {
+        const bool v = i < a.tpt ? act0 : act1;
+        if (!v) continue;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float p = exp2f(sc[i * GP + g] * ck - m[g]);
+            sc[i * GP + g] = p;
+            l[g] += p;
+        }
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) l[g] += __shfl_xor_sync(0xffffffffu, l[g], off);
+    }
+    __syncwarp();
+
+    // ---- phase V: p * v accumulated per lane over its 8 channels
+    __syncthreads();  // every warp is done with the K tables
+    stage_tables(a.v, 0, dtab);
+    __syncthreads();
+    float acc[G][8];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[g][i] = 0.f;
+    if (wact) {
+        decode_two_tiles_ordered<kAttnRing>(
+            a.v, 0, tile0, act0, act1, dtab, ring,
+            [&](bool ok, int t, uint32_t grp, uint32_t j, uint32_t cc, const int *sym) {
+                if (!ok) return;
+                float vq[8];
+                e8_from_symbols((int)cc, sym, vq);
+                const uint32_t tok = grp * TPG + j / BPT;
+                const float *pp = sc + ((uint32_t)t * a.tpt + tok) * GP;
+                float p[GP];
+#pragma unroll
+                for (int g4 = 0; g4 < GP; g4 += 4) {
+                    const float4 f = *reinterpret_cast<const float4 *>(pp + g4);
+                    p[g4] = f.x;
+                    p[g4 + 1] = f.y;
+                    p[g4 + 2] = f.z;
+                    p[g4 + 3] = f.w;
+                }
+#pragma unroll
+                for (int g = 0; g < G; ++g)
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) acc[g][i] = fmaf(p[g], vq[i], acc[g][i]);
+            },
+            a.err);
+    }
+    // lanes holding the same channels: the two tiles (xor 16), two tokens per group for BPT 8 (xor 8)
+#pragma unroll
+    for (int off = 16; off >= BPT; off >>= 1) {
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[g][i] += __shfl_xor_sync(0xffffffffu, acc[g][i], off);
+    }
+
+    // ---- merge the warps in a fixed order
+    __syncthreads();  // every warp is done with the V tables: the region holds the merge buffer
+    float *mrg = reinterpret_cast<float *>(smem);
+    const int rs = D + 2;
+    if (lane < (uint32_t)BPT) {
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) mrg[(warp * G + g) * rs + 8 * (int)lane + i] = acc[g][i];
+    }
+    if (lane == 0) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            mrg[(warp * G + g) * rs + D] = m[g];
+            mrg[(warp * G + g) * rs + D + 1] = l[g];
+        }
+    }
+    __syncthreads();
+    const float cv = __half2float(__ushort_as_half(a.v.scale_f16[head]));
+    float *out = a.part + ((size_t)head * a.nct + blockIdx.x) * G * rs;
+    for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
+        const int g = e / D, dd = e % D;
+        float mx = -INFINITY;
+        for (int w = 0; w < nwarps; ++w) mx = fmaxf(mx, mrg[(w * G + g) * rs + D]);
+        float o = 0.f, ls = 0.f;
+        for (int w = 0; w < nwarps; ++w) {
+            const float mw = mrg[(w * G + g) * rs + D];
+            if (mw == -INFINITY) continue;
+            const float f = exp2f(mw - mx);
+            o = fmaf(mrg[(w * G + g) * rs + dd], f, o);
+            ls = fmaf(mrg[(w * G + g) * rs + D + 1], f, ls);
+        }
+        out[g * rs + dd] = o * cv;
+        if (dd == 0) {
+            out[g * rs + D] = mx;
+            out[g * rs + D + 1] = ls;
+        }
+    }
+}
+
+// One block per query row: merge the head's CTA partials into o = O / L and
+// lse = ln(sum exp(s)) (natural log of the unnormalised softmax mass).
+template <int ODT>
+__global__ void attn_combine_kernel(const float *__restrict__ part, uint32_t n_kv_heads, uint32_t G, uint32_t D,
+                                    uint32_t nct, void *__restrict__ out, float *__restrict__ lse) {
+    const uint32_t row = blockIdx.x;  // head * G + g
+    const uint32_t head = row / G, g = row % G;
+    const uint32_t b = head / n_kv_heads, kvh = head % n_kv_heads;
+    const uint32_t orow = (b * n_kv_heads + kvh) * G + g;  // (b, q-head) with q-head = kvh * G + g
+    const size_t rs = D + 2;
+    const float *p = part + (size_t)head * nct * G * rs + (size_t)g * rs;
+    float mx = -INFINITY;
+    for (uint32_t c = 0; c < nct; ++c) mx = fmaxf(mx, p[(size_t)c * G * rs + D]);
+    float ls = 0.f;
+    for (uint32_t c = 0; c < nct; ++c) {
+        const float mc = p[(size_t)c * G * rs + D];
+        if (mc != -INFINITY) ls = fmaf(p[(size_t)c * G * rs + D + 1], exp2f(mc - mx), ls);
+    }
+    const float inv = 1.f / ls;
+    for (uint32_t d = threadIdx.x; d < D; d += blockDim.x) {
+        float o = 0.f;
+        for (uint32_t c = 0; c < nct; ++c) {
+            const float mc = p[(size_t)c * G * rs + D];
+            if (mc != -INFINITY) o = fmaf(p[(size_t)c * G * rs + d], exp2f(mc - mx), o);
+        }
+        Elem<ODT>::store(out, (int64_t)orow * D + d, o * inv);
+    }
+    if (lse && threadIdx.x == 0) lse[orow] = (mx + log2f(ls)) * kLn2;
+}
+
+// Merge of attention parts over disjoint key sets (sequence shards, chunks):
+// o = sum_i o_i exp(lse_i - lse), lse = log sum_i exp(lse_i).
+template <int ODT>
+__global__ void attn_merge_kernel(const float *__restrict__ o_parts, const float *__restrict__ lse_parts,
+                                  int64_t n_parts, int64_t rows, uint32_t D, void *__restrict__ out,
+                                  float *__restrict__ lse) {
+    const int64_t row = blockIdx.x;
+    float mx = -INFINITY;
+    for (int64_t i = 0; i < n_parts; ++i) mx = fmaxf(mx, lse_parts[i * rows + row]);
+    float ls = 0.f;
+    for (int64_t i = 0; i < n_parts; ++i) {
+        const float li = lse_parts[i * rows + row];
+        if (li != -INFINITY) ls += exp2f((li - mx) * kLog2e);
+    }
+    const float inv = 1.f / ls;
+    for (uint32_t d = threadIdx.x; d < D; d += blockDim.x) {
+        float o = 0.f;
+        for (int64_t i = 0; i < n_parts; ++i) {
+            const float li = lse_parts[i * rows + row];
+            if (li != -INFINITY) o = fmaf(o_parts[(i * rows + row) * D + d], exp2f((li - mx) * kLog2e), o);
+        }
+        Elem<ODT>::store(out, row * D + d, o * inv);
+    }
+    if (lse && threadIdx.x == 0) lse[row] = mx + log2f(ls) * kLn2;
+}
+
+struct AttnPlan {
+    int nwarps;
+    uint32_t nct, n_pairs, tph, tpt, region0, warp_bytes;
+    size_t smem, part_floats;
+};
+
+size_t attn_warp_bytes(int G, uint32_t tpt) {
+    return (size_t)kAttnRing * kRingStride * 2 + (size_t)2 * tpt * ((G + 3) & ~3) * 4;
+}
+
+int attn_plan(int64_t n_heads, int64_t bph, int64_t tile_blocks, int G, int D, AttnPlan *p) {
+    if (n_heads <= 0 || bph <= 0 || tile_blocks <= 0 || G < 1 || G > 8 || (D != 64 && D != 128)) return LQ_ERR_INVALID;
+    const int bpt = D / 8;
+    if (tile_blocks % 32 != 0 || bph % tile_blocks != 0 || bph % bpt != 0) return LQ_ERR_INVALID;
+    if (n_heads > 65535 || n_heads * bph >= ((int64_t)1 << 31)) return LQ_ERR_INVALID;
+    p->tph = (uint32_t)(bph / tile_blocks);
+    p->tpt = (uint32_t)(tile_blocks / bpt);
+    p->n_pairs = (p->tph + 1) / 2;
+    const size_t wb = attn_warp_bytes(G, p->tpt);
+    int nw = G <= 4 ? 24 : 16;
+    for (;; --nw) {
+        if (nw < 4) return LQ_ERR_INVALID;  // tiles too long for shared memory
+        const size_t r0 = (std::max<size_t>(kTablesSmem, (size_t)nw * G * (D + 2) * 4) + 127) & ~(size_t)127;
+        if (r0 + (size_t)nw * wb <= 227 * 1024) {
+            p->region0 = (uint32_t)r0;
+            break;
+        }
+    }
+    p->nwarps = nw;
+    p->warp_bytes = (uint32_t)wb;
+    p->smem = p->region0 + (size_t)nw * wb;
+    p->nct = (uint32_t)ceil_div(p->n_pairs, nw);
+    p->part_floats = (size_t)n_heads * p->nct * G * (D + 2);
+    return LQ_OK;
+}
+
+template <int G, int BPT, int QDT>
+int launch_partial(const AttnArgs &a, const AttnPlan &p, uint32_t n_heads, cudaStream_t st) {
+    auto kern = attn_partial_kernel<G, BPT, QDT>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem) != cudaSuccess)
+        return LQ_ERR_CUDA;
+    kern<<<dim3(p.nct, n_heads), 32 * p.nwarps, p.smem, st>>>(a);
+    return check_launch();
+}
+
+template <int G, int BPT>
+int launch_partial_q(const AttnArgs &a, const AttnPlan &p, uint32_t n_heads, int q_dtype, cudaStream_t st) {
+    switch (q_dtype) {
+        case LQ_F32: return launch_partial<G, BPT, LQ_F32>(a, p, n_heads, st);
+        case LQ_F16: return launch_partial<G, BPT, LQ_F16>(a, p, n_heads, st);
+        case LQ_BF16: return launch_partial<G, BPT, LQ_BF16>(a, p, n_heads, st);
+        default: return LQ_ERR_INVALID;
+    }
+}
+
+template <int G>
+int launch_partial_g(const AttnArgs &a, const AttnPlan &p, uint32_t n_heads, int q_dtype, int D, cudaStream_t st) {
+    return D == 128 ? launch_partial_q<G, 16>(a, p, n_heads, q_dtype, st)
+                    : launch_partial_q<G, 8>(a, p, n_heads, q_dtype, st);
+}
+
+bool view_ok(const lq_chunk_view *c) {
+    return c && c->lane_off && c->lane_nbits && c->lane_state && c->coset_words && c->tile_n0 && c->tab_lo &&
+           c->tab_nsym && c->tab_freq && c->dec_tab && c->scale_f16 && c->n_words >= 0 && (c->n_words == 0 || c->words);
+}
+
+ChunkDev to_dev(const lq_chunk_view *c) {
+    const int64_t N = c->n_heads * c->bph;
+    return ChunkDev{c->words,        (uint32_t)c->n_words, c->lane_off,          c->lane_nbits,
+                    c->lane_state,   c->coset_words,       c->tile_n0,           (uint32_t)c->n_heads,
+                    (uint32_t)c->bph, (uint32_t)c->tile_blocks, (uint32_t)ceil_div(N, c->tile_blocks), c->tab_lo,
+                    c->tab_nsym,     c->tab_freq,          c->dec_tab,           c->scale_f16};
+}
+
+}  // namespace
+}  // namespace lq
+
+using namespace lq;
+
+extern "C" size_t lq_attn_decode_workspace(int64_t n_heads, int64_t bph, int64_t tile_blocks, int group,
+                                           int head_dim) {
+    AttnPlan p;
+    if (attn_plan(n_heads, bph, tile_blocks, group, head_dim, &p) != LQ_OK) return 0;
+    return (p.part_floats * 4 + 255) & ~(size_t)255;
+}
+
+extern "C" int lq_attn_decode(const lq_chunk_view *k, const lq_chunk_view *v, const void *q, int q_dtype,
+                              int64_t n_kv_heads, int group, int head_dim, float sm_scale, void *out, int out_dtype,
+                              float *lse, void *workspace, size_t workspace_bytes, uint32_t *err, void *stream) {
+    if (!view_ok(k) || !view_ok(v) || !q || !out || !workspace || n_kv_heads <= 0) return LQ_ERR_INVALID;
+    if (k->n_heads != v->n_heads || k->bph != v->bph || k->tile_blocks != v->tile_blocks) return LQ_ERR_INVALID;
+    if (k->n_heads % n_kv_heads != 0) return LQ_ERR_INVALID;
+    if ((reinterpret_cast<uintptr_t>(q) & 15) || (reinterpret_cast<uintptr_t>(workspace) & 15)) return LQ_ERR_INVALID;
+    if (!(sm_scale > 0.f) || !isfinite(sm_scale)) return LQ_ERR_INVALID;
+    AttnPlan p;
+    const int rc = attn_plan(k->n_heads, k->bph, k->tile_blocks, group, head_dim, &p);
+    if (rc != LQ_OK) return rc;
+    if (workspace_bytes < p.part_floats * 4) return LQ_ERR_CAPACITY;
+    if (out_dtype != LQ_F32 && out_dtype != LQ_F16 && out_dtype != LQ_BF16) return LQ_ERR_INVALID;
+    cudaStream_t st = as_stream(stream);
+    AttnArgs a;
+    a.k = to_dev(k);
+    a.v = to_dev(v);
+    a.q = q;
+    a.n_kv_heads = (uint32_t)n_kv_heads;
+    a.tph = p.tph;
+    a.n_pairs = p.n_pairs;
+    a.nct = p.nct;
+    a.tpt = p.tpt;
+    a.region0 = p.region0;
+    a.warp_bytes = p.warp_bytes;
+    a.qk_log2 = sm_scale * kLog2e;
+    a.part = static_cast<float *>(workspace);
+    a.err = err;
+    const uint32_t nh = (uint32_t)k->n_heads;
+    int r;
+    switch (group) {
+        case 1: r = launch_partial_g<1>(a, p, nh, q_dtype, head_dim, st); break;
+        case 2: r = launch_partial_g<2>(a, p, nh, q_dtype, head_dim, st); break;
+        case 3: r = launch_partial_g<3>(a, p, nh, q_dtype, head_dim, st); break;
+        case 4: r = launch_partial_g<4>(a, p, nh, q_dtype, head_dim, st); break;
+        case 5: r = launch_partial_g<5>(a, p, nh, q_dtype, head_dim, st); break;
+        case 6: r = launch_partial_g<6>(a, p, nh, q_dtype, head_dim, st); break;
+        case 7: r = launch_partial_g<7>(a, p, nh, q_dtype, head_dim, st); break;
+        case 8: r = launch_partial_g<8>(a, p, nh, q_dtype, head_dim, st); break;
+        default: return LQ_ERR_INVALID;
+    }
+    if (r != LQ_OK) return r;
+    const unsigned rows = (unsigned)(k->n_heads * group);
+    const float *part = a.part;
+    const uint32_t hkv = (uint32_t)n_kv_heads, G = (uint32_t)group, D = (uint32_t)head_dim;
+    if (out_dtype == LQ_F32) attn_combine_kernel<LQ_F32><<<rows, D, 0, st>>>(part, hkv, G, D, p.nct, out, lse);
+    else if (out_dtype == LQ_F16) attn_combine_kernel<LQ_F16><<<rows, D, 0, st>>>(part, hkv, G, D, p.nct, out, lse);
+    else attn_combine_kernel<LQ_BF16><<<rows, D, 0, st>>>(part, hkv, G, D, p.nct, out, lse);
+    return check_launch();
+}
+
+extern "C" int lq_attn_merge(const float *o_parts, const float *lse_parts, int64_t n_parts, int64_t rows,
+                             int head_dim, void *out, int out_dtype, float *lse, void *stream) {
+    if (n_parts < 0 || rows < 0 || head_dim <= 0 || head_dim > 1024) return LQ_ERR_INVALID;
+    if (n_parts == 0 || rows == 0) return n_parts == 0 && rows > 0 ? LQ_ERR_INVALID : LQ_OK;
+    if (!o_parts || !lse_parts || !out || rows > 0x7fffffff) return LQ_ERR_INVALID;
+    cudaStream_t st = as_stream(stream);
+    const unsigned tb = head_dim < 128 ? (unsigned)head_dim : 128u;
+    if (out_dtype == LQ_F32)
+        attn_merge_kernel<LQ_F32><<<(unsigned)rows, tb, 0, st>>>(o_parts, lse_parts, n_parts, rows, head_dim, out, lse);
+    else if (out_dtype == LQ_F16)
+        attn_merge_kernel<LQ_F16><<<(unsigned)rows, tb, 0, st>>>(o_parts, lse_parts, n_parts, rows, head_dim, out, lse);
+    else if (out_dtype == LQ_BF16)
+        attn_merge_kernel<LQ_BF16><<<(unsigned)rows, tb, 0, st>>>(o_parts, lse_parts, n_parts, rows, head_dim, out,
+                                                                  lse);
+    else
+        return LQ_ERR_INVALID;
+    return check_launch();
+}

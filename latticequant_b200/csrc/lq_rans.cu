@@ -22,7 +22,7 @@
 // a state outside [L, 2L), the reference formula runs literally, including
 // its stop at n_bits, so truncated or odd streams decode exactly as the
 // reference decodes them.
-#include "lq_common.cuh"
+#include "lq_tiledec.cuh"
 
 namespace lq {
 namespace {
@@ -397,215 +397,45 @@ __global__ void __launch_bounds__(256) reconstruct_kernel(const int16_t *__restr
 }
 
 // ---------------------------------------------------------------- fused decode
-// One warp decodes two tiles (32 lanes).  Per round each lane decodes up to
-// kRing symbols of its lane into a shared ring; the warp then rebuilds the
-// blocks whose symbols just arrived (rank r of coset c in tile t -> block
-// position via a rank->position list built from the coset bits) and writes
-// them scaled by the fp16 head scale.  The chunk's 16 decode tables live in
-// shared memory.
-constexpr int kRing = 32;
-constexpr int kRingStride = 40;  // int16 per ring row: 80 B, keeps 8-symbol groups 16-B aligned and conflict-free
-
+// Decode + dequantise: lq_tiledec.cuh's tile decoder with an epilogue that
+// rebuilds the E8 point (symbols_to_e8) and writes it times the fp16 head
+// scale, 16 bytes per block for 16-bit outputs.
 __host__ __device__ inline size_t fused_smem_bytes(int nwarps, uint32_t TB) {
-    return (size_t)LQ_NSTREAMS * LQ_L * 4 + (size_t)nwarps * (2 * TB * 2 + kRing * kRingStride * 2);
+    return kTablesSmem + (size_t)nwarps * tiledec_warp_smem(TB);
 }
 
 template <int DO>
-__global__ void __launch_bounds__(768) decode_fused_kernel(
-    const uint32_t *__restrict__ words, uint32_t n_words, const uint32_t *__restrict__ lane_off,
-    const uint32_t *__restrict__ lane_nbits, const uint32_t *__restrict__ lane_state,
-    const uint32_t *__restrict__ coset_words, const uint32_t *__restrict__ tile_n0, uint32_t n_heads, uint32_t bph,
-    FastDiv bph_div, uint32_t TB, uint32_t n_tiles, const int32_t *__restrict__ tab_lo,
-    const int32_t *__restrict__ tab_nsym, const uint16_t *__restrict__ tab_freq, const uint32_t *__restrict__ dec_tab,
-    const uint16_t *__restrict__ scale_f16, void *__restrict__ out, int32_t *__restrict__ sym_out, uint32_t *err) {
+__global__ void __launch_bounds__(768) decode_fused_kernel(ChunkDev a, FastDiv bph_div, void *__restrict__ out,
+                                                          int32_t *__restrict__ sym_out, uint32_t *err) {
     extern __shared__ __align__(16) unsigned char smem[];
     uint32_t *dtab = reinterpret_cast<uint32_t *>(smem);
     const int nwarps = blockDim.x >> 5;
-    uint16_t *rows_all = reinterpret_cast<uint16_t *>(smem + (size_t)LQ_NSTREAMS * LQ_L * 4);
-    int16_t *ring_all = reinterpret_cast<int16_t *>(rows_all + (size_t)nwarps * 2 * TB);
-
+    unsigned char *wbase = smem + kTablesSmem + (size_t)(threadIdx.x >> 5) * tiledec_warp_smem(a.TB);
+    uint16_t *rows = reinterpret_cast<uint16_t *>(wbase);
+    int16_t *ring = reinterpret_cast<int16_t *>(wbase + (size_t)2 * a.TB * 2);
     const uint32_t chunk = blockIdx.y;
-    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    {
-        const uint4 *src = reinterpret_cast<const uint4 *>(dec_tab + (size_t)chunk * LQ_NSTREAMS * LQ_L);
-        uint4 *dst = reinterpret_cast<uint4 *>(dtab);
-        for (int i = threadIdx.x; i < LQ_NSTREAMS * LQ_L / 4; i += blockDim.x) dst[i] = __ldg(src + i);
-    }
+    stage_tables(a, chunk, dtab);
     __syncthreads();
-
-    const uint32_t N = n_heads * bph;
-    const uint32_t wpc = (N + 31) >> 5;
-    const uint32_t tile0 = (blockIdx.x * nwarps + warp) * 2;
-    if (tile0 >= n_tiles) return;
-    uint16_t *rows = rows_all + (size_t)warp * 2 * TB;
-    int16_t *ring = ring_all + (size_t)warp * kRing * kRingStride;
-    const uint32_t lt = (1u << lane) - 1u;
-
-    uint32_t tbv[2], n0v[2];
-    bool tact[2];
+    const uint32_t tile0 = (blockIdx.x * nwarps + (threadIdx.x >> 5)) * 2;
+    if (tile0 >= a.n_tiles) return;
+    const uint32_t N = a.n_heads * a.bph;
+    decode_two_tiles(a, chunk, tile0, dtab, rows, ring, [&](int t, int cc, uint32_t p, const int *sym) {
+        const uint32_t b = (tile0 + t) * a.TB + p;
+        const size_t gb = (size_t)chunk * N + b;
+        if (sym_out) {
+            int4 *so = reinterpret_cast<int4 *>(sym_out) + 2 * gb;
+            so[0] = make_int4(sym[0], sym[1], sym[2], sym[3]);
+            so[1] = make_int4(sym[4], sym[5], sym[6], sym[7]);
+        }
+        if constexpr (DO >= 0) {
+            float q[8];
+            e8_from_symbols(cc, sym, q);
+            const float sc = __half2float(__ushort_as_half(a.scale_f16[chunk * a.n_heads + bph_div.div(b)]));
 #pragma unroll
-    for (int t = 0; t < 2; ++t) {
-        const uint32_t tile = tile0 + t;
-        tact[t] = tile < n_tiles;
-        tbv[t] = tact[t] ? ((tile * TB + TB <= N) ? TB : N - tile * TB) : 0u;
-        n0v[t] = tact[t] ? tile_n0[chunk * n_tiles + tile] : 0u;
-        if (!tact[t]) continue;
-        // rank -> position lists: coset-0 rank r at r, coset-1 rank r at tb-1-r
-        const uint32_t *cw = coset_words + (size_t)chunk * wpc + (size_t)tile * (TB >> 5);
-        uint32_t c0 = 0, c1 = 0;
-        const uint32_t tb = tbv[t];
-        for (uint32_t off = 0; off < tb; off += 32) {
-            const uint32_t word = __ldg(cw + (off >> 5));
-            const uint32_t left = tb - off;
-            const uint32_t actm = left >= 32 ? 0xffffffffu : ((1u << left) - 1u);
-            const uint32_t w1 = word & actm, w0 = ~word & actm;
-            if (lane < left) {
-                const uint32_t pos = ((word >> lane) & 1u) ? tb - 1 - (c1 + __popc(w1 & lt)) : c0 + __popc(w0 & lt);
-                rows[t * TB + pos] = (uint16_t)(off + lane);
-            }
-            c1 += __popc(w1);
-            c0 += __popc(w0);
+            for (int i = 0; i < 8; ++i) q[i] = __fmul_rn(q[i], sc);
+            store_block8<DO>(out, gb, q);
         }
-    }
-
-    // lane setup: lanes 0-15 -> tile0, 16-31 -> tile0+1; stream s = lane & 15
-    const uint32_t lt_tile = lane >> 4, s = lane & 15u, c = s >> 3;
-    const uint32_t tile = tile0 + lt_tile;
-    const bool my_act = lt_tile ? tact[1] : tact[0];
-    const uint32_t my_tb = lt_tile ? tbv[1] : tbv[0], my_n0 = lt_tile ? n0v[1] : n0v[0];
-    int n = my_act ? (int)(c ? my_tb - my_n0 : my_n0) : 0;
-    const uint32_t tabi = chunk * LQ_NSTREAMS + s;
-    int lo = 0;
-    uint32_t x = LQ_L, nb = 0, nw = 0;
-    const uint32_t *wp = words;
-    if (n > 0) {
-        const int nsym = tab_nsym[tabi];
-        lo = tab_lo[tabi];
-        const uint32_t lg = (chunk * n_tiles + tile) * LQ_NSTREAMS + s;
-        const uint32_t w0 = lane_off[lg];
-        nb = lane_nbits[lg];
-        nw = (nb + 31u) >> 5;
-        x = lane_state[lg];
-        if (nsym <= 0 || nsym > LQ_L) {
-            raise_flag(err, LQ_EF_ALPHABET);
-            n = 0;
-        } else if ((uint64_t)w0 + nw > n_words) {
-            raise_flag(err, LQ_EF_BITSTREAM);
-            n = 0;
-        }
-        wp = words + w0;
-    }
-    const uint32_t *dt = dtab + s * LQ_L;
-    const uint16_t *fr = tab_freq + (size_t)tabi * LQ_L;
-    // 64-bit MSB-first bit buffer over the lane's words (bit-reversed reference
-    // words).  `avail` counts valid bits; a step takes at most 10, so after a
-    // refill (avail >= 33) three table-driven steps can run before the next
-    // refill, which is predicated rather than branched.
-    uint64_t bb = 0;
-    int avail = 0;
-    uint32_t wi = 0;
-    auto refill = [&]() {
-        const bool need = avail <= 32;
-        const uint32_t w = (need && wi < nw) ? __brev(__ldg(wp + wi)) : 0u;
-        if (need) {
-            bb |= (uint64_t)w << (32 - avail);
-            avail += 32;
-            ++wi;
-        }
-    };
-    refill();
-    refill();
-    // bits consumed so far = 32*wi - avail (words past the end read as zeros)
-    // the table-driven step is exact while x is in [L, 2L) and 10 more bits exist
-    int budget = (int)nb - 10;
-    bool fast_ok = (x >> LQ_LOG2_L) == 1u;
-    const int maxn = (int)__reduce_max_sync(0xffffffffu, (unsigned)n);
-
-    auto fast_step = [&](int j) {
-        const uint32_t slot = x & (LQ_L - 1);
-        const uint32_t e = dt[slot];
-        ring[j * kRingStride + lane] = (int16_t)((int)(e & 0x3ffu) + lo);
-        const uint32_t k = (e >> 10) & 0xfu;
-        x = (e >> 14) | __funnelshift_lc((uint32_t)(bb >> 32), 0u, k);
-        bb <<= k;
-        avail -= (int)k;
-        budget -= (int)k;
-    };
-    auto slow_step = [&](int j) {
-        const uint32_t slot = x & (LQ_L - 1);
-        const uint32_t e = dt[slot];
-        const uint32_t si = e & 0x3ffu;
-        ring[j * kRingStride + lane] = (int16_t)((int)si + lo);
-        const uint32_t k = (e >> 10) & 0xfu;
-        if (fast_ok && budget >= 0) {
-            x = (e >> 14) | __funnelshift_lc((uint32_t)(bb >> 32), 0u, k);
-            bb <<= k;
-            avail -= (int)k;
-            budget -= (int)k;
-        } else {
-            // literal reference step (end of lane, or a state outside [L, 2L))
-            uint32_t pos = (uint32_t)((int)nb - 10 - budget);
-            const uint32_t f = fr[si];
-            const uint32_t cf = f + slot - ((e >> 14) >> k);  // (e >> 14) >> k == f + slot - cf
-            x = f * (x >> LQ_LOG2_L) + slot - cf;
-            while (x < (uint32_t)LQ_L && pos < nb) {
-                x = (x << 1) | (uint32_t)(bb >> 63);
-                bb <<= 1;
-                --avail;
-                ++pos;
-                refill();
-            }
-            budget = (int)nb - 10 - (int)pos;
-            fast_ok = (x >> LQ_LOG2_L) == 1u;
-        }
-        refill();
-    };
-
-    for (int base = 0; base < maxn; base += kRing) {
-        const int cnt = min(kRing, n - base);
-        int j = 0;
-        // groups of three table-driven steps while every step of the group is exact
-        for (; j + 3 <= cnt && fast_ok && budget >= 20; j += 3) {
-            fast_step(j);
-            fast_step(j + 1);
-            fast_step(j + 2);
-            refill();
-        }
-        for (; j < cnt; ++j) slow_step(j);
-        __syncwarp();
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-            const int t = g >> 1, cc = g & 1;
-            if (!tact[t]) continue;
-            const int nc = (int)(cc ? tbv[t] - n0v[t] : n0v[t]);
-            const int r = base + (int)lane;
-            if (r < nc) {
-                const uint32_t p = rows[t * TB + (cc ? tbv[t] - 1 - r : r)];
-                const uint4 u = *reinterpret_cast<const uint4 *>(ring + lane * kRingStride + t * 16 + cc * 8);
-                int sym[8];
-                sym[0] = (int16_t)(u.x & 0xffffu); sym[1] = (int16_t)(u.x >> 16);
-                sym[2] = (int16_t)(u.y & 0xffffu); sym[3] = (int16_t)(u.y >> 16);
-                sym[4] = (int16_t)(u.z & 0xffffu); sym[5] = (int16_t)(u.z >> 16);
-                sym[6] = (int16_t)(u.w & 0xffffu); sym[7] = (int16_t)(u.w >> 16);
-                const uint32_t b = (tile0 + t) * TB + p;
-                const size_t gb = (size_t)chunk * N + b;
-                if (sym_out) {
-                    int4 *so = reinterpret_cast<int4 *>(sym_out) + 2 * gb;
-                    so[0] = make_int4(sym[0], sym[1], sym[2], sym[3]);
-                    so[1] = make_int4(sym[4], sym[5], sym[6], sym[7]);
-                }
-                if constexpr (DO >= 0) {
-                    float q[8];
-                    e8_from_symbols(cc, sym, q);
-                    const float sc = __half2float(__ushort_as_half(scale_f16[chunk * n_heads + bph_div.div(b)]));
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) q[i] = __fmul_rn(q[i], sc);
-                    store_block8<DO>(out, gb, q);
-                }
-            }
-        }
-        __syncwarp();
-    }
+    }, err);
 }
 
 // ---------------------------------------------------------------- reference streams
@@ -741,15 +571,16 @@ extern "C" int lq_rans_decode(const uint32_t *words, int64_t n_words, const uint
         const size_t sm = fused_smem_bytes(nwarps, (uint32_t)tile_blocks);
         dim3 grid((unsigned)ceil_div(n_tiles, 2 * nwarps), (unsigned)n_chunks);
         const FastDiv bd((uint32_t)bph);
+        const ChunkDev cv{words,     (uint32_t)n_words, lane_off,          lane_nbits,           lane_state,
+                          coset_words, tile_n0,         (uint32_t)n_heads, (uint32_t)bph,        (uint32_t)tile_blocks,
+                          (uint32_t)n_tiles, tab_lo,    tab_nsym,          tab_freq,             dec_tab,
+                          scale_f16};
 #define LQ_LAUNCH_FUSED(DOV)                                                                                    \
     do {                                                                                                        \
         if (cudaFuncSetAttribute(decode_fused_kernel<DOV>, cudaFuncAttributeMaxDynamicSharedMemorySize,        \
                                  (int)sm) != cudaSuccess)                                                       \
             return LQ_ERR_CUDA;                                                                                 \
-        decode_fused_kernel<DOV><<<grid, 32 * nwarps, sm, st>>>(                                                \
-            words, (uint32_t)n_words, lane_off, lane_nbits, lane_state, coset_words, tile_n0, (uint32_t)n_heads, \
-            (uint32_t)bph, bd, (uint32_t)tile_blocks, (uint32_t)n_tiles, tab_lo, tab_nsym, tab_freq, dec_tab,     \
-            scale_f16, out, sym_out, err);                                                                      \
+        decode_fused_kernel<DOV><<<grid, 32 * nwarps, sm, st>>>(cv, bd, out, sym_out, err);                   \
     } while (0)
         if (!out) LQ_LAUNCH_FUSED(-1);
         else if (out_dtype == LQ_F32) LQ_LAUNCH_FUSED(LQ_F32);
