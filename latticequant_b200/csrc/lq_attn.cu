@@ -56,12 +56,12 @@ __host__ __device__ constexpr int padded_g() {
 
 template <int G, int BPT>
 __host__ __device__ constexpr int attn_threads() {
-    return G <= 4 ? 768 : 512;
+    return G <= 2 ? 768 : G <= 4 ? 640 : 512;
 }
 
 // Fused attention partials.  BPT = blocks per token = head_dim / 8.
 template <int G, int BPT, int QDT>
-__global__ void __launch_bounds__(attn_threads<G, BPT>()) attn_partial_kernel(AttnArgs a) {
+__global__ void __launch_bounds__(attn_threads<G, BPT>(), 1) attn_partial_kernel(AttnArgs a) {
     static_assert(BPT == 8 || BPT == 16, "head_dim 64 or 128");
     static_assert(G >= 1 && G <= 8, "query group 1..8");
     constexpr int D = 8 * BPT, GP = padded_g<G>(), TPG = 16 / BPT;
@@ -70,8 +70,9 @@ __global__ void __launch_bounds__(attn_threads<G, BPT>()) attn_partial_kernel(At
     const int warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     const uint32_t lane = threadIdx.x & 31, dc = lane % BPT;
     unsigned char *wb = smem + a.region0 + (size_t)warp * a.warp_bytes;
-    int16_t *ring = reinterpret_cast<int16_t *>(wb);
-    float *sc = reinterpret_cast<float *>(wb + kAttnRing * kRingStride * 2);
+    const uint32_t ring = smem_addr(wb);
+    const uint32_t dta = smem_addr(dtab);
+    float *sc = reinterpret_cast<float *>(wb + (kAttnRing + 2) * kRingStride * 2);
 
     const uint32_t head = blockIdx.y;
     const uint32_t pb = (uint32_t)(((uint64_t)blockIdx.x * a.n_pairs) / a.nct);
@@ -95,10 +96,10 @@ __global__ void __launch_bounds__(attn_threads<G, BPT>()) attn_partial_kernel(At
     __syncthreads();
     if (wact) {
         decode_two_tiles_ordered<kAttnRing>(
-            a.k, 0, tile0, act0, act1, dtab, ring,
-            [&](bool ok, int t, uint32_t grp, uint32_t j, uint32_t cc, const int *sym) {
+            a.k, 0, tile0, act0, act1, dta, ring,
+            [&](bool ok, int t, uint32_t grp, uint32_t j, uint32_t cc, const uint4 blk) {
                 float kq[8];
-                e8_from_symbols((int)cc, sym, kq);
+                ring_point(blk, kq);
                 float dot[G];
 #pragma unroll
                 for (int g = 0; g < G; ++g) {
@@ -173,11 +174,11 @@ __global__ void __launch_bounds__(attn_threads<G, BPT>()) attn_partial_kernel(At
         for (int i = 0; i < 8; ++i) acc[g][i] = 0.f;
     if (wact) {
         decode_two_tiles_ordered<kAttnRing>(
-            a.v, 0, tile0, act0, act1, dtab, ring,
-            [&](bool ok, int t, uint32_t grp, uint32_t j, uint32_t cc, const int *sym) {
+            a.v, 0, tile0, act0, act1, dta, ring,
+            [&](bool ok, int t, uint32_t grp, uint32_t j, uint32_t cc, const uint4 blk) {
                 if (!ok) return;
                 float vq[8];
-                e8_from_symbols((int)cc, sym, vq);
+                ring_point(blk, vq);
                 const uint32_t tok = grp * TPG + j / BPT;
                 const float *pp = sc + ((uint32_t)t * a.tpt + tok) * GP;
                 float p[GP];
@@ -308,7 +309,7 @@ struct AttnPlan {
 };
 
 size_t attn_warp_bytes(int G, uint32_t tpt) {
-    return (size_t)kAttnRing * kRingStride * 2 + (size_t)2 * tpt * ((G + 3) & ~3) * 4;
+    return (size_t)(kAttnRing + 2) * kRingStride * 2 + (size_t)2 * tpt * ((G + 3) & ~3) * 4;
 }
 
 int attn_plan(int64_t n_heads, int64_t bph, int64_t tile_blocks, int G, int D, AttnPlan *p) {
@@ -320,7 +321,7 @@ int attn_plan(int64_t n_heads, int64_t bph, int64_t tile_blocks, int G, int D, A
     p->tpt = (uint32_t)(tile_blocks / bpt);
     p->n_pairs = (p->tph + 1) / 2;
     const size_t wb = attn_warp_bytes(G, p->tpt);
-    int nw = G <= 4 ? 24 : 16;
+    int nw = G <= 2 ? 24 : G <= 4 ? 20 : 16;
     for (;; --nw) {
         if (nw < 4) return LQ_ERR_INVALID;  // tiles too long for shared memory
         const size_t r0 = (std::max<size_t>(kTablesSmem, (size_t)nw * G * (D + 2) * 4) + 127) & ~(size_t)127;

@@ -93,15 +93,14 @@ __device__ inline void store_block8(void *y, int64_t blk, const float v[8]) {
         uint32_t w[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            uint16_t lo, hi;
+            // paired round-to-nearest-even conversions (one cvt per two values)
             if constexpr (DT == LQ_F16) {
-                lo = __half_as_ushort(__float2half_rn(v[2 * i]));
-                hi = __half_as_ushort(__float2half_rn(v[2 * i + 1]));
+                const __half2 h = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+                w[i] = *reinterpret_cast<const uint32_t *>(&h);
             } else {
-                lo = __bfloat16_as_ushort(__float2bfloat16_rn(v[2 * i]));
-                hi = __bfloat16_as_ushort(__float2bfloat16_rn(v[2 * i + 1]));
+                const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+                w[i] = *reinterpret_cast<const uint32_t *>(&h);
             }
-            w[i] = (uint32_t)lo | ((uint32_t)hi << 16);
         }
         reinterpret_cast<uint4 *>(y)[blk] = make_uint4(w[0], w[1], w[2], w[3]);
     }

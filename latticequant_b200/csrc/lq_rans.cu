@@ -397,45 +397,49 @@ __global__ void __launch_bounds__(256) reconstruct_kernel(const int16_t *__restr
 }
 
 // ---------------------------------------------------------------- fused decode
-// Decode + dequantise: lq_tiledec.cuh's tile decoder with an epilogue that
-// rebuilds the E8 point (symbols_to_e8) and writes it times the fp16 head
-// scale, 16 bytes per block for 16-bit outputs.
-__host__ __device__ inline size_t fused_smem_bytes(int nwarps, uint32_t TB) {
-    return kTablesSmem + (size_t)nwarps * tiledec_warp_smem(TB);
-}
+// Decode + dequantise: lq_tiledec.cuh's position-ordered tile decoder with
+// an epilogue that rebuilds the E8 point (symbols_to_e8) and writes it times
+// the fp16 head scale; a half-warp writes 16 consecutive blocks per step.
+constexpr int kDecR = 48;                                             // ring rows per round
+constexpr size_t kDecRingBytes = (size_t)(kDecR + 2) * kRingStride * 2;  // + 2 carried rows
+__host__ __device__ inline size_t fused_smem_bytes(int nwarps) { return kTablesSmem + (size_t)nwarps * kDecRingBytes; }
 
 template <int DO>
-__global__ void __launch_bounds__(768) decode_fused_kernel(ChunkDev a, FastDiv bph_div, void *__restrict__ out,
-                                                          int32_t *__restrict__ sym_out, uint32_t *err) {
+__global__ void __launch_bounds__(1024, 1) decode_fused_kernel(ChunkDev a, FastDiv bph_div, void *__restrict__ out,
+                                                              int32_t *__restrict__ sym_out, uint32_t *err) {
     extern __shared__ __align__(16) unsigned char smem[];
     uint32_t *dtab = reinterpret_cast<uint32_t *>(smem);
     const int nwarps = blockDim.x >> 5;
-    unsigned char *wbase = smem + kTablesSmem + (size_t)(threadIdx.x >> 5) * tiledec_warp_smem(a.TB);
-    uint16_t *rows = reinterpret_cast<uint16_t *>(wbase);
-    int16_t *ring = reinterpret_cast<int16_t *>(wbase + (size_t)2 * a.TB * 2);
+    const uint32_t ring = smem_addr(smem + kTablesSmem + (size_t)(threadIdx.x >> 5) * kDecRingBytes);
     const uint32_t chunk = blockIdx.y;
     stage_tables(a, chunk, dtab);
     __syncthreads();
     const uint32_t tile0 = (blockIdx.x * nwarps + (threadIdx.x >> 5)) * 2;
     if (tile0 >= a.n_tiles) return;
     const uint32_t N = a.n_heads * a.bph;
-    decode_two_tiles(a, chunk, tile0, dtab, rows, ring, [&](int t, int cc, uint32_t p, const int *sym) {
-        const uint32_t b = (tile0 + t) * a.TB + p;
-        const size_t gb = (size_t)chunk * N + b;
-        if (sym_out) {
-            int4 *so = reinterpret_cast<int4 *>(sym_out) + 2 * gb;
-            so[0] = make_int4(sym[0], sym[1], sym[2], sym[3]);
-            so[1] = make_int4(sym[4], sym[5], sym[6], sym[7]);
-        }
-        if constexpr (DO >= 0) {
-            float q[8];
-            e8_from_symbols(cc, sym, q);
-            const float sc = __half2float(__ushort_as_half(a.scale_f16[chunk * a.n_heads + bph_div.div(b)]));
+    decode_two_tiles_ordered<kDecR>(
+        a, chunk, tile0, true, true, smem_addr(dtab), ring,
+        [&](bool ok, int t, uint32_t grp, uint32_t j, uint32_t cc, const uint4 blk) {
+            if (!ok) return;
+            const uint32_t b = (tile0 + t) * a.TB + grp * 16 + j;
+            const size_t gb = (size_t)chunk * N + b;
+            if (sym_out) {
+                int sym[8];
+                ring_symbols(blk, cc, sym);
+                int4 *so = reinterpret_cast<int4 *>(sym_out) + 2 * gb;
+                so[0] = make_int4(sym[0], sym[1], sym[2], sym[3]);
+                so[1] = make_int4(sym[4], sym[5], sym[6], sym[7]);
+            }
+            if constexpr (DO >= 0) {
+                float q[8];
+                ring_point(blk, q);
+                const float sc = __half2float(__ushort_as_half(a.scale_f16[chunk * a.n_heads + bph_div.div(b)]));
 #pragma unroll
-            for (int i = 0; i < 8; ++i) q[i] = __fmul_rn(q[i], sc);
-            store_block8<DO>(out, gb, q);
-        }
-    }, err);
+                for (int i = 0; i < 8; ++i) q[i] = __fmul_rn(q[i], sc);
+                store_block8<DO>(out, gb, q);
+            }
+        },
+        err);
 }
 
 // ---------------------------------------------------------------- reference streams
@@ -565,10 +569,9 @@ extern "C" int lq_rans_decode(const uint32_t *words, int64_t n_words, const uint
     const int64_t n_tiles = ceil_div(N, tile_blocks);
     const int64_t n_lanes = n_chunks * n_tiles * LQ_NSTREAMS;
     // fused path: tables + per-warp rank lists + rings fit in shared memory
-    int nwarps = 24;  // one CTA per SM; as many warps as shared memory allows
-    while (nwarps >= 4 && fused_smem_bytes(nwarps, (uint32_t)tile_blocks) > 227 * 1024) nwarps -= 1;
-    if (nwarps >= 4 && n_chunks <= 65535 && n_lanes < ((int64_t)1 << 32)) {
-        const size_t sm = fused_smem_bytes(nwarps, (uint32_t)tile_blocks);
+    const int nwarps = 32;  // one CTA of 32 warps per SM
+    if (n_chunks <= 65535 && n_lanes < ((int64_t)1 << 32)) {
+        const size_t sm = fused_smem_bytes(nwarps);
         dim3 grid((unsigned)ceil_div(n_tiles, 2 * nwarps), (unsigned)n_chunks);
         const FastDiv bd((uint32_t)bph);
         const ChunkDev cv{words,     (uint32_t)n_words, lane_off,          lane_nbits,           lane_state,

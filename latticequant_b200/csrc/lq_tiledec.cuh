@@ -2,26 +2,50 @@
 //
 // One warp decodes two tiles of a chunk: lanes 0-15 the 16 lanes (streams) of
 // the first tile, lanes 16-31 those of the second.  Per round each lane
-// decodes up to kRing symbols of its lane into a shared ring; then the warp
-// hands every block whose 8 symbols just arrived (rank r of coset c in tile
-// t -> block position via a rank->position list built from the coset bits)
-// to an epilogue: write it out dequantised, or fold it into attention scores
+// decodes a run of symbols of its lane into a shared ring; then the warp
+// hands the blocks whose 8 symbols just arrived, in block order, to an
+// epilogue: write them out dequantised, or fold them into attention scores
 // or value sums.  The chunk's 16 decode tables live in shared memory.
 //
 // Decoder step (reference: core/gpu_ans.py:146-168): for x in [L, 2L) the
-// table entry for slot = x & (L-1) gives (symbol, k, base) and
-// x = base | next k bits, read MSB-first from a 64-bit buffer over the
+// table entry for slot = x & (L-1) gives (symbol, k, xs) and
+// x = xs << k | next k bits, read MSB-first from a 64-bit buffer over the
 // bit-reversed reference words.  Near the end of a lane, or for a state
 // outside [L, 2L), the reference formula runs literally, including its stop
 // at n_bits, so truncated or odd streams decode exactly as the reference does.
+//
+// Shared memory is addressed with 32-bit shared-window addresses and moved
+// with ld.shared / st.shared, so the hot loop carries no generic-pointer
+// arithmetic.
 #pragma once
 
 #include "lq_common.cuh"
 
 namespace lq {
 
-constexpr int kRing = 32;
-constexpr int kRingStride = 40;  // int16 per ring row: 80 B keeps 8-symbol groups 16-B aligned, conflict-free
+constexpr int kRingStride = 40;  // u16 per ring row: 80 B keeps 8-symbol groups 16-B aligned, conflict-free
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint4 lds_v4(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ void sts_u16(uint32_t a, uint32_t v) {
+    asm volatile("st.shared.u16 [%0], %1;" ::"r"(a), "r"(v));
+}
+__device__ __forceinline__ uint32_t lds_u16(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
 
 // Device view of a batch of equal chunks in the lane layout.
 struct ChunkDev {
@@ -35,52 +59,109 @@ struct ChunkDev {
     const uint16_t *scale_f16;
 };
 
-// per-warp shared memory of the decoder: rank lists for 2 tiles + the ring
-__host__ __device__ inline size_t tiledec_warp_smem(uint32_t TB) {
-    return (size_t)2 * TB * 2 + (size_t)kRing * kRingStride * 2;
-}
 constexpr size_t kTablesSmem = (size_t)LQ_NSTREAMS * LQ_L * 4;
+
+// Shared-memory form of a decode-table entry, for x in [L, 2L):
+//   bits  0-15  the symbol as a biased doubled lattice coordinate:
+//               2*sym + c + 2^15 for coordinates 0-6, 4*sym + c + 2^15 for
+//               coordinate 7 (c = the stream's coset), i.e. 2*q + 2^15 before
+//               the parity bit of q7 (entropy_coder.py:71-89 inverted later)
+//   bits 16-26  xs = f + slot - cf, the state before renormalisation
+//   bits 27-31  k, the bits renormalisation reads (x' = xs << k | next k bits)
+// Built from lq_expand_tables' entry (si | k << 10 | (xs << k) << 14).
+__device__ __forceinline__ uint32_t smem_entry(uint32_t e, int lo, int c, int mul) {
+    const uint32_t si = e & 0x3ffu, k = (e >> 10) & 0xfu, xs = (e >> 14) >> k;
+    const uint32_t v = (uint32_t)(((int)si + lo) * mul + c + 32768) & 0xffffu;
+    return v | (xs << 16) | (k << 27);
+}
 
 // all threads of the CTA: the chunk's 16 decode tables into shared memory
 __device__ inline void stage_tables(const ChunkDev &a, uint32_t chunk, uint32_t *dtab) {
     const uint4 *src = reinterpret_cast<const uint4 *>(a.dec_tab + (size_t)chunk * LQ_NSTREAMS * LQ_L);
     uint4 *dst = reinterpret_cast<uint4 *>(dtab);
-    for (int i = threadIdx.x; i < LQ_NSTREAMS * LQ_L / 4; i += blockDim.x) dst[i] = __ldg(src + i);
+    for (int i = threadIdx.x; i < LQ_NSTREAMS * LQ_L / 4; i += blockDim.x) {
+        const int s = i >> 8;  // 256 uint4 per table
+        const int lo = __ldg(a.tab_lo + chunk * LQ_NSTREAMS + s);
+        const int c = s >> 3, mul = (s & 7) == 7 ? 4 : 2;
+        uint4 u = __ldg(src + i);
+        u.x = smem_entry(u.x, lo, c, mul);
+        u.y = smem_entry(u.y, lo, c, mul);
+        u.z = smem_entry(u.z, lo, c, mul);
+        u.w = smem_entry(u.w, lo, c, mul);
+        dst[i] = u;
+    }
 }
 
-// the 8 int16 symbols of one block, 16-byte aligned in shared memory
-__device__ __forceinline__ void ring_block(const int16_t *p, int *sym) {
-    const uint4 u = *reinterpret_cast<const uint4 *>(p);
-    sym[0] = (int16_t)(u.x & 0xffffu);
-    sym[1] = (int16_t)(u.x >> 16);
-    sym[2] = (int16_t)(u.y & 0xffffu);
-    sym[3] = (int16_t)(u.y >> 16);
-    sym[4] = (int16_t)(u.z & 0xffffu);
-    sym[5] = (int16_t)(u.z >> 16);
-    sym[6] = (int16_t)(u.w & 0xffffu);
-    sym[7] = (int16_t)(u.w >> 16);
+// ---- blocks in the ring: 8 u16 = 2q + 2^15 (q7 without its parity bit)
+// Exact E8 point of a ring block.  A value v < 2^16 placed in the mantissa of
+// 1.5 * 2^22 (where the spacing is 0.5) reads back as 1.5 * 2^22 + v / 2, so
+// one byte permute and one subtraction give q exactly.
+__device__ __forceinline__ float ring_value(uint32_t w, bool hi, float off) {
+    return __int_as_float(__byte_perm(w, 0x4AC00000u, hi ? 0x7632u : 0x7610u)) - off;
+}
+
+__device__ __forceinline__ uint32_t ring_parity(const uint4 u) {
+    // parity of sum(sym[0..6]) = xor of bit 1 of the seven stored values
+    const uint32_t x = u.x ^ u.y ^ u.z ^ (u.w & 0xffffu);
+    return ((x ^ (x >> 16)) >> 1) & 1u;
+}
+
+__device__ __forceinline__ void ring_point(const uint4 u, float q[8]) {
+    constexpr float kOff = 6307840.0f;  // 1.5 * 2^22 + 2^15 / 2
+    q[0] = ring_value(u.x, false, kOff);
+    q[1] = ring_value(u.x, true, kOff);
+    q[2] = ring_value(u.y, false, kOff);
+    q[3] = ring_value(u.y, true, kOff);
+    q[4] = ring_value(u.z, false, kOff);
+    q[5] = ring_value(u.z, true, kOff);
+    q[6] = ring_value(u.w, false, kOff);
+    // q7 = (4*sym7 + c)/2 + parity
+    q[7] = ring_value(u.w, true, __int_as_float(0x4AC08000 - 2 * (int)ring_parity(u)));
+}
+
+// the reference's integer symbols (entropy_coder.py:46-68) of a ring block
+__device__ __forceinline__ void ring_symbols(const uint4 u, int c, int sym[8]) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int v = (int)((w[i >> 1] >> (16 * (i & 1))) & 0xffffu) - 32768 - c;
+        sym[i] = v >> (i == 7 ? 2 : 1);
+    }
 }
 
 // Decoder state of one lane (one stream of one tile).
+//
+// Bits are read MSB-first from a 64-bit buffer bh:bl over the bit-reversed
+// reference words (`avail` valid bits from the top of bh), with the word
+// after them already loaded in `nxt`, so the load of a word is issued a full
+// word of symbols before it is needed.  A table-driven ("fast") step is exact
+// while x is in [L, 2L) and the k bits it reads exist (consumed + 10 <=
+// n_bits); during a run of fast steps only x's low 10 bits (the next slot)
+// are kept exact and x is rebuilt as (x & (L-1)) | L before a literal step.
 struct LaneDec {
     const uint32_t *wp;
-    const uint32_t *dt;
     const uint16_t *fr;
-    uint64_t bb;  // 64-bit MSB-first bit buffer, `avail` valid bits
-    uint32_t x, nb, nw, wi;
-    int lo, avail, budget;
+    uint32_t dtb;  // shared address of this stream's table
+    uint32_t bh, bl;
+    uint32_t x, nb, nw, wi, nxt;
+    int lo, avail, c, shift;
     bool fast_ok;
+
+    // bits consumed so far: words moved into the buffer minus what is left there
+    __device__ __forceinline__ int consumed() const { return 32 * (int)(wi - 1u) - avail; }
 
     // Set up lane `s` of tile `tile`; returns the symbol count n (0 on a bad
     // table or a lane running past the word array, with the flag raised).
-    __device__ __forceinline__ int init(const ChunkDev &a, uint32_t chunk, uint32_t tile, uint32_t s,
-                                        const uint32_t *dtab, int n, uint32_t *err) {
+    __device__ __forceinline__ int init(const ChunkDev &a, uint32_t chunk, uint32_t tile, uint32_t s, uint32_t dtab,
+                                        int n, uint32_t *err) {
         const uint32_t tabi = chunk * LQ_NSTREAMS + s;
         lo = 0;
         x = LQ_L;
         nb = 0;
         nw = 0;
         wp = a.words;
+        c = (int)(s >> 3);
+        shift = (s & 7) == 7 ? 2 : 1;
         if (n > 0) {
             const int nsym = a.tab_nsym[tabi];
             lo = a.tab_lo[tabi];
@@ -92,177 +173,182 @@ struct LaneDec {
             if (nsym <= 0 || nsym > LQ_L) {
                 raise_flag(err, LQ_EF_ALPHABET);
                 n = 0;
+                nw = 0;
             } else if ((uint64_t)w0 + nw > a.n_words) {
                 raise_flag(err, LQ_EF_BITSTREAM);
                 n = 0;
+                nw = 0;
             }
             wp = a.words + w0;
         }
-        dt = dtab + s * LQ_L;
+        dtb = dtab + s * (LQ_L * 4);
         fr = a.tab_freq + (size_t)tabi * LQ_L;
-        bb = 0;
-        avail = 0;
-        wi = 0;
-        refill();
-        refill();
-        // the table-driven step is exact while x is in [L, 2L) and 10 more bits exist
-        budget = (int)nb - 10;
+        bh = __brev(nw > 0 ? __ldg(wp) : 0u);
+        bl = __brev(nw > 1 ? __ldg(wp + 1) : 0u);
+        nxt = nw > 2 ? __ldg(wp + 2) : 0u;
+        avail = 64;
+        wi = 3;
         fast_ok = (x >> LQ_LOG2_L) == 1u;
         return n;
     }
 
-    // A step takes at most 10 bits, so after a refill (avail >= 33) three
-    // table-driven steps can run before the next refill, which is predicated
-    // rather than branched.
-    __device__ __forceinline__ void refill() {
-        const bool need = avail <= 32;
-        const uint32_t w = (need && wi < nw) ? __brev(__ldg(wp + wi)) : 0u;
-        if (need) {
-            bb |= (uint64_t)w << (32 - avail);
-            avail += 32;
-            ++wi;
-        }
-    }
-
-    __device__ __forceinline__ void fast_step(int16_t *dst) {
-        const uint32_t slot = x & (LQ_L - 1);
-        const uint32_t e = dt[slot];
-        *dst = (int16_t)((int)(e & 0x3ffu) + lo);
-        const uint32_t k = (e >> 10) & 0xfu;
-        x = (e >> 14) | __funnelshift_lc((uint32_t)(bb >> 32), 0u, k);
-        bb <<= k;
+    // drop the top k (<= 31) bits of the buffer
+    __device__ __forceinline__ void take(uint32_t k) {
+        bh = __funnelshift_l(bl, bh, k);
+        bl = __funnelshift_l(0u, bl, k);  // bl << k for k < 32, without clamping code
         avail -= (int)k;
-        budget -= (int)k;
     }
 
-    __device__ __forceinline__ void slow_step(int16_t *dst) {
-        const uint32_t slot = x & (LQ_L - 1);
-        const uint32_t e = dt[slot];
-        const uint32_t si = e & 0x3ffu;
-        *dst = (int16_t)((int)si + lo);
-        const uint32_t k = (e >> 10) & 0xfu;
-        if (fast_ok && budget >= 0) {
-            x = (e >> 14) | __funnelshift_lc((uint32_t)(bb >> 32), 0u, k);
-            bb <<= k;
-            avail -= (int)k;
-            budget -= (int)k;
+    // move the prefetched word into the buffer once 32 bits are free (no branch)
+    __device__ __forceinline__ void refill() {
+        const bool r = avail <= 32;
+        const uint32_t w = __brev(nxt);
+        bh |= r ? __funnelshift_rc(w, 0u, (uint32_t)avail) : 0u;  // w >> avail, 0 when avail == 32
+        bl |= r ? __funnelshift_l(0u, w, (uint32_t)(32 - avail)) : 0u;
+        avail += r ? 32 : 0;
+        uint32_t v = 0;
+        if (r && wi < nw) v = __ldg(wp + wi);
+        nxt = r ? v : nxt;
+        wi += r ? 1u : 0u;
+    }
+
+    __device__ __forceinline__ void fast_step(uint32_t dst) {
+        const uint32_t e = lds_u32(dtb + ((x & (LQ_L - 1)) << 2));
+        sts_u16(dst, e);
+        const uint32_t k = e >> 27;
+        // (xs << k) | next k bits; the k-field above xs lands above bit 10
+        x = __funnelshift_l(bh, e >> 16, k);
+        take(k);
+    }
+
+    // one step, table-driven when exact, else the reference formula literally
+    // (including its stop at n_bits: core/gpu_ans.py:160-166)
+    __device__ __forceinline__ void single_step(uint32_t dst) {
+        if (fast_ok && consumed() + 10 <= (int)nb) {
+            fast_step(dst);
         } else {
-            // literal reference step (end of lane, or a state outside [L, 2L))
-            uint32_t pos = (uint32_t)((int)nb - 10 - budget);
+            if (fast_ok) x = (x & (LQ_L - 1)) | LQ_L;
+            const uint32_t slot = x & (LQ_L - 1);
+            const uint32_t e = lds_u32(dtb + (slot << 2));
+            sts_u16(dst, e);
+            const int sym = ((int)(e & 0xffffu) - 32768 - c) >> shift;
+            const uint32_t si = (uint32_t)(sym - lo) & 0x3ffu;
             const uint32_t f = fr[si];
-            const uint32_t cf = f + slot - ((e >> 14) >> k);  // (e >> 14) >> k == f + slot - cf
+            const uint32_t cf = f + slot - ((e >> 16) & 0x7ffu);
             x = f * (x >> LQ_LOG2_L) + slot - cf;
-            while (x < (uint32_t)LQ_L && pos < nb) {
-                x = (x << 1) | (uint32_t)(bb >> 63);
-                bb <<= 1;
-                --avail;
-                ++pos;
+            while (x < (uint32_t)LQ_L && consumed() < (int)nb) {
+                x = (x << 1) | (bh >> 31);
+                take(1);
                 refill();
             }
-            budget = (int)nb - 10 - (int)pos;
             fast_ok = (x >> LQ_LOG2_L) == 1u;
         }
         refill();
     }
 
-    // decode `cnt` symbols into col[0], col[stride], ...
-    __device__ __forceinline__ void run(int cnt, int16_t *col, int stride) {
+    // Three table-driven steps and a refill, written out in PTX so the group
+    // costs what its arithmetic costs: per step a slot lookup, the ring
+    // store, two shifts out of the entry, three funnel shifts (the new state
+    // and the 64-bit buffer) and the bit count; the refill is predicated, not
+    // branched.  Variable shifts are funnel shifts whose amount the hardware
+    // takes as given (wrap) or clamps itself, so no range fix-up is emitted.
+    // Ring rows are kRingStride u16 apart.
+    __device__ __forceinline__ void fast_group(uint32_t dst) {
+        static_assert(kRingStride * 2 == 80, "ring row offsets below");
+        asm volatile(
+            "{\n\t"
+            ".reg .b32 e, k, t, a, w, z;\n\t"
+            ".reg .pred p, q;\n\t"
+            ".reg .b64 ad;\n\t"
+            "mov.b32 z, 0;\n\t"
+            "and.b32 a, %0, 1023;\n\t"
+            "mad.lo.u32 a, a, 4, %6;\n\t"
+            "ld.shared.u32 e, [a];\n\t"
+            "st.shared.u16 [%7], e;\n\t"
+            "shr.u32 k, e, 27;\n\t"
+            "shr.u32 t, e, 16;\n\t"
+            "shf.l.wrap.b32 %0, %1, t, k;\n\t"
+            "shf.l.wrap.b32 %1, %2, %1, k;\n\t"
+            "shf.l.wrap.b32 %2, z, %2, k;\n\t"
+            "sub.s32 %3, %3, k;\n\t"
+            "and.b32 a, %0, 1023;\n\t"
+            "mad.lo.u32 a, a, 4, %6;\n\t"
+            "ld.shared.u32 e, [a];\n\t"
+            "st.shared.u16 [%7+80], e;\n\t"
+            "shr.u32 k, e, 27;\n\t"
+            "shr.u32 t, e, 16;\n\t"
+            "shf.l.wrap.b32 %0, %1, t, k;\n\t"
+            "shf.l.wrap.b32 %1, %2, %1, k;\n\t"
+            "shf.l.wrap.b32 %2, z, %2, k;\n\t"
+            "sub.s32 %3, %3, k;\n\t"
+            "and.b32 a, %0, 1023;\n\t"
+            "mad.lo.u32 a, a, 4, %6;\n\t"
+            "ld.shared.u32 e, [a];\n\t"
+            "st.shared.u16 [%7+160], e;\n\t"
+            "shr.u32 k, e, 27;\n\t"
+            "shr.u32 t, e, 16;\n\t"
+            "shf.l.wrap.b32 %0, %1, t, k;\n\t"
+            "shf.l.wrap.b32 %1, %2, %1, k;\n\t"
+            "shf.l.wrap.b32 %2, z, %2, k;\n\t"
+            "sub.s32 %3, %3, k;\n\t"
+            // refill: when at most 32 bits are left, append the prefetched word
+            // below them and prefetch the next one (0 past the lane's end)
+            "setp.le.s32 p, %3, 32;\n\t"
+            "@p brev.b32 w, %4;\n\t"
+            "@p sub.s32 t, 32, %3;\n\t"
+            "@p shf.l.wrap.b32 t, z, w, t;\n\t"
+            "@p or.b32 %2, %2, t;\n\t"
+            "@p shf.r.clamp.b32 t, w, z, %3;\n\t"
+            "@p or.b32 %1, %1, t;\n\t"
+            "@p add.s32 %3, %3, 32;\n\t"
+            "setp.lt.and.u32 q, %5, %8, p;\n\t"
+            "@p mov.b32 %4, 0;\n\t"
+            "@q mad.wide.u32 ad, %5, 4, %9;\n\t"
+            "@q ld.global.nc.u32 %4, [ad];\n\t"
+            "@p add.u32 %5, %5, 1;\n\t"
+            "}"
+            : "+r"(x), "+r"(bh), "+r"(bl), "+r"(avail), "+r"(nxt), "+r"(wi)
+            : "r"(dtb), "r"(dst), "r"(nw), "l"(wp));
+    }
+
+    // decode `cnt` symbols to shared addresses dst, dst + sb, dst + 2*sb, ...
+    // (sb = one ring row)
+    __device__ __forceinline__ void run(int cnt, uint32_t dst) {
+        constexpr uint32_t sb = kRingStride * 2;
         int j = 0;
-        // groups of three table-driven steps while every step of the group is exact
-        for (; j + 3 <= cnt && fast_ok && budget >= 20; j += 3) {
-            fast_step(col + j * stride);
-            fast_step(col + (j + 1) * stride);
-            fast_step(col + (j + 2) * stride);
-            refill();
+        if (fast_ok) {
+            // groups of three table-driven steps while all three stay inside the lane
+            const int lim = (int)nb - 30;
+            for (; j + 3 <= cnt && consumed() <= lim; j += 3) {
+                fast_group(dst);
+                dst += 3 * sb;
+            }
         }
-        for (; j < cnt; ++j) slow_step(col + j * stride);
+        for (; j < cnt; ++j) {
+            single_step(dst);
+            dst += sb;
+        }
     }
 };
-
-// One warp: decode tiles tile0 and tile0+1 (when they exist) of `chunk` and
-// call epi(t, coset, position_in_tile, sym[8]) once per block, in rank order;
-// `rows` holds 2*TB u16, `ring` kRing*kRingStride int16 of this warp's
-// shared memory.
-template <class Epi>
-__device__ __forceinline__ void decode_two_tiles(const ChunkDev &a, uint32_t chunk, uint32_t tile0,
-                                                 const uint32_t *dtab, uint16_t *rows, int16_t *ring, Epi &&epi,
-                                                 uint32_t *err) {
-    const uint32_t lane = threadIdx.x & 31;
-    const uint32_t TB = a.TB, n_tiles = a.n_tiles;
-    const uint32_t N = a.n_heads * a.bph;
-    const uint32_t wpc = (N + 31) >> 5;
-    const uint32_t lt = (1u << lane) - 1u;
-
-    uint32_t tbv[2], n0v[2];
-    bool tact[2];
-#pragma unroll
-    for (int t = 0; t < 2; ++t) {
-        const uint32_t tile = tile0 + t;
-        tact[t] = tile < n_tiles;
-        tbv[t] = tact[t] ? ((tile * TB + TB <= N) ? TB : N - tile * TB) : 0u;
-        n0v[t] = tact[t] ? a.tile_n0[chunk * n_tiles + tile] : 0u;
-        if (!tact[t]) continue;
-        // rank -> position lists: coset-0 rank r at r, coset-1 rank r at tb-1-r
-        const uint32_t *cw = a.coset_words + (size_t)chunk * wpc + (size_t)tile * (TB >> 5);
-        uint32_t c0 = 0, c1 = 0;
-        const uint32_t tb = tbv[t];
-        for (uint32_t off = 0; off < tb; off += 32) {
-            const uint32_t word = __ldg(cw + (off >> 5));
-            const uint32_t left = tb - off;
-            const uint32_t actm = left >= 32 ? 0xffffffffu : ((1u << left) - 1u);
-            const uint32_t w1 = word & actm, w0 = ~word & actm;
-            if (lane < left) {
-                const uint32_t pos = ((word >> lane) & 1u) ? tb - 1 - (c1 + __popc(w1 & lt)) : c0 + __popc(w0 & lt);
-                rows[t * TB + pos] = (uint16_t)(off + lane);
-            }
-            c1 += __popc(w1);
-            c0 += __popc(w0);
-        }
-    }
-    __syncwarp();
-
-    // lane setup: lanes 0-15 -> tile0, 16-31 -> tile0+1; stream s = lane & 15
-    const uint32_t lt_tile = lane >> 4, s = lane & 15u, c = s >> 3;
-    const bool my_act = lt_tile ? tact[1] : tact[0];
-    const uint32_t my_tb = lt_tile ? tbv[1] : tbv[0], my_n0 = lt_tile ? n0v[1] : n0v[0];
-    LaneDec d;
-    const int n = d.init(a, chunk, tile0 + lt_tile, s, dtab, my_act ? (int)(c ? my_tb - my_n0 : my_n0) : 0, err);
-    const int maxn = (int)__reduce_max_sync(0xffffffffu, (unsigned)n);
-
-    for (int base = 0; base < maxn; base += kRing) {
-        d.run(min(kRing, n - base), ring + lane, kRingStride);
-        __syncwarp();
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-            const int t = g >> 1, cc = g & 1;
-            if (!tact[t]) continue;
-            const int nc = (int)(cc ? tbv[t] - n0v[t] : n0v[t]);
-            const int r = base + (int)lane;
-            if (r < nc) {
-                const uint32_t p = rows[t * TB + (cc ? tbv[t] - 1 - r : r)];
-                int sym[8];
-                ring_block(ring + lane * kRingStride + t * 16 + cc * 8, sym);
-                epi(t, cc, p, sym);
-            }
-        }
-        __syncwarp();
-    }
-}
 
 // One warp: decode tiles tile0 (lanes 0-15, if act0) and tile0+1 (lanes
 // 16-31, if act1) in POSITION order.  Each round a half-warp takes the next
 // groups of 16 block positions of its tile, as many as keep both cosets'
 // new symbols within R (at least one group, since a group holds 16 blocks):
-// the 8 lanes of each coset decode exactly the symbols of those groups into
-// ring rows 0.., and then every lane j of the half takes block 16*group + j.
-// All 32 lanes call epi(ok, t, group, j, coset, sym) together once per group
-// step (ok = false for a lane without a block), so the epilogue may use
-// warp shuffles; blocks reach it in increasing position order per lane.
+// the 8 lanes of each coset own exactly the symbols of those groups in ring
+// rows 0.., and then every lane j of the half takes block 16*group + j.
+// Lanes decode in whole groups of three steps; the one or two symbols a lane
+// decodes past the round's need are carried to rows 0.. of the next round.
+// All 32 lanes call epi(ok, t, group, j, coset, block) together once per
+// group step (ok = false for a lane without a block), so the epilogue may
+// use warp shuffles; blocks reach it in increasing position order per lane.
+// `ring` is (R + 2) rows of kRingStride u16.
 template <int R, class Epi>
 __device__ __forceinline__ void decode_two_tiles_ordered(const ChunkDev &a, uint32_t chunk, uint32_t tile0, bool act0,
-                                                         bool act1, const uint32_t *dtab, int16_t *ring, Epi &&epi,
+                                                         bool act1, uint32_t dtab, uint32_t ring, Epi &&epi,
                                                          uint32_t *err) {
-    static_assert(R >= 16 && R * kRingStride * 2 < 65536, "ring rows");
+    static_assert(R >= 16 && (R + 2) * kRingStride * 2 < 65536, "ring rows");
+    constexpr uint32_t kRow = kRingStride * 2;
     const uint32_t lane = threadIdx.x & 31, hb = lane & 16u, j = lane & 15u, c = j >> 3;
     const uint32_t TB = a.TB, N = a.n_heads * a.bph;
     const uint32_t wpc = (N + 31) >> 5;
@@ -272,9 +358,11 @@ __device__ __forceinline__ void decode_two_tiles_ordered(const ChunkDev &a, uint
     const uint32_t ngroups = (tb + 15u) >> 4;
     const uint32_t n0 = act ? a.tile_n0[chunk * a.n_tiles + tile] : 0u;
     const uint32_t *cw = a.coset_words + (size_t)chunk * wpc + (size_t)(act ? tile : 0u) * (TB >> 5);
+    const uint32_t col = ring + lane * 2;
     LaneDec d;
     const int n = d.init(a, chunk, act ? tile : 0u, j, dtab, act ? (int)(c ? tb - n0 : n0) : 0, err);
     uint32_t gpos = 0;
+    int ahead = 0, prev = 0;  // symbols decoded past the last round's need, at rows prev..
     for (;;) {
         // coset bits of this half's next 16 groups, one per lane, and their prefix counts
         const uint32_t gk = gpos + j;
@@ -305,7 +393,19 @@ __device__ __forceinline__ void decode_two_tiles_ordered(const ChunkDev &a, uint
         const int n1r = __shfl_sync(0xffffffffu, p1, last);
         const int n0r = __shfl_sync(0xffffffffu, p0, last);
         const int cnt = (ng > 0 && n > 0) ? (c ? n1r : n0r) : 0;
-        d.run(cnt, ring + lane, kRingStride);
+        if (ahead > 0 && prev > 0) {  // carried symbols to rows 0, 1 (forward copy)
+            sts_u16(col, lds_u16(col + (uint32_t)prev * kRow));
+            if (ahead > 1) sts_u16(col + kRow, lds_u16(col + (uint32_t)(prev + 1) * kRow));
+        }
+        const int need = cnt - ahead;
+        if (need > 0) {
+            const int dec = (need + 2) / 3 * 3;
+            d.run(dec, col + (uint32_t)ahead * kRow);
+            ahead += dec - cnt;
+        } else {
+            ahead = -need;
+        }
+        prev = cnt;
         __syncwarp();
         for (int it = 0; it < ngmax; ++it) {
             const int src = (int)hb + it;
@@ -317,14 +417,9 @@ __device__ __forceinline__ void decode_two_tiles_ordered(const ChunkDev &a, uint
             const uint32_t cc = (bi >> j) & 1u;
             const uint32_t below = (1u << j) - 1u;
             const int rr = cc ? b1 + __popc(bi & below) : b0 + __popc(~bi & below);
-            int sym[8];
-            if (ok) {
-                ring_block(ring + rr * kRingStride + hb + cc * 8u, sym);
-            } else {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) sym[i] = 0;
-            }
-            epi(ok, (int)(hb >> 4), gpos + (uint32_t)it, j, cc, sym);
+            uint4 blk = make_uint4(0x80008000u, 0x80008000u, 0x80008000u, 0x80008000u);  // q = 0
+            if (ok) blk = lds_v4(ring + (uint32_t)rr * kRow + (hb + cc * 8u) * 2u);
+            epi(ok, (int)(hb >> 4), gpos + (uint32_t)it, j, cc, blk);
         }
         __syncwarp();
         gpos += (uint32_t)ng;
