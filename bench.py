@@ -13,6 +13,14 @@ decode every chunk back to bf16.  value = E8 blocks round-tripped per second
 e2e = the same through the public API from pinned host memory: H2D of the
 bf16 cache, compress, decompress, D2H of the decoded cache.
 
+The line also carries "attention": BASELINE config 3, one fused dequant +
+decode-attention step (B=16, 32 query / 8 KV heads, head_dim 128, context
+32768 compressed at 4 bits/dim; K/V = N(0,1) * lognormal(0, 0.5) per vector,
+q ~ N(0, 1/sqrt(128)) bf16), metric = algorithmic bytes (compressed K+V +
+lane metadata + q + o) per second.  At N GPUs the context is sequence-sharded:
+each rank attends over its slice and one NCCL all-gather of (o, lse) plus the
+LSE merge completes the step (strong scaling of one decode step).
+
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 """
 import argparse
@@ -34,6 +42,9 @@ BLOCKS = N_CHUNKS * N_KV * BPH
 TILE = 1024
 METRIC = "E8+rANS encode/decode Gvec/s"
 UNIT = "Gvec/s"
+# config 3 (fused dequant + decode attention)
+A_B, A_HKV, A_G, A_S, A_D = 16, 8, 4, 32768, 128
+A_METRIC = "fused dequant-attn HBM GB/s"
 
 
 def make_cache(gen_device, seed, n_layers=N_LAYERS):
@@ -131,6 +142,170 @@ def cpu_baseline(n_threads, sample_chunks=2, reps=1):
     return blocks / dt / 1e9, blocks, dt
 
 
+def attention_kv(gen_device, seed, s_len):
+    """Config-3 K or V slice: N(0,1) * lognormal(0, 0.5) per vector, bf16."""
+    import torch
+
+    g = torch.Generator(device=gen_device)
+    g.manual_seed(seed)
+    shape = (A_B, A_HKV, s_len, A_D)
+    return (torch.randn(shape, generator=g, device=gen_device) *
+            torch.exp(0.5 * torch.randn(A_B, A_HKV, s_len, 1, generator=g, device=gen_device))).to(torch.bfloat16)
+
+
+def attention_query(gen_device):
+    import torch
+
+    g = torch.Generator(device=gen_device)
+    g.manual_seed(3003)
+    return (torch.randn(A_B, A_HKV * A_G, A_D, generator=g, device=gen_device) / A_D ** 0.5).to(torch.bfloat16)
+
+
+def cpu_attention_baseline(s_len=2048):
+    """Reference CPU path of one decode step on a sample: oracle lane decode +
+    dequant (oracle/lq_oracle_codec.c) of K and V for one batch row, then the
+    softmax attention in numpy; rate in GB/s of the same algorithmic bytes."""
+    import numpy as np
+
+    import oracle.lq_oracle as O
+
+    O.build()
+    rng = np.random.default_rng(11)
+    shape = (1, A_HKV, s_len, A_D)
+    chunks = []
+    for _ in range(2):
+        x = (rng.standard_normal(shape) * np.exp(0.5 * rng.standard_normal(shape[:3] + (1,)))).astype(np.float32)
+        chunks.append(O.compress_chunk(x, O.DT_F32, A_HKV, s_len * A_D // 8, BITS, TILE))
+    q = (rng.standard_normal((1, A_HKV * A_G, A_D)) / A_D ** 0.5).astype(np.float32)
+    t0 = time.perf_counter()
+    k = O.decompress_chunk(chunks[0]).reshape(shape)
+    v = O.decompress_chunk(chunks[1]).reshape(shape)
+    O.decode_attention_f64(q, k, v, 1 / A_D ** 0.5)
+    dt = time.perf_counter() - t0
+    nbytes = sum(4 * len(c.words) + (c.n_vectors + 7) // 8 + 2 * c.n_heads for c in chunks) + 2 * q.nbytes
+    return nbytes / dt / 1e9, nbytes, dt
+
+
+def bench_attention(dev, rank, world, steps, warmup, barrier):
+    """Config 3 on `world` ranks (sequence-sharded).  Returns the line's
+    "attention" object on rank 0 (None elsewhere)."""
+    import torch
+    import torch.distributed as dist
+
+    from latticequant_b200 import attention as A
+    from latticequant_b200 import codec as C
+    from latticequant_b200 import sharding as SH
+
+    lo, hi = SH.sequence_slice(A_S, world, rank, TILE // (A_D // 8))
+    k = attention_kv(dev, 4000 + 2 * rank, hi - lo)
+    v = attention_kv(dev, 4001 + 2 * rank, hi - lo)
+    q = attention_query(dev)
+    kc, _ = C.compress(k, BITS, tile_blocks=TILE)
+    vc, _ = C.compress(v, BITS, tile_blocks=TILE)
+    del k, v
+    op = A.DecodeAttention(kc, vc, A_G)
+    rows = A_B * A_HKV * A_G
+    o_loc = torch.empty(rows, A_D, dtype=torch.float32 if world > 1 else torch.bfloat16, device=dev)
+    l_loc = torch.empty(rows, dtype=torch.float32, device=dev)
+    out = torch.empty(rows, A_D, dtype=torch.bfloat16, device=dev)
+    l_out = torch.empty(rows, dtype=torch.float32, device=dev)
+    o_all = torch.empty(world, rows, A_D, dtype=torch.float32, device=dev)
+    l_all = torch.empty(world, rows, dtype=torch.float32, device=dev)
+
+    def step():
+        op(q, o_loc, l_loc if world > 1 else None)
+        if world > 1:
+            dist.all_gather_into_tensor(o_all, o_loc)
+            dist.all_gather_into_tensor(l_all, l_loc)
+            A.merge_attention(o_all, l_all, out=out, lse=l_out)
+
+    for _ in range(max(warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    if op.flags():
+        raise RuntimeError(f"attention device error flags {op.flags():#x}")
+    st = torch.cuda.current_stream(dev)
+    # the fused kernel pair alone (roofline), then the whole step
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(steps):
+        op(q, o_loc, l_loc if world > 1 else None)
+    e1.record(st)
+    torch.cuda.synchronize()
+    k_ms = e0.elapsed_time(e1) / steps
+    barrier()
+    e0.record(st)
+    for _ in range(steps):
+        step()
+    e1.record(st)
+    torch.cuda.synchronize()
+    barrier()
+    ms = e0.elapsed_time(e1) / steps
+    local_bytes = (kc.compressed_bytes() + vc.compressed_bytes() + kc.metadata_bytes() + vc.metadata_bytes() +
+                   q.numel() * 2 + rows * A_D * o_loc.element_size())
+    comp_bytes = kc.compressed_bytes() + vc.compressed_bytes()
+
+    # e2e: the public API call per step with host buffers (q in, o out)
+    host_q = q.cpu().pin_memory()
+    host_o = torch.empty(rows, A_D, dtype=torch.bfloat16).pin_memory()
+    dq = torch.empty_like(q)
+
+    def e2e_step():
+        dq.copy_(host_q, non_blocking=True)
+        if world > 1:
+            ol, ll = A.decode_attention(dq, kc, vc, out_dtype=torch.float32, return_lse=True)
+            o, _ = SH.sequence_sharded_merge(ol.view(rows, A_D), ll.view(rows), out_dtype=torch.bfloat16)
+        else:
+            o = A.decode_attention(dq, kc, vc)
+        host_o.copy_(o.view(rows, A_D), non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e0.record(st)
+    k2 = max(2, min(steps, 5))
+    for _ in range(k2):
+        e2e_step()
+    e1.record(st)
+    torch.cuda.synchronize()
+    ems = e0.elapsed_time(e1) / k2
+
+    vals = torch.tensor([ms, k_ms, ems, float(local_bytes), float(comp_bytes)], dtype=torch.float64, device=dev)
+    if world > 1:
+        mx = vals[:3].clone()
+        sm = vals[3:].clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        vals = torch.cat([mx, sm])
+    ms, k_ms, ems, tot_bytes, tot_comp = [float(t) for t in vals.tolist()]
+    if rank != 0:
+        return None
+    peak, peak_kind = measured_peaks()
+    achieved = local_bytes / (k_ms * 1e-3) / 1e9  # rank 0's kernel pair
+    cpu = None
+    try:
+        v_cpu, nb, dt = cpu_attention_baseline()
+        cpu = {"value": v_cpu, "unit": "GB/s", "cores": 1, "kind": "port",
+               "sample": f"1 of {A_B} batch rows, 2048 tokens: oracle lane decode + dequant of K and V, "
+                         f"numpy attention ({nb} B, {dt:.2f} s)"}
+    except Exception as e:  # the baseline is reported, not required
+        cpu = {"unavailable": str(e)[:200]}
+    return {"metric": A_METRIC, "value": tot_bytes / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms,
+            "compressed_GBps": tot_comp / (ms * 1e-3) / 1e9,
+            "decode_steps_per_s": 1e3 / ms, "tokens_per_s": A_B * 1e3 / ms,
+            "config": {"workload": "config3: B16 x 32 q-heads / 8 kv-heads x D128, ctx 32768, 4 b/dim, one decode "
+                                   "step", "parallelism": f"sequence-sharded over {world} (all-gather + LSE merge)"
+                                   if world > 1 else "single GPU", "tile_blocks": TILE,
+                       "bits_per_dim": tot_comp * 8 / (2 * A_B * A_HKV * A_S * A_D),
+                       "l2": "compressed K+V larger than L2"},
+            "roofline": {"bound": "hbm", "kernel": "attn_partial_kernel + attn_combine_kernel", "achieved": achieved,
+                         "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind,
+                         "traffic": None, "kernel_ms": k_ms},
+            "e2e": {"value": tot_bytes / (ems * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ems,
+                    "h2d_bytes_per_step": q.numel() * 2, "d2h_bytes_per_step": rows * A_D * 2},
+            "gpu_launches": steps * (2 + (1 if world > 1 else 0)), "cpu_baseline": cpu}
+
+
 def run_reference(args):
     """--impl reference: the reference's CPU path (C oracle port) on the host cores."""
     rank = int(os.environ.get("RANK", "0"))
@@ -155,6 +330,11 @@ def run_reference(args):
             "cpu_baseline": {"value": v, "unit": UNIT, "cores": n_thr, "kind": "port",
                              "sample": f"{sample} of 64 chunks per step (oracle/lq_oracle_codec.c, pthreads)"},
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if not args.no_attn:
+        va, nb, dt = cpu_attention_baseline()
+        line["attention"] = {"metric": A_METRIC, "value": va, "unit": "GB/s",
+                             "cpu_baseline": {"value": va, "unit": "GB/s", "cores": 1, "kind": "port",
+                                              "sample": f"1 of {A_B} batch rows, 2048 tokens ({nb} B, {dt:.2f} s)"}}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -168,6 +348,7 @@ def main():
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-attn", action="store_true", help="skip the config-3 attention measurement")
     ap.add_argument("--layers", type=int, default=N_LAYERS,
                     help="layers of the cache (profiling runs use fewer; bench lines use 32)")
     args = ap.parse_args()
@@ -206,8 +387,8 @@ def main():
         cd.expand_tables(enc=False, dec=True)
         cd.decode(out)
 
-    # launches per step: scales 2, quantize 1, tables 2 (+1 expand dec), encode 5, decode 4
-    launches_per_step = (1 if C.lib().lq_head_scales_workspace(N_CHUNKS * N_KV, BPH * 8) == 0 else 2) + 1 + 2 + 5 + 1 + 4
+    # launches per step: scales 1-2, quantize 1, tables 2 (+1 expand dec), encode 5, decode 1
+    launches_per_step = (1 if C.lib().lq_head_scales_workspace(N_CHUNKS * N_KV, BPH * 8) == 0 else 2) + 1 + 2 + 5 + 1 + 1
 
     # correctness gate: one eager step, error word clear, lossless round trip on a sample chunk
     step()
@@ -328,6 +509,13 @@ def main():
                "sample": f"{blocks} blocks ({blocks // (N_KV * BPH)} chunks of config 2), "
                          f"oracle/lq_oracle_codec.c on {n_thr} threads, {dt:.1f} s"}
 
+    attn = None
+    if not args.no_attn:
+        del x, out
+        cd = None
+        torch.cuda.empty_cache()
+        attn = bench_attention(dev, rank, world, args.steps, args.warmup, barrier)
+
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
@@ -342,7 +530,7 @@ def main():
                 "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
                              "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None},
                 "clocks": clocks, "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
-                "cpu_baseline": cpu}
+                "cpu_baseline": cpu, "attention": attn}
         print(json.dumps(line), flush=True)
     if graph is not None:
         del graph

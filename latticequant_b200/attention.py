@@ -60,22 +60,8 @@ def supports(k_chunk: LaneChunk, group: int) -> bool:
     return attention_workspace_bytes(k_chunk, group) > 0
 
 
-def decode_attention(q: torch.Tensor, k_chunk: LaneChunk, v_chunk: LaneChunk, sm_scale: Optional[float] = None,
-                     out_dtype: Optional[torch.dtype] = None, return_lse: bool = False,
-                     out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None,
-                     workspace: Optional[torch.Tensor] = None):
-    """softmax(q K^T * sm_scale) V for one decode step, K/V read compressed.
-
-    q: (B, Hq, D) or (B, Hq, 1, D) on the device; K/V chunks of a (B, Hkv, S, D)
-    tensor each with Hq a multiple of Hkv (GQA as repeat_kv).  Returns o with
-    q's shape (and the fp32 (B, Hq) log-sum-exp of the scores if return_lse).
-    """
-    _lib.require_cuda(q)
-    kshape, vshape = tuple(k_chunk.orig_shape), tuple(v_chunk.orig_shape)
-    if len(kshape) != 4 or kshape != vshape:
-        raise ValueError("K and V chunks must hold (B, Hkv, S, D) tensors of one shape")
+def _q3(q: torch.Tensor, kshape) -> torch.Tensor:
     B, Hkv, S, D = kshape
-    qshape = tuple(q.shape)
     if q.dim() == 4:
         if q.shape[2] != 1:
             raise ValueError("decode attention takes one query position")
@@ -85,40 +71,76 @@ def decode_attention(q: torch.Tensor, k_chunk: LaneChunk, v_chunk: LaneChunk, sm
     else:
         raise ValueError("q must be (B, Hq, D) or (B, Hq, 1, D)")
     if q3.shape[0] != B or q3.shape[2] != D or q3.shape[1] % Hkv != 0:
-        raise ValueError(f"q {qshape} does not match K/V {kshape}")
-    group = q3.shape[1] // Hkv
-    q3 = q3.contiguous()
-    od = out_dtype or q.dtype
+        raise ValueError(f"q {tuple(q.shape)} does not match K/V {tuple(kshape)}")
+    return q3
+
+
+class DecodeAttention:
+    """A prepared fused attention over one (K chunk, V chunk) pair: device
+    workspace and error word allocated once, launches without host syncs (so
+    a decode step can be captured in a CUDA graph); flags() reads the error word."""
+
+    def __init__(self, k_chunk: LaneChunk, v_chunk: LaneChunk, group: int):
+        kshape, vshape = tuple(k_chunk.orig_shape), tuple(v_chunk.orig_shape)
+        if len(kshape) != 4 or kshape != vshape:
+            raise ValueError("K and V chunks must hold (B, Hkv, S, D) tensors of one shape")
+        self.shape = kshape
+        self.group = int(group)
+        self.k, self.v = k_chunk, v_chunk
+        self.kv, self.vv = chunk_view(k_chunk), chunk_view(v_chunk)
+        need = attention_workspace_bytes(k_chunk, self.group)
+        if need == 0:
+            raise ValueError(f"fused attention does not take head_dim={kshape[3]}, group={group}, "
+                             f"tile_blocks={k_chunk.geom.tile_blocks} with {k_chunk.geom.bph} blocks per head")
+        dev = k_chunk.words.device
+        self.workspace = torch.empty(need, dtype=torch.uint8, device=dev)
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def __call__(self, q3: torch.Tensor, out: torch.Tensor, lse: Optional[torch.Tensor] = None,
+                 sm_scale: Optional[float] = None):
+        B, Hkv, S, D = self.shape
+        if sm_scale is None:
+            sm_scale = 1.0 / math.sqrt(D)
+        check(lib().lq_attn_decode(ctypes.byref(self.kv), ctypes.byref(self.vv), ptr(q3), _lib.dtype_code(q3.dtype),
+                                   Hkv, self.group, D, float(sm_scale), ptr(out), _lib.dtype_code(out.dtype),
+                                   ptr(lse), ptr(self.workspace), self.workspace.numel(), ptr(self.err),
+                                   stream_handle(q3.device)), "lq_attn_decode")
+
+    def flags(self) -> int:
+        return int(self.err.item()) & 0xFFFFFFFF
+
+
+def decode_attention(q: torch.Tensor, k_chunk: LaneChunk, v_chunk: LaneChunk, sm_scale: Optional[float] = None,
+                     out_dtype: Optional[torch.dtype] = None, return_lse: bool = False,
+                     out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None):
+    """softmax(q K^T * sm_scale) V for one decode step, K/V read compressed.
+
+    q: (B, Hq, D) or (B, Hq, 1, D) on the device; K/V chunks of a (B, Hkv, S, D)
+    tensor each with Hq a multiple of Hkv (GQA as repeat_kv).  Returns o with
+    q's shape (and the fp32 (B, Hq) log-sum-exp of the scores if return_lse).
+    """
+    _lib.require_cuda(q)
+    q3 = _q3(q, tuple(k_chunk.orig_shape)).contiguous()
+    Hkv, D = k_chunk.orig_shape[1], k_chunk.orig_shape[3]
+    op = DecodeAttention(k_chunk, v_chunk, q3.shape[1] // Hkv)
     dev = q.device
-    if sm_scale is None:
-        sm_scale = 1.0 / math.sqrt(D)
-    kv, vv = chunk_view(k_chunk), chunk_view(v_chunk)
-    ws_need = attention_workspace_bytes(k_chunk, group)
-    if ws_need == 0:
-        raise ValueError(f"fused attention does not take head_dim={D}, group={group}, "
-                         f"tile_blocks={k_chunk.geom.tile_blocks} with {k_chunk.geom.bph} blocks per head")
-    if workspace is None or workspace.numel() < ws_need:
-        workspace = torch.empty(ws_need, dtype=torch.uint8, device=dev)
     if out is None:
-        out = torch.empty(q3.shape, dtype=od, device=dev)
+        out = torch.empty(q3.shape, dtype=out_dtype or q.dtype, device=dev)
     if return_lse and lse is None:
         lse = torch.empty(q3.shape[:2], dtype=torch.float32, device=dev)
-    err = torch.zeros(1, dtype=torch.int32, device=dev)
-    check(lib().lq_attn_decode(ctypes.byref(kv), ctypes.byref(vv), ptr(q3), _lib.dtype_code(q3.dtype), Hkv, group,
-                               D, float(sm_scale), ptr(out), _lib.dtype_code(out.dtype),
-                               ptr(lse) if return_lse else None, ptr(workspace), workspace.numel(), ptr(err),
-                               stream_handle(dev)), "lq_attn_decode")
-    raise_flags(int(err.item()) & 0xFFFFFFFF, "decode_attention")
-    o = out.view(qshape[:-1] + (D,)) if q.dim() == 4 else out
+    op(q3, out, lse if return_lse else None, sm_scale)
+    raise_flags(op.flags(), "decode_attention")
+    o = out.view(tuple(q.shape[:-1]) + (D,)) if q.dim() == 4 else out
     return (o, lse) if return_lse else o
 
 
 def merge_attention(o_parts: Sequence[torch.Tensor] | torch.Tensor, lse_parts: Sequence[torch.Tensor] | torch.Tensor,
-                    out_dtype: Optional[torch.dtype] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+                    out_dtype: Optional[torch.dtype] = None, out: Optional[torch.Tensor] = None,
+                    lse: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
     """Combine attention over disjoint key sets: o = sum_i o_i exp(lse_i - lse).
 
     o_parts: n tensors (or one stacked tensor) of shape (..., D); lse_parts the
-    matching (...) log-sum-exps.  Returns (o, lse)."""
+    matching (...) log-sum-exps.  Returns (o, lse); out / lse may be given."""
     o = torch.stack(list(o_parts)) if not torch.is_tensor(o_parts) else o_parts
     ls = torch.stack(list(lse_parts)) if not torch.is_tensor(lse_parts) else lse_parts
     _lib.require_cuda(o)
@@ -126,11 +148,16 @@ def merge_attention(o_parts: Sequence[torch.Tensor] | torch.Tensor, lse_parts: S
     rows = o[0].numel() // D
     if ls.numel() != n * rows:
         raise ValueError("lse parts do not match the o parts")
-    of = o.reshape(n, rows, D).to(torch.float32).contiguous()
-    lf = ls.reshape(n, rows).to(torch.float32).contiguous()
-    od = out_dtype or o.dtype
-    out = torch.empty((rows, D), dtype=od, device=o.device)
-    lse = torch.empty(rows, dtype=torch.float32, device=o.device)
-    check(lib().lq_attn_merge(ptr(of), ptr(lf), n, rows, D, ptr(out), _lib.dtype_code(od), ptr(lse),
+    of = o.reshape(n, rows, D)
+    of = of if (of.dtype == torch.float32 and of.is_contiguous()) else of.to(torch.float32).contiguous()
+    lf = ls.reshape(n, rows)
+    lf = lf if (lf.dtype == torch.float32 and lf.is_contiguous()) else lf.to(torch.float32).contiguous()
+    if out is None:
+        out = torch.empty((rows, D), dtype=out_dtype or o.dtype, device=o.device)
+    if lse is None:
+        lse = torch.empty(rows, dtype=torch.float32, device=o.device)
+    if out.numel() != rows * D or lse.numel() != rows or not out.is_contiguous():
+        raise ValueError("merge outputs have the wrong size")
+    check(lib().lq_attn_merge(ptr(of), ptr(lf), n, rows, D, ptr(out), _lib.dtype_code(out.dtype), ptr(lse),
                               stream_handle(o.device)), "lq_attn_merge")
     return out.view(o.shape[1:]), lse.view(ls.shape[1:])
