@@ -149,6 +149,31 @@ __device__ __forceinline__ float div_by_scale(float a, float b, float y, bool b_
     return r == 0.0f ? q0 : __fmaf_rn(r, y, q0);
 }
 
+// The eight quotients of a block.  The FMA path is exact when every nonzero
+// |v| of the block lies in [2^-40, 2^40] (a NaN passes through it as NaN);
+// otherwise each value takes div_by_scale.  One range test per block keeps
+// the common case free of per-value branches.
+__device__ __forceinline__ void div_block_by_scale(const float v[8], float b, float y, bool b_ok, float xs[8]) {
+    float amax = 0.0f, amin = INFINITY;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float a = fabsf(v[i]);
+        amax = fmaxf(amax, a);
+        amin = fminf(amin, a == 0.0f ? INFINITY : a);
+    }
+    if (b_ok && amax <= 1.0995116e12f && amin >= 9.094947e-13f) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float q0 = __fmul_rn(v[i], y);
+            const float r = __fmaf_rn(-b, q0, v[i]);
+            xs[i] = v[i] == 0.0f ? q0 : __fmaf_rn(r, y, q0);  // r == 0 gives q0 as well
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) xs[i] = div_by_scale(v[i], b, y, b_ok);
+    }
+}
+
 // ---- E8 nearest point ---------------------------------------------------
 // Bit-exact restatement of core/e8_quantizer.py:20-83 as torch evaluates it
 // on the CPU: every operation below is one rounded binary32 op (explicit
@@ -187,9 +212,12 @@ __device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsig
 // D8 nearest point (core/e8_quantizer.py:20-58).  Flip cost RN(1 - 2|res|)
 // is one FMA because 2|res| is exact; the first-index argmin runs as a
 // tree in which the right operand wins only when strictly smaller, which
-// selects the same index as a left-to-right scan.
-__device__ __forceinline__ void d8_nearest(const float x[8], float r[8]) {
-    float res[8], c[8];
+// selects the same index as a left-to-right scan, and the tree's three
+// levels of outcomes select the flipped coordinate.  The flip adds
+// sign(res) with sign(0) = +1, i.e. copysign(1, res) (res is never -0:
+// x - rint(x) of equal values is +0).
+__device__ __forceinline__ void d8_nearest(const float x[8], float r[8], float res[8]) {
+    float c[8];
     float s = 0.0f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -201,30 +229,29 @@ __device__ __forceinline__ void d8_nearest(const float x[8], float r[8]) {
     }
     // parity = s % 2 != 0; s is integer valued, and even once |s| >= 2^24
     const bool odd = (fabsf(s) < 16777216.0f) && (((int)s) & 1);
-    float c01 = c[0], c23 = c[2], c45 = c[4], c67 = c[6];
-    int i01 = 0, i23 = 2, i45 = 4, i67 = 6;
-    if (c[1] < c01) { c01 = c[1]; i01 = 1; }
-    if (c[3] < c23) { c23 = c[3]; i23 = 3; }
-    if (c[5] < c45) { c45 = c[5]; i45 = 5; }
-    if (c[7] < c67) { c67 = c[7]; i67 = 7; }
-    if (c23 < c01) { c01 = c23; i01 = i23; }
-    if (c67 < c45) { c45 = c67; i45 = i67; }
-    const int best = (c45 < c01) ? i45 : i01;
+    const bool w01 = c[1] < c[0], w23 = c[3] < c[2], w45 = c[5] < c[4], w67 = c[7] < c[6];
+    const float c01 = w01 ? c[1] : c[0], c23 = w23 ? c[3] : c[2];
+    const float c45 = w45 ? c[5] : c[4], c67 = w67 ? c[7] : c[6];
+    const bool wa = c23 < c01, wb = c67 < c45;
+    const float ca = wa ? c23 : c01, cb = wb ? c67 : c45;
+    const bool wc = cb < ca;
+    const bool lo = odd && !wc, hi = odd && wc;
+    const bool f[8] = {lo && !wa && !w01, lo && !wa && w01, lo && wa && !w23, lo && wa && w23,
+                       hi && !wb && !w45, hi && !wb && w45, hi && wb && !w67, hi && wb && w67};
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        const float sg = res[i] < 0.0f ? -1.0f : 1.0f;  // sign(0) -> +1
-        if (odd && i == best) r[i] = __fadd_rn(r[i], sg);
+        if (f[i]) r[i] = __fadd_rn(r[i], copysignf(1.0f, res[i]));
     }
 }
 
 // E8 nearest point (core/e8_quantizer.py:61-83).  The two squared-distance
 // sums run left to right as the two halves of packed fp32x2 operations.
 __device__ __forceinline__ void e8_nearest(const float x[8], float q[8]) {
-    float c1[8], y[8], c2[8];
-    d8_nearest(x, c1);
+    float c1[8], y[8], c2[8], res[8];
+    d8_nearest(x, c1, res);
 #pragma unroll
     for (int i = 0; i < 8; ++i) y[i] = __fsub_rn(x[i], 0.5f);
-    d8_nearest(y, c2);
+    d8_nearest(y, c2, res);
     unsigned long long d = 0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -244,19 +271,20 @@ __device__ __forceinline__ void e8_nearest(const float x[8], float q[8]) {
 // The winning candidate's D8 coordinates are the symbols directly: for the
 // integer coset q = c1 and round(q) = c1; for the half coset q = c2 + 1/2 and
 // round(q - 1/2) = c2 (exact while |q| < 2^22, far beyond the symbol range).
-// Returns the coset bit; *finite is false when any distance is NaN/inf
-// (a non-finite input).
+// Returns the coset bit; *finite is false when any distance is NaN/inf (a
+// non-finite input).  q is written only when WANT_Q.
+template <bool WANT_Q>
 __device__ __forceinline__ int e8_nearest_symbols(const float x[8], float q[8], int sym[8], bool *finite) {
-    float c1[8], y[8], c2[8];
-    d8_nearest(x, c1);
+    float c1[8], y[8], c2[8], res[8];
+    d8_nearest(x, c1, res);
 #pragma unroll
     for (int i = 0; i < 8; ++i) y[i] = __fsub_rn(x[i], 0.5f);
-    d8_nearest(y, c2);
+    d8_nearest(y, c2, res);
     unsigned long long d = 0;
     float h[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        h[i] = __fadd_rn(c2[i], 0.5f);
+        h[i] = __fadd_rn(c2[i], 0.5f);  // the half-coset point, as the reference forms it
         const unsigned long long e = f2_pack(__fsub_rn(x[i], c1[i]), __fsub_rn(x[i], h[i]));
         const unsigned long long e2 = f2_mul(e, e);
         d = i ? f2_add(d, e2) : e2;
@@ -267,7 +295,7 @@ __device__ __forceinline__ int e8_nearest_symbols(const float x[8], float q[8], 
     const bool use1 = d1 <= d2;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        q[i] = use1 ? c1[i] : h[i];
+        if constexpr (WANT_Q) q[i] = use1 ? c1[i] : h[i];
         sym[i] = __float2int_rn(use1 ? c1[i] : c2[i]);
     }
     sym[7] = sym[7] >> 1;  // floor(coord8 / 2)

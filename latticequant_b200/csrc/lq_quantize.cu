@@ -26,7 +26,11 @@ constexpr int kQWarps = 8;          // tiles per CTA
 constexpr int kSmemHalf = 128;      // shared histogram window [-128, 128)
 constexpr int kSmemBins = 2 * kSmemHalf;
 
-template <int DT, int DQ>
+__device__ __forceinline__ void red_shared_add1(uint32_t addr) {
+    asm volatile("red.shared.add.u32 [%0], 1;" ::"r"(addr) : "memory");
+}
+
+template <int DT, int DQ, bool QO>
 __global__ void __launch_bounds__(32 * kQWarps, 4) quantize_kernel(
     const void *__restrict__ x, uint32_t n_heads, uint32_t bph, FastDiv bph_div, const float *__restrict__ scale_f32,
     uint32_t TB, uint32_t n_tiles, int16_t *__restrict__ sym_rows, uint32_t *__restrict__ coset_words,
@@ -41,6 +45,7 @@ __global__ void __launch_bounds__(32 * kQWarps, 4) quantize_kernel(
 
     for (int i = threadIdx.x; i < LQ_NSTREAMS * kSmemBins; i += blockDim.x) sh_hist[i] = 0;
     __syncthreads();
+    const uint32_t hist_base = static_cast<uint32_t>(__cvta_generic_to_shared(sh_hist));
 
     const uint32_t tile = blockIdx.x * kQWarps + warp;
     uint32_t flags = 0;
@@ -72,10 +77,9 @@ __global__ void __launch_bounds__(32 * kQWarps, 4) quantize_kernel(
                 const int64_t blk = cblk0 + b0 + off + lane;
                 float v[8], xs[8], q[8];
                 load_block8<DT>(x, blk, v);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) xs[i] = div_by_scale(v[i], sc, rcp, fast);
+                div_block_by_scale(v, sc, rcp, fast, xs);
                 bool finite;
-                coset = e8_nearest_symbols(xs, q, sym, &finite);
+                coset = e8_nearest_symbols<(DQ >= 0) || QO>(xs, q, sym, &finite);
                 if (!finite) flags |= LQ_EF_NONFINITE;
                 if constexpr (DQ >= 0) {
                     float o[8];
@@ -83,7 +87,7 @@ __global__ void __launch_bounds__(32 * kQWarps, 4) quantize_kernel(
                     for (int i = 0; i < 8; ++i) o[i] = __fmul_rn(q[i], sc);
                     store_block8<DQ>(deq, blk, o);
                 }
-                if (q_out) {
+                if constexpr (QO) {
                     float4 *qp = reinterpret_cast<float4 *>(q_out) + 2 * blk;
                     qp[0] = make_float4(q[0], q[1], q[2], q[3]);
                     qp[1] = make_float4(q[4], q[5], q[6], q[7]);
@@ -101,12 +105,12 @@ __global__ void __launch_bounds__(32 * kQWarps, 4) quantize_kernel(
                 packed.z = (uint32_t)(uint16_t)sym[4] | ((uint32_t)(uint16_t)sym[5] << 16);
                 packed.w = (uint32_t)(uint16_t)sym[6] | ((uint32_t)(uint16_t)sym[7] << 16);
                 reinterpret_cast<uint4 *>(rows)[row] = packed;
-                uint32_t *sh = sh_hist + coset * 8 * kSmemBins + kSmemHalf;
+                const uint32_t sh = hist_base + (uint32_t)coset * (8 * kSmemBins * 4);
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
                     const int v = sym[i];
                     if ((uint32_t)(v + kSmemHalf) < (uint32_t)kSmemBins) {
-                        atomicAdd(&sh[i * kSmemBins + v], 1u);
+                        red_shared_add1(sh + (uint32_t)(i * kSmemBins + v + kSmemHalf) * 4u);
                     } else if ((uint32_t)(v + LQ_SYM_LIMIT) < (uint32_t)(2 * LQ_SYM_LIMIT)) {
                         uint32_t *gh = hist + ((int64_t)chunk * LQ_NSTREAMS + coset * 8 + i) * LQ_HIST_BINS;
                         atomicAdd(&gh[v + LQ_SYM_LIMIT], 1u);
@@ -139,48 +143,58 @@ __global__ void __launch_bounds__(32 * kQWarps, 4) quantize_kernel(
     }
 }
 
-template <int DT, int DQ>
+template <int DT, int DQ, bool QO>
 int launch_quantize(const void *x, int64_t n_chunks, int64_t n_heads, int64_t bph, const float *scale_f32, int64_t TB,
                     int16_t *sym_rows, uint32_t *coset_words, uint32_t *tile_n0, uint32_t *hist, void *deq,
                     float *q_out, uint32_t *err, cudaStream_t st) {
     const int64_t N = n_heads * bph;
     const int64_t n_tiles = ceil_div(N, TB);
     dim3 grid((unsigned)ceil_div(n_tiles, kQWarps), (unsigned)n_chunks);
-    quantize_kernel<DT, DQ><<<grid, 32 * kQWarps, 0, st>>>(x, (uint32_t)n_heads, (uint32_t)bph, FastDiv((uint32_t)bph),
+    quantize_kernel<DT, DQ, QO><<<grid, 32 * kQWarps, 0, st>>>(x, (uint32_t)n_heads, (uint32_t)bph, FastDiv((uint32_t)bph),
                                                             scale_f32, (uint32_t)TB, (uint32_t)n_tiles, sym_rows,
                                                             coset_words, tile_n0, hist, deq, q_out, err);
     return check_launch();
 }
 
-template <int DT>
+template <int DT, bool QO>
 int dispatch_deq(int deq_dtype, const void *x, int64_t n_chunks, int64_t n_heads, int64_t bph, const float *sc,
                  int64_t TB, int16_t *sym_rows, uint32_t *cw, uint32_t *tn0, uint32_t *hist, void *deq, float *q_out,
                  uint32_t *err, cudaStream_t st) {
     if (deq == nullptr)
-        return launch_quantize<DT, -1>(x, n_chunks, n_heads, bph, sc, TB, sym_rows, cw, tn0, hist, deq, q_out, err,
-                                       st);
+        return launch_quantize<DT, -1, QO>(x, n_chunks, n_heads, bph, sc, TB, sym_rows, cw, tn0, hist, deq, q_out,
+                                           err, st);
     switch (deq_dtype) {
         case LQ_F32:
-            return launch_quantize<DT, LQ_F32>(x, n_chunks, n_heads, bph, sc, TB, sym_rows, cw, tn0, hist, deq, q_out,
-                                               err, st);
+            return launch_quantize<DT, LQ_F32, QO>(x, n_chunks, n_heads, bph, sc, TB, sym_rows, cw, tn0, hist, deq,
+                                                   q_out, err, st);
         case LQ_F16:
-            return launch_quantize<DT, LQ_F16>(x, n_chunks, n_heads, bph, sc, TB, sym_rows, cw, tn0, hist, deq, q_out,
-                                               err, st);
+            return launch_quantize<DT, LQ_F16, QO>(x, n_chunks, n_heads, bph, sc, TB, sym_rows, cw, tn0, hist, deq,
+                                                   q_out, err, st);
         case LQ_BF16:
-            return launch_quantize<DT, LQ_BF16>(x, n_chunks, n_heads, bph, sc, TB, sym_rows, cw, tn0, hist, deq,
-                                                q_out, err, st);
+            return launch_quantize<DT, LQ_BF16, QO>(x, n_chunks, n_heads, bph, sc, TB, sym_rows, cw, tn0, hist, deq,
+                                                    q_out, err, st);
         default:
             return LQ_ERR_INVALID;
     }
 }
 
+template <int DT>
+int dispatch_q(int deq_dtype, const void *x, int64_t n_chunks, int64_t n_heads, int64_t bph, const float *sc,
+               int64_t TB, int16_t *sym_rows, uint32_t *cw, uint32_t *tn0, uint32_t *hist, void *deq, float *q_out,
+               uint32_t *err, cudaStream_t st) {
+    return q_out ? dispatch_deq<DT, true>(deq_dtype, x, n_chunks, n_heads, bph, sc, TB, sym_rows, cw, tn0, hist, deq,
+                                          q_out, err, st)
+                 : dispatch_deq<DT, false>(deq_dtype, x, n_chunks, n_heads, bph, sc, TB, sym_rows, cw, tn0, hist, deq,
+                                           q_out, err, st);
+}
+
 __global__ void encode_e8_kernel(const float *__restrict__ x, int64_t n, float *__restrict__ out, int d8_only) {
     const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= n) return;
-    float v[8], q[8];
+    float v[8], q[8], res[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = x[8 * b + i];
-    if (d8_only) d8_nearest(v, q);
+    if (d8_only) d8_nearest(v, q, res);
     else e8_nearest(v, q);
 #pragma unroll
     for (int i = 0; i < 8; ++i) out[8 * b + i] = q[i];
@@ -207,13 +221,13 @@ extern "C" int lq_e8_quantize(const void *x, int dtype, int64_t n_chunks, int64_
         return LQ_ERR_CUDA;
     switch (dtype) {
         case LQ_F32:
-            return lq::dispatch_deq<LQ_F32>(deq_dtype, x, n_chunks, n_heads, bph, scale_f32, tile_blocks, sym_rows,
+            return lq::dispatch_q<LQ_F32>(deq_dtype, x, n_chunks, n_heads, bph, scale_f32, tile_blocks, sym_rows,
                                             coset_words, tile_n0, hist, deq, q_out, err, st);
         case LQ_F16:
-            return lq::dispatch_deq<LQ_F16>(deq_dtype, x, n_chunks, n_heads, bph, scale_f32, tile_blocks, sym_rows,
+            return lq::dispatch_q<LQ_F16>(deq_dtype, x, n_chunks, n_heads, bph, scale_f32, tile_blocks, sym_rows,
                                             coset_words, tile_n0, hist, deq, q_out, err, st);
         case LQ_BF16:
-            return lq::dispatch_deq<LQ_BF16>(deq_dtype, x, n_chunks, n_heads, bph, scale_f32, tile_blocks, sym_rows,
+            return lq::dispatch_q<LQ_BF16>(deq_dtype, x, n_chunks, n_heads, bph, scale_f32, tile_blocks, sym_rows,
                                              coset_words, tile_n0, hist, deq, q_out, err, st);
         default:
             return LQ_ERR_INVALID;
