@@ -116,8 +116,9 @@ int lq_head_scales_static(const void *x, int dtype, int64_t n_heads_total, int64
  * -> pack_coset_bits (llm/compressed_kv_cache.py:46-54), plus the per-stream
  * counts that feed build_rans_table (:236-253).
  *   scale_f32    [n_chunks][n_heads]
- *   sym_rows     [n_chunks][n_tiles][TB][8] int16: in each tile, coset-0
- *                blocks in block order, then coset-1 blocks in reverse order
+ *   sym_rows     [n_chunks][n_tiles][8][TB] int16: per tile and coordinate
+ *                a column holding the coset-0 blocks' symbols in block order
+ *                from the front and the coset-1 blocks' from the back
  *   coset_words  [n_chunks][ceil(N/32)] u32, bit i of word w = block 32w+i
  *   tile_n0      [n_chunks][n_tiles] number of coset-0 blocks per tile
  *   hist         [n_chunks][16][LQ_HIST_BINS] u32, zeroed by this call

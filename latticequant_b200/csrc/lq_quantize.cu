@@ -11,10 +11,9 @@
 // lane: a 16-byte (or 2x16-byte for fp32) load of the block, the E8 search
 // in registers, and per step one ballot that is directly the 32-bit word of
 // the packed coset bitmap.  The ballot also ranks each block inside its
-// coset, which places its 8 symbols as one 16-byte row of the tile's
-// symbol buffer: coset-0 rows from the front in block order, coset-1 rows
-// from the back -- so each rANS lane later reads its symbols contiguously,
-// last symbol first.  Symbol counts go to a shared-memory histogram per CTA
+// coset, which places its 8 symbols in the tile's 8 coordinate columns:
+// coset-0 blocks from the front in block order, coset-1 blocks from the back
+// -- so each rANS lane later reads its symbols contiguously, 8 at a time.  Symbol counts go to a shared-memory histogram per CTA
 // (values in [-128, 128)), falling back to global atomics outside that
 // window, and are flushed once per CTA.
 #include "lq_common.cuh"
@@ -53,7 +52,7 @@ __global__ void __launch_bounds__(32 * kQWarps, 4) quantize_kernel(
         const uint32_t b0 = tile * TB;
         const uint32_t tb = (b0 + TB <= N) ? TB : N - b0;
         const int64_t cblk0 = (int64_t)chunk * N;  // first block of the chunk
-        int16_t *rows = sym_rows + ((int64_t)chunk * n_tiles + tile) * TB * 8;
+        int16_t *cols = sym_rows + ((int64_t)chunk * n_tiles + tile) * TB * 8;  // [8][TB] coordinate columns
         const float *sc_chunk = scale_f32 + (int64_t)chunk * n_heads;
         uint32_t *cw = coset_words + (int64_t)chunk * words_per_chunk + b0 / 32;
         // per-thread position: block b = b0 + off + lane lives in head `head`, at `rem` within it
@@ -99,12 +98,8 @@ __global__ void __launch_bounds__(32 * kQWarps, 4) quantize_kernel(
             const uint32_t lt = (1u << lane) - 1u;
             if (active) {
                 const uint32_t row = coset ? tb - 1 - (n1 + __popc(ball & lt)) : n0 + __popc(act & ~ball & lt);
-                uint4 packed;
-                packed.x = (uint32_t)(uint16_t)sym[0] | ((uint32_t)(uint16_t)sym[1] << 16);
-                packed.y = (uint32_t)(uint16_t)sym[2] | ((uint32_t)(uint16_t)sym[3] << 16);
-                packed.z = (uint32_t)(uint16_t)sym[4] | ((uint32_t)(uint16_t)sym[5] << 16);
-                packed.w = (uint32_t)(uint16_t)sym[6] | ((uint32_t)(uint16_t)sym[7] << 16);
-                reinterpret_cast<uint4 *>(rows)[row] = packed;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) cols[i * TB + row] = (int16_t)sym[i];
                 const uint32_t sh = hist_base + (uint32_t)coset * (8 * kSmemBins * 4);
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {

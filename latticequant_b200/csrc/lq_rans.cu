@@ -32,19 +32,39 @@ namespace {
 // From x in [L, 2L): k = k0 + (x >> k0 >= 2f) bits leave (the k low bits of
 // x), then x' = (x >> k) + L + cf - f.  The k bits are prepended to a 32-bit
 // accumulator; full words are written toward the front of the lane's slot.
-__global__ void __launch_bounds__(256) encode_lanes_kernel(
-    const int16_t *__restrict__ sym_rows, const uint32_t *__restrict__ tile_n0, uint32_t n_lanes, uint32_t n_tiles,
-    uint32_t N, uint32_t TB, const int32_t *__restrict__ tab_lo, const int32_t *__restrict__ tab_nsym,
+//
+// A CTA takes kEncTiles tiles of one chunk (16 lanes each) and stages the
+// chunk's 16 coder tables (64 KB) in shared memory.  Each lane reads its
+// symbols from its coordinate column of the tile (lq_e8_quantize's
+// lane-major layout): coset-0 lanes walk the coset-0 prefix backward,
+// coset-1 lanes the coset-1 suffix forward, 8 symbols per 16-byte load once
+// aligned (a coset-0 lane reverses each loaded vector).
+constexpr int kEncTiles = 32;
+constexpr size_t kEncSmem = (size_t)LQ_NSTREAMS * LQ_L * 4;
+
+__device__ __forceinline__ uint4 reverse8(uint4 u) {
+    return make_uint4(__byte_perm(u.w, 0, 0x1032), __byte_perm(u.z, 0, 0x1032), __byte_perm(u.y, 0, 0x1032),
+                      __byte_perm(u.x, 0, 0x1032));
+}
+
+__global__ void __launch_bounds__(16 * kEncTiles, 2) encode_lanes_kernel(
+    const int16_t *__restrict__ sym_lanes, const uint32_t *__restrict__ tile_n0, uint32_t n_tiles, uint32_t N,
+    uint32_t TB, const int32_t *__restrict__ tab_lo, const int32_t *__restrict__ tab_nsym,
     const uint32_t *__restrict__ enc_tab, uint32_t *__restrict__ scratch, uint32_t slot_words,
     uint32_t *__restrict__ lane_nbits, uint32_t *__restrict__ lane_state, uint32_t *__restrict__ lane_nwords,
     uint32_t *err) {
-    const uint32_t lg = blockIdx.x * blockDim.x + threadIdx.x;
-    if (lg >= n_lanes) return;
-    const uint32_t per_chunk = n_tiles * LQ_NSTREAMS;
-    const uint32_t chunk = lg / per_chunk;
-    const uint32_t rem = lg - chunk * per_chunk;
-    const uint32_t tile = rem >> 4;
-    const uint32_t s = rem & 15u, c = s >> 3, idx = s & 7u;
+    extern __shared__ __align__(16) uint32_t etab[];
+    const uint32_t chunk = blockIdx.y;
+    {
+        const uint4 *src = reinterpret_cast<const uint4 *>(enc_tab + (size_t)chunk * LQ_NSTREAMS * LQ_L);
+        uint4 *dst = reinterpret_cast<uint4 *>(etab);
+        for (int i = threadIdx.x; i < LQ_NSTREAMS * LQ_L / 4; i += blockDim.x) dst[i] = __ldg(src + i);
+    }
+    __syncthreads();
+    const uint32_t tile = blockIdx.x * kEncTiles + (threadIdx.x >> 4);
+    if (tile >= n_tiles) return;
+    const uint32_t s = threadIdx.x & 15u, c = s >> 3, idx = s & 7u;
+    const uint32_t lg = (chunk * n_tiles + tile) * LQ_NSTREAMS + s;
     const uint32_t tb = (tile * TB + TB <= N) ? TB : N - tile * TB;
     const uint32_t n0 = tile_n0[chunk * n_tiles + tile];
     const int n = (int)(c ? tb - n0 : n0);
@@ -61,56 +81,52 @@ __global__ void __launch_bounds__(256) encode_lanes_kernel(
             lane_nwords[lg] = 0;
             return;
         }
-        const uint32_t *enc = enc_tab + (size_t)tabi * LQ_L;
-        // symbols in reverse order: coset 0 at rows n0-1 .. 0, coset 1 at rows n0 .. tb-1.
-        // Batches of 8: the next batch's 8 row loads are in flight while this one is coded;
-        // prefetch rows past the lane's end are clamped into the tile.
-        const int16_t *rows = sym_rows + ((size_t)chunk * n_tiles + tile) * TB * 8 + idx;
-        const int r0 = c ? (int)n0 : (int)n0 - 1;
-        const int dr = c ? 1 : -1;
-        const int rlo = 0, rhi = (int)tb - 1;
-        auto row_at = [&](int j) {
-            const int r = r0 + dr * j;
-            return (int)rows[8 * (r < rlo ? rlo : (r > rhi ? rhi : r))];
-        };
-        int sv[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) sv[i] = row_at(i);
-        uint32_t acc = 0, cnt = 0;
+        const uint32_t tab = smem_addr(etab) + s * (LQ_L * 4);
+        const int16_t *col = sym_lanes + ((size_t)chunk * n_tiles + tile) * TB * 8 + (size_t)idx * TB;
+        uint32_t acc = 0, cnt = 0, bad = 0;
         uint32_t *const out_end = out;
-        auto code = [&](uint32_t e) {
+        auto code = [&](int v) {
+            const uint32_t si = (uint32_t)(v - lo);
+            bad |= si >= (uint32_t)nsym ? 1u : 0u;
+            const uint32_t e = lds_u32(tab + ((si & (LQ_L - 1)) << 2));
             const uint32_t twof = e & 0xfffu, k0 = (e >> 12) & 0xfu;
             const uint32_t k = k0 + ((x >> k0) >= twof ? 1u : 0u);
-            const uint32_t v = x & ~(0xffffffffu << k);
-            acc |= v << cnt;
+            const uint32_t w = x & ~(0xffffffffu << k);
+            acc |= w << cnt;
             const uint32_t t = cnt + k;
             if (t >= 32u) {
                 *--out = acc;
-                acc = v >> (32u - cnt);
+                acc = w >> (32u - cnt);
             }
             cnt = t & 31u;
             x = (x >> k) + (e >> 16);
         };
-        auto entry = [&](int v) {
-            const int si = min(max(v - lo, 0), nsym - 1);  // nearest alphabet entry
-            return __ldg(enc + si);
-        };
-        int j0 = 0;
-        for (; j0 + 8 <= n; j0 += 8) {
-            int sn[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) sn[i] = row_at(j0 + 8 + i);
-            uint32_t e[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) e[i] = entry(sv[i]);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) code(e[i]);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) sv[i] = sn[i];
+        // symbol j (coding order) sits at col[n0 + j] (coset 1) or col[n0 - 1 - j] (coset 0)
+        auto sym_at = [&](int j) { return (int)col[c ? (int)n0 + j : (int)n0 - 1 - j]; };
+        const int head = min(n, c ? (int)((8u - (n0 & 7u)) & 7u) : (int)(((n0 - 1u) & 7u) + 1u) & 7);
+        int j = 0;
+        for (; j < head; ++j) code(sym_at(j));
+        if (j + 8 <= n) {
+            const uint4 *vp = reinterpret_cast<const uint4 *>(col + (c ? (int)n0 + j : (int)n0 - 1 - j - 7));
+            const int step = c ? 1 : -1;
+            uint4 cur = __ldg(vp);
+            for (; j + 8 <= n; j += 8) {
+                vp += step;
+                const uint4 nxt = (j + 16 <= n) ? __ldg(vp) : cur;
+                const uint4 u = c ? cur : reverse8(cur);
+                code((int16_t)(u.x & 0xffffu));
+                code((int16_t)(u.x >> 16));
+                code((int16_t)(u.y & 0xffffu));
+                code((int16_t)(u.y >> 16));
+                code((int16_t)(u.z & 0xffffu));
+                code((int16_t)(u.z >> 16));
+                code((int16_t)(u.w & 0xffffu));
+                code((int16_t)(u.w >> 16));
+                cur = nxt;
+            }
         }
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-            if (j0 + i < n) code(entry(sv[i]));
+        for (; j < n; ++j) code(sym_at(j));
+        if (bad) raise_flag(err, LQ_EF_SYMRANGE);
         nbits = 32u * (uint32_t)(out_end - out) + cnt;
         if (cnt) *--out = acc;
     }
@@ -520,6 +536,7 @@ extern "C" int lq_rans_encode(const int16_t *sym_rows, const uint32_t *tile_n0, 
     if (!sym_rows || !tile_n0 || !tab_lo || !tab_nsym || !enc_tab || !words || !lane_nbits || !lane_state ||
         !workspace)
         return LQ_ERR_INVALID;
+    if (reinterpret_cast<uintptr_t>(sym_rows) & 15) return LQ_ERR_INVALID;  // 16-byte symbol loads
     if (workspace_bytes < lq_rans_encode_workspace(n_chunks, n_vectors, tile_blocks)) return LQ_ERR_CAPACITY;
     const int64_t n_tiles = ceil_div(n_vectors, tile_blocks);
     const int64_t n_lanes = n_chunks * n_tiles * LQ_NSTREAMS;
@@ -529,9 +546,13 @@ extern "C" int lq_rans_encode(const int16_t *sym_rows, const uint32_t *tile_n0, 
     size_t off = ((sizeof(uint32_t) * (size_t)(n_lanes * sw + n_lanes)) + 15) & ~(size_t)15;
     uint64_t *bsum = reinterpret_cast<uint64_t *>(static_cast<char *>(workspace) + off);
     const int64_t nblk = ceil_div(n_lanes, kScanTile);
-    encode_lanes_kernel<<<(unsigned)ceil_div(n_lanes, 256), 256, 0, st>>>(
-        sym_rows, tile_n0, (uint32_t)n_lanes, (uint32_t)n_tiles, (uint32_t)n_vectors, (uint32_t)tile_blocks, tab_lo,
-        tab_nsym, enc_tab, scratch, (uint32_t)sw, lane_nbits, lane_state, nwords, err);
+    if (n_chunks > 65535) return LQ_ERR_INVALID;
+    if (cudaFuncSetAttribute(encode_lanes_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kEncSmem) !=
+        cudaSuccess)
+        return LQ_ERR_CUDA;
+    encode_lanes_kernel<<<dim3((unsigned)ceil_div(n_tiles, kEncTiles), (unsigned)n_chunks), 16 * kEncTiles, kEncSmem,
+                          st>>>(sym_rows, tile_n0, (uint32_t)n_tiles, (uint32_t)n_vectors, (uint32_t)tile_blocks,
+                                tab_lo, tab_nsym, enc_tab, scratch, (uint32_t)sw, lane_nbits, lane_state, nwords, err);
     scan_reduce_kernel<<<(unsigned)nblk, kScanT, 0, st>>>(nwords, n_lanes, bsum);
     scan_blocks_kernel<<<1, kScanT, 0, st>>>(bsum, nblk);
     scan_write_kernel<<<(unsigned)nblk, kScanT, 0, st>>>(nwords, n_lanes, bsum, lane_off, words_cap, err);
