@@ -45,6 +45,12 @@ UNIT = "Gvec/s"
 # config 3 (fused dequant + decode attention)
 A_B, A_HKV, A_G, A_S, A_D = 16, 8, 4, 32768, 128
 A_METRIC = "fused dequant-attn HBM GB/s"
+# DRAM bytes (read + write) per E8 block of each codec phase and per
+# compressed byte of the attention kernel, measured with ncu
+# (dram__bytes_read.sum + dram__bytes_write.sum) on the 8-layer config-2 case
+# and the full config-3 step; scaled to each launch for roofline.traffic.
+TRAFFIC_PER_BLOCK = {"scales": 16.0, "quantize": 32.1, "encode": 30.0, "decode": 20.2}
+ATTN_TRAFFIC_PER_ALG_BYTE = 600.3 / 582.0
 
 
 def make_cache(gen_device, seed, n_layers=N_LAYERS):
@@ -300,7 +306,8 @@ def bench_attention(dev, rank, world, steps, warmup, barrier):
                        "l2": "compressed K+V larger than L2"},
             "roofline": {"bound": "hbm", "kernel": "attn_partial_kernel + attn_combine_kernel", "achieved": achieved,
                          "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind,
-                         "traffic": None, "kernel_ms": k_ms},
+                         "traffic": local_bytes * ATTN_TRAFFIC_PER_ALG_BYTE / 1e9, "traffic_unit": "GB per launch",
+                         "algorithmic_GB": local_bytes / 1e9, "kernel_ms": k_ms},
             "e2e": {"value": tot_bytes / (ems * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ems,
                     "h2d_bytes_per_step": q.numel() * 2, "d2h_bytes_per_step": rows * A_D * 2},
             "gpu_launches": steps * (2 + (1 if world > 1 else 0)), "cpu_baseline": cpu}
@@ -528,7 +535,9 @@ def main():
                 "bits_per_dim": comp_bytes * 8 / (BLOCKS * 8),
                 "phase_ms": {n: round(acc[n], 4) for n in names},
                 "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
-                             "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None},
+                             "frac": achieved / peak, "peak_kind": peak_kind,
+                             "traffic": (TRAFFIC_PER_BLOCK[dom] * BLOCKS / 1e9) if dom in TRAFFIC_PER_BLOCK else None,
+                             "traffic_unit": "GB per launch", "algorithmic_GB": alg[dom] / 1e9},
                 "clocks": clocks, "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
                 "cpu_baseline": cpu, "attention": attn}
         print(json.dumps(line), flush=True)
