@@ -193,12 +193,18 @@ int lq_rans_decode(const uint32_t *words, int64_t n_words, const uint32_t *lane_
  * SDPA with repeat_kv: for every batch b and query head h,
  *   o[b][h] = softmax(q[b][h] . K[b][h/G]^T * sm_scale) V[b][h/G]
  * with K, V = symbols_to_e8 * fp16 head scale, never materialised.
+ *   geometry   batch B, n_kv_heads Hkv, seq_len S tokens, head_dim 64/128;
+ *              scale_per_token = 0: the chunks hold B*Hkv heads of S*head_dim/8
+ *              blocks with one scale per head (a prefill chunk);
+ *              scale_per_token = 1: they hold B*Hkv*S heads of head_dim/8
+ *              blocks, one scale per token (decode appends encoded together,
+ *              each token keeping the scale the reference gives it alone)
  *   q          [B][Hkv*group][head_dim] in q_dtype (16-byte aligned)
  *   out        [B][Hkv*group][head_dim] in out_dtype
  *   lse        optional [B][Hkv*group] fp32 ln(sum_t exp(s_t)), the form
  *              lq_attn_merge combines across key sets (sequence shards)
  *   workspace  lq_attn_decode_workspace() bytes (per-CTA partials)
- * Needs head_dim 64 or 128, group 1..8, tile_blocks dividing bph.
+ * Needs head_dim 64 or 128, group 1..8, tile_blocks dividing S*head_dim/8.
  * ---------------------------------------------------------------------- */
 typedef struct lq_chunk_view {
     const uint32_t *words;
@@ -213,9 +219,10 @@ typedef struct lq_chunk_view {
 } lq_chunk_view;
 
 size_t lq_attn_decode_workspace(int64_t n_heads, int64_t bph, int64_t tile_blocks, int group, int head_dim);
-int lq_attn_decode(const lq_chunk_view *k, const lq_chunk_view *v, const void *q, int q_dtype, int64_t n_kv_heads,
-                   int group, int head_dim, float sm_scale, void *out, int out_dtype, float *lse, void *workspace,
-                   size_t workspace_bytes, uint32_t *err, void *stream);
+int lq_attn_decode(const lq_chunk_view *k, const lq_chunk_view *v, const void *q, int q_dtype, int64_t batch,
+                   int64_t n_kv_heads, int64_t seq_len, int scale_per_token, int group, int head_dim, float sm_scale,
+                   void *out, int out_dtype, float *lse, void *workspace, size_t workspace_bytes, uint32_t *err,
+                   void *stream);
 
 /* Merge attention parts over disjoint key sets (the all-gathered sequence
  * shards, or several chunks of one layer): o = sum_i o_i exp(lse_i - lse),

@@ -80,18 +80,33 @@ class DecodeAttention:
     workspace and error word allocated once, launches without host syncs (so
     a decode step can be captured in a CUDA graph); flags() reads the error word."""
 
-    def __init__(self, k_chunk: LaneChunk, v_chunk: LaneChunk, group: int):
+    def __init__(self, k_chunk: LaneChunk, v_chunk: LaneChunk, group: int, shape: Optional[Tuple[int, ...]] = None,
+                 scale_per_token: bool = False):
+        """shape: the attention geometry (B, Hkv, S, D); by default the chunks'
+        tensor shape.  scale_per_token: the chunks were compressed from the
+        (B, Hkv*S, 1, D) view, i.e. with one scale per token (decode appends)."""
         kshape, vshape = tuple(k_chunk.orig_shape), tuple(v_chunk.orig_shape)
         if len(kshape) != 4 or kshape != vshape:
-            raise ValueError("K and V chunks must hold (B, Hkv, S, D) tensors of one shape")
-        self.shape = kshape
+            raise ValueError("K and V chunks must hold tensors of one 4-d shape")
+        if shape is None:
+            if scale_per_token:
+                raise ValueError("per-token chunks need the attention shape")
+            shape = kshape
+        shape = tuple(int(d) for d in shape)
+        B, Hkv, S, D = shape
+        if scale_per_token and kshape != (B, Hkv * S, 1, D):
+            raise ValueError(f"per-token chunk shape {kshape} does not match {shape}")
+        if not scale_per_token and kshape != shape:
+            raise ValueError(f"chunk shape {kshape} does not match {shape}")
+        self.shape = shape
+        self.scale_per_token = bool(scale_per_token)
         self.group = int(group)
         self.k, self.v = k_chunk, v_chunk
         self.kv, self.vv = chunk_view(k_chunk), chunk_view(v_chunk)
-        need = attention_workspace_bytes(k_chunk, self.group)
+        need = int(lib().lq_attn_decode_workspace(B * Hkv, S * D // 8, k_chunk.geom.tile_blocks, self.group, D))
         if need == 0:
-            raise ValueError(f"fused attention does not take head_dim={kshape[3]}, group={group}, "
-                             f"tile_blocks={k_chunk.geom.tile_blocks} with {k_chunk.geom.bph} blocks per head")
+            raise ValueError(f"fused attention does not take head_dim={D}, group={group}, "
+                             f"tile_blocks={k_chunk.geom.tile_blocks} with {S * D // 8} blocks per head")
         dev = k_chunk.words.device
         self.workspace = torch.empty(need, dtype=torch.uint8, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -102,9 +117,9 @@ class DecodeAttention:
         if sm_scale is None:
             sm_scale = 1.0 / math.sqrt(D)
         check(lib().lq_attn_decode(ctypes.byref(self.kv), ctypes.byref(self.vv), ptr(q3), _lib.dtype_code(q3.dtype),
-                                   Hkv, self.group, D, float(sm_scale), ptr(out), _lib.dtype_code(out.dtype),
-                                   ptr(lse), ptr(self.workspace), self.workspace.numel(), ptr(self.err),
-                                   stream_handle(q3.device)), "lq_attn_decode")
+                                   B, Hkv, S, int(self.scale_per_token), self.group, D, float(sm_scale), ptr(out),
+                                   _lib.dtype_code(out.dtype), ptr(lse), ptr(self.workspace), self.workspace.numel(),
+                                   ptr(self.err), stream_handle(q3.device)), "lq_attn_decode")
 
     def flags(self) -> int:
         return int(self.err.item()) & 0xFFFFFFFF

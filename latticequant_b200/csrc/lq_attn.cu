@@ -37,7 +37,9 @@ constexpr float kLn2 = 0.6931471805599453f;
 struct AttnArgs {
     ChunkDev k, v;
     const void *q;        // [B][Hkv*G][D] in q dtype
-    uint32_t n_kv_heads;  // heads of the chunk = B * n_kv_heads
+    uint32_t n_kv_heads;  // attention heads = B * n_kv_heads
+    uint32_t seq;         // tokens per attention head
+    uint32_t scale_tok;   // 0: one scale per head (scale[head]); 1: one per token (scale[head * seq + t])
     uint32_t tph;         // tiles per head
     uint32_t n_pairs;     // tile pairs per head
     uint32_t nct;         // CTAs per head
@@ -127,8 +129,14 @@ __global__ void __launch_bounds__(attn_threads<G, BPT>(), 1) attn_partial_kernel
     __syncwarp();
 
     // ---- softmax statistics of this warp's tokens (base 2)
-    const float ck = __half2float(__ushort_as_half(a.k.scale_f16[head])) * a.qk_log2;
+    const float ck = a.scale_tok ? a.qk_log2 : __half2float(__ushort_as_half(a.k.scale_f16[head])) * a.qk_log2;
     const uint32_t ntok = 2 * a.tpt;
+    // per-token scales: token i of the warp is token (2*pair + i/tpt)*tpt + i%tpt of the head
+    auto tok_scale = [&](const uint16_t *sc16, uint32_t i) {
+        const uint32_t t = i < a.tpt ? 0u : 1u;
+        const uint32_t tok = (2 * pair + t) * a.tpt + (i - t * a.tpt);
+        return __half2float(__ushort_as_half(sc16[(size_t)head * a.seq + tok]));
+    };
     float m[G], l[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
@@ -138,8 +146,12 @@ __global__ void __launch_bounds__(attn_threads<G, BPT>(), 1) attn_partial_kernel
     for (uint32_t i = lane; i < ntok; i += 32) {
         const bool v = i < a.tpt ? act0 : act1;
         if (!v) continue;
+        const float cki = a.scale_tok ? ck * tok_scale(a.k.scale_f16, i) : ck;
 #pragma unroll
-        for (int g = 0; g < G; ++g) m[g] = fmaxf(m[g], sc[i * GP + g] * ck);
+        for (int g = 0; g < G; ++g) {
+            sc[i * GP + g] *= cki;
+            m[g] = fmaxf(m[g], sc[i * GP + g]);
+        }
     }
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) {
@@ -149,10 +161,12 @@ __global__ void __launch_bounds__(attn_threads<G, BPT>(), 1) attn_partial_kernel
     for (uint32_t i = lane; i < ntok; i += 32) {
         const bool v = i < a.tpt ? act0 : act1;
         if (!v) continue;
+        // with per-token V scales the token's scale rides on its weight p
+        const float cvi = a.scale_tok ? tok_scale(a.v.scale_f16, i) : 1.0f;
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-            const float p = exp2f(sc[i * GP + g] * ck - m[g]);
-            sc[i * GP + g] = p;
+            const float p = exp2f(sc[i * GP + g] - m[g]);
+            sc[i * GP + g] = p * cvi;
             l[g] += p;
         }
     }
@@ -224,7 +238,7 @@ __global__ void __launch_bounds__(attn_threads<G, BPT>(), 1) attn_partial_kernel
         }
     }
     __syncthreads();
-    const float cv = __half2float(__ushort_as_half(a.v.scale_f16[head]));
+    const float cv = a.scale_tok ? 1.0f : __half2float(__ushort_as_half(a.v.scale_f16[head]));
     float *out = a.part + ((size_t)head * a.nct + blockIdx.x) * G * rs;
     for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
         const int g = e / D, dd = e % D;
@@ -389,15 +403,21 @@ extern "C" size_t lq_attn_decode_workspace(int64_t n_heads, int64_t bph, int64_t
 }
 
 extern "C" int lq_attn_decode(const lq_chunk_view *k, const lq_chunk_view *v, const void *q, int q_dtype,
-                              int64_t n_kv_heads, int group, int head_dim, float sm_scale, void *out, int out_dtype,
-                              float *lse, void *workspace, size_t workspace_bytes, uint32_t *err, void *stream) {
-    if (!view_ok(k) || !view_ok(v) || !q || !out || !workspace || n_kv_heads <= 0) return LQ_ERR_INVALID;
+                              int64_t batch, int64_t n_kv_heads, int64_t seq_len, int scale_per_token, int group,
+                              int head_dim, float sm_scale, void *out, int out_dtype, float *lse, void *workspace,
+                              size_t workspace_bytes, uint32_t *err, void *stream) {
+    if (!view_ok(k) || !view_ok(v) || !q || !out || !workspace || batch <= 0 || n_kv_heads <= 0 || seq_len <= 0)
+        return LQ_ERR_INVALID;
     if (k->n_heads != v->n_heads || k->bph != v->bph || k->tile_blocks != v->tile_blocks) return LQ_ERR_INVALID;
-    if (k->n_heads % n_kv_heads != 0) return LQ_ERR_INVALID;
+    if (head_dim != 64 && head_dim != 128) return LQ_ERR_INVALID;
+    const int64_t heads = batch * n_kv_heads, bph = seq_len * (head_dim / 8);
+    if (scale_per_token ? (k->n_heads != heads * seq_len || k->bph != head_dim / 8)
+                        : (k->n_heads != heads || k->bph != bph))
+        return LQ_ERR_INVALID;
     if ((reinterpret_cast<uintptr_t>(q) & 15) || (reinterpret_cast<uintptr_t>(workspace) & 15)) return LQ_ERR_INVALID;
     if (!(sm_scale > 0.f) || !isfinite(sm_scale)) return LQ_ERR_INVALID;
     AttnPlan p;
-    const int rc = attn_plan(k->n_heads, k->bph, k->tile_blocks, group, head_dim, &p);
+    const int rc = attn_plan(heads, bph, k->tile_blocks, group, head_dim, &p);
     if (rc != LQ_OK) return rc;
     if (workspace_bytes < p.part_floats * 4) return LQ_ERR_CAPACITY;
     if (out_dtype != LQ_F32 && out_dtype != LQ_F16 && out_dtype != LQ_BF16) return LQ_ERR_INVALID;
@@ -407,6 +427,8 @@ extern "C" int lq_attn_decode(const lq_chunk_view *k, const lq_chunk_view *v, co
     a.v = to_dev(v);
     a.q = q;
     a.n_kv_heads = (uint32_t)n_kv_heads;
+    a.seq = (uint32_t)seq_len;
+    a.scale_tok = scale_per_token ? 1u : 0u;
     a.tph = p.tph;
     a.n_pairs = p.n_pairs;
     a.nct = p.nct;
@@ -416,7 +438,7 @@ extern "C" int lq_attn_decode(const lq_chunk_view *k, const lq_chunk_view *v, co
     a.qk_log2 = sm_scale * kLog2e;
     a.part = static_cast<float *>(workspace);
     a.err = err;
-    const uint32_t nh = (uint32_t)k->n_heads;
+    const uint32_t nh = (uint32_t)heads;
     int r;
     switch (group) {
         case 1: r = launch_partial_g<1>(a, p, nh, q_dtype, head_dim, st); break;
@@ -430,7 +452,7 @@ extern "C" int lq_attn_decode(const lq_chunk_view *k, const lq_chunk_view *v, co
         default: return LQ_ERR_INVALID;
     }
     if (r != LQ_OK) return r;
-    const unsigned rows = (unsigned)(k->n_heads * group);
+    const unsigned rows = (unsigned)(heads * group);
     const float *part = a.part;
     const uint32_t hkv = (uint32_t)n_kv_heads, G = (uint32_t)group, D = (uint32_t)head_dim;
     if (out_dtype == LQ_F32) attn_combine_kernel<LQ_F32><<<rows, D, 0, st>>>(part, hkv, G, D, p.nct, out, lse);

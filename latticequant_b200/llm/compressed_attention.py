@@ -1,0 +1,324 @@
+"""A CompressedKVCache whose decode steps attend over the compressed cache.
+
+The reference keeps a resident dequantised copy of every layer's K/V next to
+its compressed chunks (update() concatenates the new dequantised tokens and
+returns the whole buffer, llm/compressed_kv_cache.py:377-395), so its actual
+memory ratio is below 1.  ``CompressedAttentionKVCache`` keeps per layer:
+
+* the compressed chunks: a prefill chunk with one scale per (batch, KV head)
+  exactly as the reference's ``_compress_tensor`` makes it, and chunks of
+  ``tail_tokens`` decode tokens encoded together ("lazy per-tile encoding"),
+  each token keeping the scale the reference gives its own one-token chunk
+  (the tail is compressed through its (B, Hkv*T, 1, D) view, so every token
+  is a head of the chunk);
+* the tail of decode tokens not yet encoded: raw (to encode them later) and
+  dequantised with the fp32 scale, as update() returns them.
+
+A decode step (one query position) runs the fused kernel (lq_attn_decode)
+over every chunk and exact attention over the tail, then merges the parts by
+log-sum-exp (lq_attn_merge).  ``lq_compressed_attention`` is the
+transformers attention function that does this inside a model: register it
+with ``register_attention()`` and attach the cache with ``cache.bind(model)``.
+Prefill (several query positions) keeps the reference's semantics: attention
+over the dequantised K/V that update() returns.
+"""
+from __future__ import annotations
+
+import math
+from typing import List, Optional
+
+import torch
+
+from .. import attention as A
+from .. import codec
+from ..codec import LaneChunk
+from .compressed_kv_cache import CompressedKVCache, CompressedKVLayer, OptimizedChunk
+
+ATTN_NAME = "lq_compressed"
+
+
+def _attn_tile(bph: int, limit: int) -> Optional[int]:
+    """Largest tile (multiple of 32, at most `limit`) dividing the blocks per head."""
+    t = (min(limit, bph) // 32) * 32
+    while t >= 32:
+        if bph % t == 0:
+            return t
+        t -= 32
+    return None
+
+
+class _Part:
+    """One compressed (K, V) chunk pair of a layer and its prepared attention."""
+
+    def __init__(self, k: LaneChunk, v: LaneChunk, shape, per_token: bool):
+        self.k, self.v, self.shape, self.per_token = k, v, tuple(shape), per_token
+        self.ops = {}
+
+    def op(self, group: int) -> A.DecodeAttention:
+        if group not in self.ops:
+            self.ops[group] = A.DecodeAttention(self.k, self.v, group, shape=self.shape,
+                                                scale_per_token=self.per_token)
+        return self.ops[group]
+
+
+class _LayerState:
+    def __init__(self):
+        self.parts: List[_Part] = []
+        self.dense_k: List[torch.Tensor] = []  # chunks the fused kernel cannot take, kept dequantised
+        self.dense_v: List[torch.Tensor] = []
+        self.tail_raw_k = self.tail_raw_v = None
+        self.tail_deq_k = self.tail_deq_v = None
+        self.n_tail = 0
+        self.seq = 0
+
+
+class CompressedAttentionKVCache(CompressedKVCache):
+    """CompressedKVCache without the resident dequantised buffer; see the module text.
+
+      tail_tokens  decode tokens encoded together (a multiple of 2; 64 makes
+                   one 1024-block tile per (batch, KV head) at head_dim 128)
+    """
+
+    def __init__(self, bits_per_dim: int = 4, tail_tokens: int = 64,
+                 tile_blocks: Optional[int] = codec.DEFAULT_TILE_BLOCKS, table_mode: str = "device"):
+        super().__init__(bits_per_dim=bits_per_dim, eval_only_no_entropy=False, tile_blocks=tile_blocks,
+                         table_mode=table_mode)
+        if tail_tokens < 2 or tail_tokens % 2:
+            raise ValueError("tail_tokens must be an even number >= 2")
+        self.tail_tokens = int(tail_tokens)
+        self._state: List[_LayerState] = []
+
+    # ---- storage -----------------------------------------------------------
+    def _layer(self, i: int) -> _LayerState:
+        while len(self._state) <= i:
+            self._state.append(_LayerState())
+        while len(self._comp_keys) <= i:
+            self._comp_keys.append(None)
+            self._comp_values.append(None)
+        if self._comp_keys[i] is None:
+            self._comp_keys[i] = CompressedKVLayer()
+            self._comp_values[i] = CompressedKVLayer()
+        return self._state[i]
+
+    def _compress_with_tile(self, x: torch.Tensor, tile: int):
+        saved = self.tile_blocks
+        self.tile_blocks = tile
+        try:
+            return self._compress_tensor(x)
+        finally:
+            self.tile_blocks = saved
+
+    def _quantise_only(self, x: torch.Tensor) -> torch.Tensor:
+        """update()'s dequantised output for x (q * fp32 scale in x's dtype), no coding."""
+        b, h, s, d = x.shape
+        geom = codec.Geometry(1, b * h, s * d // 8, codec.round_tile(None, b * h * s * d // 8))
+        cd = codec.Codec(geom, x.device, keep_deq=True, deq_dtype=x.dtype)
+        cd.scales(x.contiguous(), self.bits)
+        cd.quantize(x.contiguous())
+        return cd.deq.view(x.shape).clone()
+
+    def update(self, key_states, value_states, layer_idx, cache_kwargs=None):
+        if self._model_dtype is None:
+            self._model_dtype = key_states.dtype
+        st = self._layer(layer_idx)
+        B, H, S, D = key_states.shape
+        if D % 8 != 0 or D not in (64, 128):
+            raise ValueError("CompressedAttentionKVCache needs head_dim 64 or 128")
+        if S > 1 or st.seq == 0:
+            return self._update_chunk(st, layer_idx, key_states, value_states)
+        return self._update_token(st, layer_idx, key_states, value_states)
+
+    def _update_chunk(self, st, layer_idx, k, v):
+        """A multi-token update: one chunk, as the reference compresses it."""
+        B, H, S, D = k.shape
+        history = self._materialise(st) if st.seq > 0 else None
+        self._flush_tail(st, layer_idx, force=True)
+        tile = _attn_tile(S * D // 8, self.tile_blocks or codec.DEFAULT_TILE_BLOCKS)
+        ck, kd = self._compress_with_tile(k, tile or 32)
+        cv, vd = self._compress_with_tile(v, tile or 32)
+        self._comp_keys[layer_idx].append_chunk(ck)
+        self._comp_values[layer_idx].append_chunk(cv)
+        if tile is not None:
+            st.parts.append(_Part(ck.lanes, cv.lanes, (B, H, S, D), per_token=False))
+        else:  # no tile divides the blocks per head: keep this chunk dequantised (fp16 scale)
+            st.dense_k.append(self._decompress_chunk(ck))
+            st.dense_v.append(self._decompress_chunk(cv))
+        st.seq += S
+        if history is not None:
+            return torch.cat([history[0], kd], 2), torch.cat([history[1], vd], 2)
+        return kd, vd
+
+    def _update_token(self, st, layer_idx, k, v):
+        """A one-token update: quantise now (update()'s output), encode with the tail later."""
+        B, H, S, D = k.shape
+        T = self.tail_tokens
+        if st.tail_raw_k is None or st.tail_raw_k.shape[:2] != (B, H):
+            st.tail_raw_k = torch.empty(B, H, T, D, dtype=k.dtype, device=k.device)
+            st.tail_raw_v = torch.empty_like(st.tail_raw_k)
+            st.tail_deq_k = torch.empty_like(st.tail_raw_k)
+            st.tail_deq_v = torch.empty_like(st.tail_raw_k)
+        kd = self._quantise_only(k)
+        vd = self._quantise_only(v)
+        i = st.n_tail
+        st.tail_raw_k[:, :, i] = k[:, :, 0]
+        st.tail_raw_v[:, :, i] = v[:, :, 0]
+        st.tail_deq_k[:, :, i] = kd[:, :, 0]
+        st.tail_deq_v[:, :, i] = vd[:, :, 0]
+        st.n_tail += 1
+        st.seq += 1
+        self.total_vectors += 2 * B * H * D // 8
+        if st.n_tail == T:
+            self._flush_tail(st, layer_idx)
+        return kd, vd
+
+    def _flush_tail(self, st, layer_idx, force=False):
+        """Encode the tail as one chunk with a scale per token (every token a head)."""
+        n = st.n_tail
+        if n == 0:
+            return
+        B, H, T, D = st.tail_raw_k.shape
+        kk = st.tail_raw_k[:, :, :n].reshape(B, H * n, 1, D)
+        vv = st.tail_raw_v[:, :, :n].reshape(B, H * n, 1, D)
+        tile = _attn_tile(n * D // 8, self.tile_blocks or codec.DEFAULT_TILE_BLOCKS)
+        saved = self.total_vectors
+        ck, _ = self._compress_with_tile(kk, tile or 32)
+        cv, _ = self._compress_with_tile(vv, tile or 32)
+        self.total_vectors = saved  # counted when the tokens arrived
+        self._comp_keys[layer_idx].append_chunk(ck)
+        self._comp_values[layer_idx].append_chunk(cv)
+        if tile is not None and not force:
+            st.parts.append(_Part(ck.lanes, cv.lanes, (B, H, n, D), per_token=True))
+        else:
+            st.dense_k.append(st.tail_deq_k[:, :, :n].clone())
+            st.dense_v.append(st.tail_deq_v[:, :, :n].clone())
+        st.n_tail = 0
+
+    def _materialise(self, st, dtype: Optional[torch.dtype] = None):
+        """Every token of a layer, dequantised (fp16 scale for chunks, fp32 for the
+        tail), in `dtype` (default: the model's)."""
+        dt = dtype or self._model_dtype
+        ks, vs = [], []
+        for p in st.parts:
+            ks.append(codec.decompress(p.k, out_dtype=dt).view(p.shape))
+            vs.append(codec.decompress(p.v, out_dtype=dt).view(p.shape))
+        ks += [t.to(dt) for t in st.dense_k]
+        vs += [t.to(dt) for t in st.dense_v]
+        if st.n_tail:
+            ks.append(st.tail_deq_k[:, :, :st.n_tail].to(dt))
+            vs.append(st.tail_deq_v[:, :, :st.n_tail].to(dt))
+        return torch.cat(ks, 2), torch.cat(vs, 2)
+
+    # ---- attention -----------------------------------------------------------
+    def decode_attention(self, layer_idx: int, query: torch.Tensor, scaling: Optional[float] = None) -> torch.Tensor:
+        """Attention of one query position over the layer's whole cache.
+
+        query (B, Hq, 1, D) -> (B, Hq, 1, D) in the query's dtype."""
+        st = self._state[layer_idx]
+        B, Hq, Q, D = query.shape
+        if Q != 1:
+            raise ValueError("decode_attention takes one query position")
+        scaling = (1.0 / math.sqrt(D)) if scaling is None else float(scaling)
+        q3 = query.reshape(B, Hq, D).contiguous()
+        o_parts, l_parts = [], []
+        for p in st.parts:
+            H = p.shape[1]
+            op = p.op(Hq // H)
+            o = torch.empty(B, Hq, D, dtype=torch.float32, device=query.device)
+            lse = torch.empty(B, Hq, dtype=torch.float32, device=query.device)
+            op(q3, o, lse, scaling)
+            o_parts.append(o)
+            l_parts.append(lse)
+        dense_k, dense_v = list(st.dense_k), list(st.dense_v)
+        if st.n_tail:
+            dense_k.append(st.tail_deq_k[:, :, :st.n_tail])
+            dense_v.append(st.tail_deq_v[:, :, :st.n_tail])
+        if dense_k:
+            k = torch.cat(dense_k, 2).float()
+            v = torch.cat(dense_v, 2).float()
+            H = k.shape[1]
+            qg = q3.float().view(B, H, Hq // H, D)
+            s = torch.einsum("bhgd,bhsd->bhgs", qg, k) * scaling
+            lse = torch.logsumexp(s, -1)
+            o = torch.einsum("bhgs,bhsd->bhgd", torch.exp(s - lse[..., None]), v)
+            o_parts.append(o.reshape(B, Hq, D))
+            l_parts.append(lse.reshape(B, Hq))
+        if len(o_parts) == 1:
+            out = o_parts[0].to(query.dtype)
+        else:
+            out, _ = A.merge_attention(o_parts, l_parts, out_dtype=query.dtype)
+        return out.view(B, Hq, 1, D)
+
+    def flags(self) -> int:
+        """OR of the fused attention kernels' error words (synchronises)."""
+        f = 0
+        for st in self._state:
+            for p in st.parts:
+                for op in p.ops.values():
+                    f |= op.flags()
+        return f
+
+    # ---- transformers glue ---------------------------------------------------
+    def bind(self, model) -> "CompressedAttentionKVCache":
+        """Point every attention module of `model` (modules with a layer_idx) at
+        this cache and switch the model to the compressed attention function."""
+        register_attention()
+        for m in model.modules():
+            if hasattr(m, "layer_idx") and hasattr(m, "num_key_value_groups"):
+                m._lq_cache = self
+        cfg = getattr(model, "config", None)
+        if cfg is not None:
+            if hasattr(model, "set_attn_implementation"):
+                model.set_attn_implementation(ATTN_NAME)
+            else:
+                cfg._attn_implementation = ATTN_NAME
+        return self
+
+    def get_seq_length(self, layer_idx=0):
+        if layer_idx < len(self._state):
+            return self._state[layer_idx].seq
+        return 0
+
+    def get_mask_sizes(self, query_length, layer_idx=0):
+        q = int(query_length.shape[0]) if torch.is_tensor(query_length) else int(query_length)
+        return self.get_seq_length(layer_idx) + q, 0
+
+    def decompressed_resident_bytes(self):
+        total = 0
+        for st in self._state:
+            for t in st.dense_k + st.dense_v + [st.tail_raw_k, st.tail_raw_v, st.tail_deq_k, st.tail_deq_v]:
+                if t is not None:
+                    total += t.nelement() * t.element_size()
+        return total
+
+
+def lq_compressed_attention(module, query, key, value, attention_mask, scaling=None, dropout=0.0, **kwargs):
+    """transformers attention function.  A decode step (one query position) of a
+    module bound to a CompressedAttentionKVCache reads the compressed cache;
+    every other call runs SDPA over the K/V it is given (what update()
+    returned: the dequantised tokens)."""
+    cache = getattr(module, "_lq_cache", None)
+    st = None
+    if cache is not None and query.shape[2] == 1 and module.layer_idx < len(cache._state):
+        st = cache._state[module.layer_idx]
+        if st.seq == 0:
+            st = None
+    if st is not None:
+        masked = attention_mask is not None and bool((attention_mask < 0).any())
+        if not masked:
+            o = cache.decode_attention(module.layer_idx, query, scaling)
+            return o.transpose(1, 2).contiguous(), None
+        key, value = cache._materialise(st)  # padding masks: attend over the dequantised cache
+    groups = query.shape[1] // key.shape[1]
+    if groups > 1:
+        key = key.repeat_interleave(groups, 1)
+        value = value.repeat_interleave(groups, 1)
+    o = torch.nn.functional.scaled_dot_product_attention(
+        query, key, value, attn_mask=attention_mask, is_causal=attention_mask is None and query.shape[2] > 1,
+        scale=scaling)
+    return o.transpose(1, 2).contiguous(), None
+
+
+def register_attention():
+    from transformers import AttentionInterface
+
+    AttentionInterface.register(ATTN_NAME, lq_compressed_attention)

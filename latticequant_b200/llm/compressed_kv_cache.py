@@ -428,3 +428,10 @@ class CompressedKVCache(DynamicCache):
         if layer_idx < len(self._comp_keys) and self._comp_keys[layer_idx] is not None:
             return self._comp_keys[layer_idx].total_seq
         return 0
+
+    def get_mask_sizes(self, query_length, layer_idx=0):
+        """(kv_length, kv_offset) for transformers' mask builders: the cached
+        tokens plus the query's (the base class reads its own layer list,
+        which this cache does not fill)."""
+        q = int(query_length.shape[0]) if torch.is_tensor(query_length) else int(query_length)
+        return self.get_seq_length(layer_idx) + q, 0

