@@ -233,6 +233,16 @@ int lq_attn_merge(const float *o_parts, const float *lse_parts, int64_t n_parts,
                   void *out, int out_dtype, float *lse, void *stream);
 
 /* ------------------------------------------------------------------------
+ * Randomized Hadamard transform (core/pipeline.py:33-122) on fp32 vectors
+ * of length d (a power of two, 2..4096):
+ *   out = (FWHT(x * pre_signs) / sqrt(d)) * post_signs
+ * with either sign vector NULL: pre_signs for RHT.forward, post_signs for
+ * RHT.inverse, neither for fast_hadamard_transform.  Bit-exact with torch.
+ * ---------------------------------------------------------------------- */
+int lq_fwht(const float *x, int64_t n_vec, int d, const float *pre_signs, const float *post_signs, float *out,
+            void *stream);
+
+/* ------------------------------------------------------------------------
  * Reference-stream decode: the argument meaning of _rans_decode_kernel
  * (core/gpu_ans.py:175-235) as prepared by prepare_gpu_decode (:274-342):
  * bit offsets, n_bits, initial states, symbol counts, per-table lookup /

@@ -35,3 +35,69 @@ def symbols_to_e8(coset: torch.Tensor, free_coords: torch.Tensor, coord8_half: t
     q = torch.empty(n, 8, dtype=torch.float32, device=dev)
     check(lib().lq_symbols_to_e8(ptr(cos), ptr(sym), n, ptr(q), stream_handle(dev)), "symbols_to_e8")
     return _dev.back(q, dev_out)
+
+
+# ============================================================
+# Frequency model and code-length measurement (core/entropy_coder.py:112-251)
+# ============================================================
+import numpy as np  # noqa: E402
+
+
+class FrequencyModel:
+    """Per-(coset, coordinate) symbol counts (core/entropy_coder.py:112-139);
+    host bookkeeping over numpy arrays, as the reference does it."""
+
+    def __init__(self):
+        self.tables = {}
+        self.totals = {}
+        self.coset_prob = [0.5, 0.5]
+
+    def fit(self, coset: np.ndarray, free_coords: np.ndarray, coord8_half: np.ndarray):
+        p_half = (coset == 1).mean()
+        self.coset_prob = [max(1 - p_half, 1e-30), max(p_half, 1e-30)]
+        all_symbols = np.concatenate([free_coords, coord8_half[:, None]], axis=1)
+        for c in [0, 1]:
+            mask = coset == c
+            if mask.sum() == 0:
+                continue
+            syms_c = all_symbols[mask]
+            for idx in range(8):
+                unique, counts = np.unique(syms_c[:, idx], return_counts=True)
+                self.tables[(c, idx)] = dict(zip(unique.tolist(), counts.tolist()))
+                self.totals[(c, idx)] = int(mask.sum())
+
+
+def measure_ideal_code_length(model: FrequencyModel, coset: np.ndarray, free_coords: np.ndarray,
+                              coord8_half: np.ndarray) -> dict:
+    """Laplace-smoothed ideal code length (core/entropy_coder.py:147-185)."""
+    N = len(coset)
+    total_bits = 0.0
+    n0 = (coset == 0).sum()
+    total_bits += n0 * (-np.log2(model.coset_prob[0]))
+    total_bits += (N - n0) * (-np.log2(model.coset_prob[1]))
+    all_symbols = np.concatenate([free_coords, coord8_half[:, None]], axis=1)
+    for c_val in [0, 1]:
+        mask = coset == c_val
+        if mask.sum() == 0:
+            continue
+        syms_c = all_symbols[mask]
+        total_c = model.totals.get((c_val, 0), syms_c.shape[0])
+        for idx in range(8):
+            table = model.tables.get((c_val, idx), {})
+            alphabet_size = len(table) + 1
+            unique_vals, counts = np.unique(syms_c[:, idx], return_counts=True)
+            for val, cnt in zip(unique_vals, counts):
+                prob = (table.get(int(val), 0) + 1) / (total_c + alphabet_size)
+                total_bits += cnt * (-np.log2(prob))
+    return {"total_bits": total_bits, "bits_per_dim": total_bits / (N * 8)}
+
+
+def measure_real_ans(model: FrequencyModel, coset: np.ndarray, free_coords: np.ndarray,
+                     coord8_half: np.ndarray) -> dict:
+    """Real coded size with this package's rANS on Laplace-smoothed tables (the
+    reference measures constriction's coder here, core/entropy_coder.py:191-251)."""
+    from .entropy_storage import compress_symbols
+
+    streams, _ = compress_symbols(model, np.asarray(coset), np.asarray(free_coords), np.asarray(coord8_half))
+    total_bits = 32 * sum(len(s.bitstream) for s in streams if s is not None)
+    return {"total_bits": total_bits, "bits_per_dim": total_bits / (len(coset) * 8), "status": "ok"}

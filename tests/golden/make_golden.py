@@ -23,6 +23,10 @@ inputs (torch.manual_seed / np.random.seed as the reference's tests use):
   compact.npz   pack_e8 / unpack_e8 (core/compact_storage.py:87-222) on the
                 handcrafted cases (:377-456) and a Gaussian round trip
   cache.npz     CompressedKVCache.update over a prefill + decode steps
+  rht.npz       RHT signs, fast_hadamard_transform, RHT forward / inverse and
+                LatticeQuantEncoder.encode (core/pipeline.py:33-239)
+
+    python tests/golden/make_golden.py [fixture ...]   (default: all)
 """
 import os
 import sys
@@ -40,6 +44,7 @@ import entropy_coder as ref_ec  # noqa: E402
 import gpu_ans as ref_ans  # noqa: E402
 import compact_storage as ref_cs  # noqa: E402
 import compressed_kv_cache as ref_kv  # noqa: E402
+import pipeline as ref_pipe  # noqa: E402
 
 
 def save(name, **arrs):
@@ -360,12 +365,40 @@ def cache_fixture():
     save("cache.npz", **out)
 
 
+def rht_fixture():
+    out = {}
+    # signs of RHT(d, seed) (core/pipeline.py:81-101)
+    for d in (8, 64, 128):
+        for seed in (0, 7):
+            out[f"signs_d{d}_s{seed}"] = ref_pipe.RHT(d, seed=seed).signs.numpy()
+    torch.manual_seed(3)
+    for d in (8, 64, 128, 256):
+        x = torch.randn(32, d) * torch.exp(torch.randn(32, 1))
+        out[f"fwht_x_d{d}"] = x.numpy()
+        out[f"fwht_y_d{d}"] = ref_pipe.fast_hadamard_transform(x).numpy()
+    r = ref_pipe.RHT(128, seed=0)
+    v = torch.randn(64, 128)
+    out["rht_v"] = v.numpy()
+    out["rht_w"] = r.forward(v).numpy()
+    out["rht_inv"] = r.inverse(r.forward(v)).numpy()
+    # LatticeQuantEncoder.encode (core/pipeline.py:151-205)
+    torch.manual_seed(42)
+    for bits in (3, 4, 5):
+        enc = ref_pipe.LatticeQuantEncoder(128, bits, rht_seed=0)
+        v = torch.randn(256, 128)
+        e = enc.encode(v)
+        out[f"enc{bits}_v"] = v.numpy()
+        for key in ("v_hat", "w", "w_hat", "coset", "free_coords", "coord8_half"):
+            out[f"enc{bits}_{key}"] = e[key].numpy()
+        out[f"enc{bits}_scale"] = np.float64(e["scale"])
+        out[f"enc{bits}_sigma2"] = np.float64(e["sigma2"])
+    save("rht.npz", **out)
+
+
+FIXTURES = {"e8": e8_fixture, "scales": scales_fixture, "symbols": symbols_fixture, "rans": rans_fixture,
+            "pipeline": pipeline_fixture, "chunks": chunks, "compact": compact_fixture, "cache": cache_fixture,
+            "rht": rht_fixture}
+
 if __name__ == "__main__":
-    e8_fixture()
-    scales_fixture()
-    symbols_fixture()
-    rans_fixture()
-    pipeline_fixture()
-    chunks()
-    compact_fixture()
-    cache_fixture()
+    for name in (sys.argv[1:] or list(FIXTURES)):
+        FIXTURES[name]()

@@ -4,6 +4,7 @@ The library is loaded and its exports are checked against the header; no
 compute entry point is called here.
 """
 import ctypes
+import torch
 import os
 import re
 
@@ -103,3 +104,16 @@ def test_geometry_and_capacity():
     assert g.words_capacity >= 3 * (8 * g.n_vectors * 10) // 32
     assert codec.round_tile(None, 1000) == 1024 and codec.round_tile(33, 1) == 64
     assert codec.vol_mult(4) == 4.0 ** -4
+
+
+def test_rht_signs_match_reference():
+    from latticequant_b200.core.pipeline import RHT, hadamard_matrix, to_blocks, from_blocks
+
+    g = golden("rht.npz")
+    for d in (8, 64, 128):
+        for seed in (0, 7):
+            assert np.array_equal(RHT(d, seed=seed).signs.numpy(), g[f"signs_d{d}_s{seed}"])
+    H = hadamard_matrix(8)
+    assert torch.equal(H @ H.T, 8 * torch.eye(8))
+    w = torch.arange(32.0).reshape(2, 16)
+    assert torch.equal(from_blocks(to_blocks(w)), w)
