@@ -232,6 +232,18 @@ int lq_attn_decode(const lq_chunk_view *k, const lq_chunk_view *v, const void *q
 int lq_attn_merge(const float *o_parts, const float *lse_parts, int64_t n_parts, int64_t rows, int head_dim,
                   void *out, int out_dtype, float *lse, void *stream);
 
+/* Fused merge of the compact layout with an fp16 fallback
+ * (llm/fused_triton_merge.py:33-177): for each of n_heads*bph blocks,
+ * repr_mask[k] != 0 -> decode code repr_rank[k] of `packed` (bits bytes per
+ * code) times scales[k / bph] to fp16; else copy fallback row fb_rank[k].
+ * repr_rank / fb_rank are the exclusive prefix counts of the mask and of its
+ * complement.  coord7's parity uses the non-negative remainder (the
+ * reference kernel's signed remainder decodes odd negative sums wrongly).
+ *   out  [n_heads*bph][8] fp16, 16-byte aligned; fallback 16-byte aligned */
+int lq_compact_merge(const uint8_t *packed, int64_t n_repr, int bits, const uint8_t *repr_mask,
+                     const int32_t *repr_rank, const int32_t *fb_rank, const uint16_t *fallback, int64_t n_fallback,
+                     const float *scales, int64_t n_heads, int64_t bph, uint16_t *out, uint32_t *err, void *stream);
+
 /* ------------------------------------------------------------------------
  * Randomized Hadamard transform (core/pipeline.py:33-122) on fp32 vectors
  * of length d (a power of two, 2..4096):

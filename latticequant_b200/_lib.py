@@ -79,6 +79,7 @@ def _declare(lib):
                             i32, f32, vp, i32, vp, vp, sz, vp, vp], i32),
         "lq_attn_merge": ([vp, vp, i64, i64, i32, vp, i32, vp, vp], i32),
         "lq_fwht": ([vp, i64, i32, vp, vp, vp, vp], i32),
+        "lq_compact_merge": ([vp, i64, i32, vp, vp, vp, vp, i64, vp, i64, i64, vp, vp, vp], i32),
         "lq_quantize_e8": ([vp, i64, f32, vp, vp, vp], i32),
         "lq_e8_to_symbols": ([vp, i64, vp, vp, vp], i32),
         "lq_symbols_to_e8": ([vp, vp, i64, vp, vp], i32),

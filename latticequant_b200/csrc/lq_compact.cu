@@ -101,6 +101,64 @@ __global__ void unpack_kernel(const uint8_t *__restrict__ in, int64_t n, int b, 
     }
 }
 
+// Fused merge of the compact layout with its fp16 fallback
+// (llm/fused_triton_merge.py:33-130): block k is representable (mask[k]) and
+// stored as code number repr_rank[k] of `packed`, or out of range and stored
+// as row fb_rank[k] of `fallback`.  Output fp16 = (point * head scale) for
+// coded blocks, the fallback row otherwise.  coord7's low bit is the
+// non-negative (sum c0..c6) mod 2; the reference's kernel takes Triton's
+// remainder, which is -1 for odd negative sums and then decodes a wrong c7.
+__global__ void compact_merge_kernel(const uint8_t *__restrict__ packed, int b, const uint8_t *__restrict__ mask,
+                                     const int32_t *__restrict__ repr_rank, const int32_t *__restrict__ fb_rank,
+                                     const uint16_t *__restrict__ fallback, const float *__restrict__ scales,
+                                     FastDiv bph_div, int64_t n, int64_t n_repr, int64_t n_fb,
+                                     uint16_t *__restrict__ out, uint32_t *err) {
+    const int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (k >= n) return;
+    uint4 o;
+    if (mask[k]) {
+        const int64_t r = repr_rank[k];
+        if (r < 0 || r >= n_repr) {
+            raise_flag(err, LQ_EF_BITSTREAM);
+            return;
+        }
+        uint64_t acc = 0;
+        for (int i = 0; i < b; ++i) acc = (acc << 8) | packed[r * b + i];
+        const int R = 1 << (b - 1);
+        const uint64_t cm = (1ull << b) - 1, um = (1ull << (b - 1)) - 1;
+        const int c7u = (int)(acc & um);
+        acc >>= (b - 1);
+        int s[7], ps = 0;
+#pragma unroll
+        for (int i = 6; i >= 0; --i) {
+            s[i] = (int)(acc & cm) - R;
+            acc >>= b;
+            ps += s[i];
+        }
+        const float off = (acc & 1u) ? 0.5f : 0.0f;
+        const float sc = scales[bph_div.div((uint32_t)k)];
+        float q[8];
+#pragma unroll
+        for (int i = 0; i < 7; ++i) q[i] = __fmul_rn(__fadd_rn((float)s[i], off), sc);
+        q[7] = __fmul_rn(__fadd_rn((float)(c7u * 2 + (ps & 1) - R), off), sc);
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const __half2 h = __floats2half2_rn(q[2 * i], q[2 * i + 1]);
+            w[i] = *reinterpret_cast<const uint32_t *>(&h);
+        }
+        o = make_uint4(w[0], w[1], w[2], w[3]);
+    } else {
+        const int64_t f = fb_rank[k];
+        if (f < 0 || f >= n_fb) {
+            raise_flag(err, LQ_EF_BITSTREAM);
+            return;
+        }
+        o = reinterpret_cast<const uint4 *>(fallback)[f];
+    }
+    reinterpret_cast<uint4 *>(out)[k] = o;
+}
+
 __global__ void selftest_div_kernel(const float *__restrict__ a, const float *__restrict__ b, int64_t n,
                                     float *__restrict__ out) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -170,5 +228,23 @@ extern "C" int lq_unpack_e8(const uint8_t *packed, int64_t n, int bits, const fl
     if (bits == 4 && (reinterpret_cast<uintptr_t>(packed) & 3)) return LQ_ERR_INVALID;
     lq::unpack_kernel<<<(unsigned)lq::ceil_div(n, 256), 256, 0, lq::as_stream(stream)>>>(packed, n, bits, scales,
                                                                                           head_idx, q_out, f16_out);
+    return lq::check_launch();
+}
+
+extern "C" int lq_compact_merge(const uint8_t *packed, int64_t n_repr, int bits, const uint8_t *repr_mask,
+                                const int32_t *repr_rank, const int32_t *fb_rank, const uint16_t *fallback,
+                                int64_t n_fallback, const float *scales, int64_t n_heads, int64_t bph, uint16_t *out,
+                                uint32_t *err, void *stream) {
+    if (n_heads < 0 || bph <= 0 || bits < 3 || bits > 5 || n_repr < 0 || n_fallback < 0) return LQ_ERR_INVALID;
+    const int64_t n = n_heads * bph;
+    if (n == 0) return LQ_OK;
+    if (!repr_mask || !repr_rank || !fb_rank || !scales || !out || (n_repr && !packed) || (n_fallback && !fallback))
+        return LQ_ERR_INVALID;
+    if ((reinterpret_cast<uintptr_t>(out) & 15) || (fallback && (reinterpret_cast<uintptr_t>(fallback) & 15)))
+        return LQ_ERR_INVALID;
+    if (n >= ((int64_t)1 << 32) || bph >= ((int64_t)1 << 31)) return LQ_ERR_INVALID;
+    lq::compact_merge_kernel<<<(unsigned)lq::ceil_div(n, 256), 256, 0, lq::as_stream(stream)>>>(
+        packed, bits, repr_mask, repr_rank, fb_rank, fallback, scales, lq::FastDiv((uint32_t)bph), n, n_repr,
+        n_fallback, out, err);
     return lq::check_launch();
 }

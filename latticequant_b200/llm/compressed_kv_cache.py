@@ -160,6 +160,9 @@ class CompressedKVLayer:
     def total_bytes(self):
         total = 0
         for c in self.chunks:
+            if not hasattr(c, "gpu_bitstream"):  # other chunk layouts count themselves
+                total += c.total_bytes
+                continue
             total += c.gpu_bitstream.nelement() * c.gpu_bitstream.element_size()
             total += c.coset_packed.nelement() * c.coset_packed.element_size()
             total += c.scales.nelement() * c.scales.element_size()
