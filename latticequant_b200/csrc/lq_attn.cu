@@ -86,11 +86,23 @@ __global__ void __launch_bounds__(attn_threads<G, BPT>(), 1) attn_partial_kernel
 
     // query channels 8*dc .. 8*dc+7 of the G heads reading this kv head
     const uint32_t b = head / a.n_kv_heads, kvh = head % a.n_kv_heads;
-    float qr[G][8];
+    // as packed pairs of heads (g, g+1) for fma.rn.f32x2; an odd last head alone
+    constexpr int GH = G / 2;
+    unsigned long long q2[GH > 0 ? GH : 1][8];
+    float qlast[8];
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
+    for (int g = 0; g < G; g += 2) {
         const int64_t row = (int64_t)b * a.n_kv_heads * G + (int64_t)kvh * G + g;
-        load_block8<QDT>(a.q, row * BPT + dc, qr[g]);
+        float x0[8], x1[8];
+        load_block8<QDT>(a.q, row * BPT + dc, x0);
+        if (g + 1 < G) {
+            load_block8<QDT>(a.q, (row + 1) * BPT + dc, x1);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) q2[g / 2][i] = f2_pack(x0[i], x1[i]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) qlast[i] = x0[i];
+        }
     }
 
     // ---- phase K: scores
@@ -102,26 +114,52 @@ __global__ void __launch_bounds__(attn_threads<G, BPT>(), 1) attn_partial_kernel
             [&](bool ok, int t, uint32_t grp, uint32_t j, uint32_t cc, const uint4 blk) {
                 float kq[8];
                 ring_point(blk, kq);
+                // per-lane partial dots over its 8 channels, i in order, two heads per fma.rn.f32x2
                 float dot[G];
 #pragma unroll
-                for (int g = 0; g < G; ++g) {
-                    float s = 0.f;
+                for (int g = 0; g + 1 < G; g += 2) {
+                    unsigned long long s2 = f2_mul(q2[g / 2][0], f2_pack(kq[0], kq[0]));
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) s = fmaf(qr[g][i], kq[i], s);
-                    dot[g] = ok ? s : 0.f;
+                    for (int i = 1; i < 8; ++i) s2 = f2_fma(q2[g / 2][i], f2_pack(kq[i], kq[i]), s2);
+                    f2_unpack(s2, dot[g], dot[g + 1]);
+                }
+                if constexpr (G % 2) {
+                    float s = __fmul_rn(qlast[0], kq[0]);
+#pragma unroll
+                    for (int i = 1; i < 8; ++i) s = __fmaf_rn(qlast[i], kq[i], s);
+                    dot[G - 1] = s;
                 }
 #pragma unroll
-                for (int off = BPT / 2; off >= 1; off >>= 1) {
-#pragma unroll
-                    for (int g = 0; g < G; ++g) dot[g] += __shfl_xor_sync(0xffffffffu, dot[g], off);
-                }
+                for (int g = 0; g < G; ++g) dot[g] = ok ? dot[g] : 0.f;
                 const uint32_t jc = j % BPT;
-                if (ok && jc < (uint32_t)G) {
-                    float v = dot[0];
+                const uint32_t tok = grp * TPG + j / BPT;
+                float *row = sc + ((uint32_t)t * a.tpt + tok) * GP;
+                if constexpr (G == 4 && BPT == 16) {
+                    // transposing reduction over the token's 16 lanes: halve the
+                    // heads a lane carries at each of the first two steps
+                    const bool h8 = (jc & 8u) != 0, h4 = (jc & 4u) != 0;
+                    float a0 = h8 ? dot[2] : dot[0], a1 = h8 ? dot[3] : dot[1];
+                    const float s0 = h8 ? dot[0] : dot[2], s1 = h8 ? dot[1] : dot[3];
+                    a0 += __shfl_xor_sync(0xffffffffu, s0, 8);
+                    a1 += __shfl_xor_sync(0xffffffffu, s1, 8);
+                    float bsum = h4 ? a1 : a0;
+                    bsum += __shfl_xor_sync(0xffffffffu, h4 ? a0 : a1, 4);
+                    bsum += __shfl_xor_sync(0xffffffffu, bsum, 2);
+                    bsum += __shfl_xor_sync(0xffffffffu, bsum, 1);
+                    // lane jc holds head (jc >> 2) & 3 (bit 3 picked heads 2-3, bit 2 the odd one)
+                    if (ok && (jc & 3u) == 0) row[jc >> 2] = bsum;
+                } else {
 #pragma unroll
-                    for (int g = 1; g < G; ++g) v = (jc == (uint32_t)g) ? dot[g] : v;
-                    const uint32_t tok = grp * TPG + j / BPT;
-                    sc[((uint32_t)t * a.tpt + tok) * GP + jc] = v;
+                    for (int off = BPT / 2; off >= 1; off >>= 1) {
+#pragma unroll
+                        for (int g = 0; g < G; ++g) dot[g] += __shfl_xor_sync(0xffffffffu, dot[g], off);
+                    }
+                    if (ok && jc < (uint32_t)G) {
+                        float v = dot[0];
+#pragma unroll
+                        for (int g = 1; g < G; ++g) v = (jc == (uint32_t)g) ? dot[g] : v;
+                        row[jc] = v;
+                    }
                 }
             },
             a.err);
@@ -181,11 +219,12 @@ __global__ void __launch_bounds__(attn_threads<G, BPT>(), 1) attn_partial_kernel
     __syncthreads();  // every warp is done with the K tables
     stage_tables(a.v, 0, dtab);
     __syncthreads();
-    float acc[G][8];
+    // p * v accumulated as packed channel pairs (i, i+1) per head
+    unsigned long long acc2[G][4];
 #pragma unroll
     for (int g = 0; g < G; ++g)
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[g][i] = 0.f;
+        for (int i = 0; i < 4; ++i) acc2[g][i] = 0ull;
     if (wact) {
         decode_two_tiles_ordered<kAttnRing>(
             a.v, 0, tile0, act0, act1, dta, ring,
@@ -204,13 +243,23 @@ __global__ void __launch_bounds__(attn_threads<G, BPT>(), 1) attn_partial_kernel
                     p[g4 + 2] = f.z;
                     p[g4 + 3] = f.w;
                 }
+                unsigned long long v2[4];
 #pragma unroll
-                for (int g = 0; g < G; ++g)
+                for (int i = 0; i < 4; ++i) v2[i] = f2_pack(vq[2 * i], vq[2 * i + 1]);
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) acc[g][i] = fmaf(p[g], vq[i], acc[g][i]);
+                for (int g = 0; g < G; ++g) {
+                    const unsigned long long pg = f2_pack(p[g], p[g]);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) acc2[g][i] = f2_fma(pg, v2[i], acc2[g][i]);
+                }
             },
             a.err);
     }
+    float acc[G][8];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) f2_unpack(acc2[g][i], acc[g][2 * i], acc[g][2 * i + 1]);
     // lanes holding the same channels: the two tiles (xor 16), two tokens per group for BPT 8 (xor 8)
 #pragma unroll
     for (int off = 16; off >= BPT; off >>= 1) {
