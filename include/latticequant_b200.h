@@ -130,6 +130,28 @@ int lq_e8_quantize(const void *x, int dtype, int64_t n_chunks, int64_t n_heads, 
                    int64_t tile_blocks, int16_t *sym_rows, uint32_t *coset_words, uint32_t *tile_n0, uint32_t *hist,
                    void *deq, int deq_dtype, float *q_out, uint32_t *err, void *stream);
 
+/* lq_e8_quantize with the outlier side channel (no counterpart in the
+ * reference, whose table build never ends for alphabets over L): a token of
+ * blocks_per_token consecutive blocks (a power of two <= 32 dividing bph and
+ * tile_blocks) holding any symbol outside [-limit, limit] is written to
+ * outlier_rec as blocks_per_token records (block index in the chunk, coset,
+ * 8 symbols; int32 x 10 each) and coded as zero blocks, so every stream's
+ * alphabet stays within 2*limit+5 values.  deq / q_out keep the true points.
+ *   outlier_words  optional [n_chunks][ceil(N/32)] bitmap of extracted blocks
+ *   outlier_rec    [n_chunks][outlier_cap][10]; outlier_count [n_chunks]
+ *                  (zeroed by this call); a full list raises LQ_EF_CAPACITY */
+int lq_e8_quantize_outliers(const void *x, int dtype, int64_t n_chunks, int64_t n_heads, int64_t bph,
+                            const float *scale_f32, int64_t tile_blocks, int16_t *sym_rows, uint32_t *coset_words,
+                            uint32_t *tile_n0, uint32_t *hist, void *deq, int deq_dtype, float *q_out, int limit,
+                            int blocks_per_token, uint32_t *outlier_words, int32_t *outlier_rec,
+                            uint32_t *outlier_count, int64_t outlier_cap, uint32_t *err, void *stream);
+
+/* Put the extracted blocks back into a decoded chunk batch: point * fp16
+ * head scale into out (out_dtype), symbols into sym_out (either may be NULL). */
+int lq_patch_outliers(const int32_t *outlier_rec, const uint32_t *outlier_count, int64_t n_chunks,
+                      int64_t outlier_cap, int64_t n_heads, int64_t bph, const uint16_t *scale_f16, void *out,
+                      int out_dtype, int32_t *sym_out, uint32_t *err, void *stream);
+
 /* Plain encode_e8 (core/e8_quantizer.py:61-83) / encode_d8 (:20-58) on (n,8) fp32. */
 int lq_encode_e8(const float *x, int64_t n, float *out, int d8_only, void *stream);
 
@@ -203,6 +225,8 @@ int lq_rans_decode(const uint32_t *words, int64_t n_words, const uint32_t *lane_
  *   out        [B][Hkv*group][head_dim] in out_dtype
  *   lse        optional [B][Hkv*group] fp32 ln(sum_t exp(s_t)), the form
  *              lq_attn_merge combines across key sets (sequence shards)
+ *   tok_mask   optional [B*Hkv][ceil(S/32)] u32 bitmap of tokens to leave
+ *              out (e.g. the chunks' outlier tokens, attended separately)
  *   workspace  lq_attn_decode_workspace() bytes (per-CTA partials)
  * Needs head_dim 64 or 128, group 1..8, tile_blocks dividing S*head_dim/8.
  * ---------------------------------------------------------------------- */
@@ -221,8 +245,8 @@ typedef struct lq_chunk_view {
 size_t lq_attn_decode_workspace(int64_t n_heads, int64_t bph, int64_t tile_blocks, int group, int head_dim);
 int lq_attn_decode(const lq_chunk_view *k, const lq_chunk_view *v, const void *q, int q_dtype, int64_t batch,
                    int64_t n_kv_heads, int64_t seq_len, int scale_per_token, int group, int head_dim, float sm_scale,
-                   void *out, int out_dtype, float *lse, void *workspace, size_t workspace_bytes, uint32_t *err,
-                   void *stream);
+                   void *out, int out_dtype, float *lse, const uint32_t *tok_mask, void *workspace,
+                   size_t workspace_bytes, uint32_t *err, void *stream);
 
 /* Merge attention parts over disjoint key sets (the all-gathered sequence
  * shards, or several chunks of one layer): o = sum_i o_i exp(lse_i - lse),

@@ -76,10 +76,13 @@ def _declare(lib):
         "lq_selftest": ([i32, vp, vp, i64, ctypes.c_uint32, vp, vp], i32),
         "lq_attn_decode_workspace": ([i64, i64, i64, i32, i32], sz),
         "lq_attn_decode": ([ctypes.POINTER(ChunkView), ctypes.POINTER(ChunkView), vp, i32, i64, i64, i64, i32, i32,
-                            i32, f32, vp, i32, vp, vp, sz, vp, vp], i32),
+                            i32, f32, vp, i32, vp, vp, vp, sz, vp, vp], i32),
         "lq_attn_merge": ([vp, vp, i64, i64, i32, vp, i32, vp, vp], i32),
         "lq_fwht": ([vp, i64, i32, vp, vp, vp, vp], i32),
         "lq_compact_merge": ([vp, i64, i32, vp, vp, vp, vp, i64, vp, i64, i64, vp, vp, vp], i32),
+        "lq_e8_quantize_outliers": ([vp, i32, i64, i64, i64, vp, i64, vp, vp, vp, vp, vp, i32, vp, i32, i32, vp, vp,
+                                     vp, i64, vp, vp], i32),
+        "lq_patch_outliers": ([vp, vp, i64, i64, i64, i64, vp, vp, i32, vp, vp, vp], i32),
         "lq_quantize_e8": ([vp, i64, f32, vp, vp, vp], i32),
         "lq_e8_to_symbols": ([vp, i64, vp, vp, vp], i32),
         "lq_symbols_to_e8": ([vp, vp, i64, vp, vp], i32),

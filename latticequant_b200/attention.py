@@ -20,7 +20,7 @@ import torch
 
 from . import _lib
 from ._lib import ChunkView, check, lib, ptr, raise_flags, stream_handle
-from .codec import LaneChunk, expand_dec_tables
+from .codec import LaneChunk, decompress, expand_dec_tables
 
 
 def chunk_view(chunk: LaneChunk) -> ChunkView:
@@ -110,16 +110,62 @@ class DecodeAttention:
         dev = k_chunk.words.device
         self.workspace = torch.empty(need, dtype=torch.uint8, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.mask = None
+        if k_chunk.n_outliers or v_chunk.n_outliers:
+            self._prepare_outliers()
+
+    def _prepare_outliers(self):
+        """Tokens with outlier records in K or V are left out of the fused kernel
+        (tok_mask) and attended exactly from their decoded rows."""
+        B, Hkv, S, D = self.shape
+        bpt = D // 8
+        dev = self.k.words.device
+        toks = []
+        for ch in (self.k, self.v):
+            if ch.n_outliers:
+                toks.append(ch.outlier_rec[:, 0].long() // bpt)  # token index over all heads (head-major)
+        tg = torch.unique(torch.cat(toks))
+        words = (S + 31) // 32
+        mask = torch.zeros(B * Hkv * words, dtype=torch.int64, device=dev)
+        lh, tok = tg // S, tg % S
+        mask.index_add_(0, lh * words + tok // 32, torch.ones_like(tok) << (tok % 32))
+        self.mask = mask.to(torch.int32)  # bit patterns fit: each bit is added once
+        kd = decompress(self.k, out_dtype=torch.float32).reshape(B * Hkv, S, D)
+        vd = decompress(self.v, out_dtype=torch.float32).reshape(B * Hkv, S, D)
+        self.ex_head = lh
+        self.ex_k = kd[lh, tok].contiguous()
+        self.ex_v = vd[lh, tok].contiguous()
+
+    def _launch(self, q3, out, lse, sm_scale):
+        B, Hkv, S, D = self.shape
+        check(lib().lq_attn_decode(ctypes.byref(self.kv), ctypes.byref(self.vv), ptr(q3), _lib.dtype_code(q3.dtype),
+                                   B, Hkv, S, int(self.scale_per_token), self.group, D, float(sm_scale), ptr(out),
+                                   _lib.dtype_code(out.dtype), ptr(lse), ptr(self.mask), ptr(self.workspace),
+                                   self.workspace.numel(), ptr(self.err), stream_handle(q3.device)), "lq_attn_decode")
 
     def __call__(self, q3: torch.Tensor, out: torch.Tensor, lse: Optional[torch.Tensor] = None,
                  sm_scale: Optional[float] = None):
         B, Hkv, S, D = self.shape
         if sm_scale is None:
             sm_scale = 1.0 / math.sqrt(D)
-        check(lib().lq_attn_decode(ctypes.byref(self.kv), ctypes.byref(self.vv), ptr(q3), _lib.dtype_code(q3.dtype),
-                                   B, Hkv, S, int(self.scale_per_token), self.group, D, float(sm_scale), ptr(out),
-                                   _lib.dtype_code(out.dtype), ptr(lse), ptr(self.workspace), self.workspace.numel(),
-                                   ptr(self.err), stream_handle(q3.device)), "lq_attn_decode")
+        if self.mask is None:
+            self._launch(q3, out, lse, sm_scale)
+            return
+        # fused part without the outlier tokens, exact part over them, merged by lse
+        rows = q3.shape[0] * q3.shape[1]
+        o1 = torch.empty(q3.shape, dtype=torch.float32, device=q3.device)
+        l1 = torch.empty(q3.shape[:2], dtype=torch.float32, device=q3.device)
+        self._launch(q3, o1, l1, sm_scale)
+        qf = q3.float().reshape(rows, D)
+        row_head = (torch.arange(rows, device=q3.device) // q3.shape[1]) * Hkv + \
+                   (torch.arange(rows, device=q3.device) % q3.shape[1]) // self.group
+        s = (qf @ self.ex_k.T) * sm_scale
+        s = s.masked_fill(row_head[:, None] != self.ex_head[None, :], float("-inf"))
+        l2 = torch.logsumexp(s, -1)
+        w = torch.exp(s - torch.where(torch.isfinite(l2), l2, torch.zeros_like(l2))[:, None])
+        o2 = (w @ self.ex_v)
+        merge_attention(torch.stack([o1.reshape(rows, D), o2]), torch.stack([l1.reshape(rows), l2]),
+                        out=out.view(rows, D), lse=lse.view(rows) if lse is not None else None)
 
     def flags(self) -> int:
         return int(self.err.item()) & 0xFFFFFFFF

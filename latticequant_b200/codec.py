@@ -89,6 +89,10 @@ class LaneChunk:
     lane_state: torch.Tensor     # [n_lanes] int32 (u32)
     n_words: int = 0
     dec_tab: Optional[torch.Tensor] = field(default=None, repr=False)
+    # outlier side channel: tokens with a symbol beyond OUTLIER_LIMIT, as records
+    # (block index, coset, 8 symbols) -- only when the chunk would exceed L symbols
+    outlier_rec: Optional[torch.Tensor] = field(default=None, repr=False)  # (n, 10) int32
+    n_outliers: int = 0
 
     # ---- accounting -----------------------------------------------------
     def coset_bytes(self) -> int:
@@ -96,8 +100,9 @@ class LaneChunk:
 
     def compressed_bytes(self) -> int:
         """Bytes counted as CompressedKVCache.compressed_bytes counts them
-        (llm/compressed_kv_cache.py:113-119): bitstream words + coset bits + fp16 scales."""
-        return 4 * self.n_words + self.coset_bytes() + 2 * self.scale_f16.numel()
+        (llm/compressed_kv_cache.py:113-119): bitstream words + coset bits + fp16 scales
+        (+ 40 bytes per outlier record)."""
+        return 4 * self.n_words + self.coset_bytes() + 2 * self.scale_f16.numel() + OUTLIER_REC_BYTES * self.n_outliers
 
     def metadata_bytes(self) -> int:
         """Side information the reference does not count: lane offsets / bit counts / states
@@ -105,6 +110,19 @@ class LaneChunk:
         n_lanes = self.geom.n_lanes
         tab = int(self.tab_nsym.clamp(min=0).sum().item()) * 2 + 8 * self.tab_nsym.numel()
         return 8 * n_lanes + tab + 4 * self.tile_n0.numel()
+
+
+OUTLIER_LIMIT = 255     # symbols beyond +-255 go to the outlier records when a table would exceed L
+OUTLIER_REC_BYTES = 40  # int32 block index, coset, 8 symbols
+
+
+def blocks_per_token(head_dim: int, tile_blocks: int, bph: int) -> int:
+    """Token granularity of the outlier records: head_dim/8 when it is a power
+    of two <= 32 dividing the tile and the blocks per head, else 1."""
+    b = head_dim // 8
+    if 0 < b <= 32 and b & (b - 1) == 0 and tile_blocks % b == 0 and bph % b == 0:
+        return b
+    return 1
 
 
 class Codec:
@@ -159,6 +177,42 @@ class Codec:
                                    ptr(self.scale_f32), g.tile_blocks, ptr(self.sym_rows), ptr(self.coset_words),
                                    ptr(self.tile_n0), ptr(self.hist), ptr(deq), dq, ptr(q_out), ptr(self.err), s),
               "lq_e8_quantize")
+
+    def quantize_outliers(self, x: torch.Tensor, q_out: Optional[torch.Tensor] = None, bpt: int = 1,
+                          cap: Optional[int] = None):
+        """quantize() with the outlier side channel (lq_e8_quantize_outliers)."""
+        g = self.geom
+        cap = int(cap or max(4096, g.n_vectors // 64))
+        if getattr(self, "out_cap", 0) < cap:
+            self.out_rec = torch.empty(g.n_chunks * cap * 10, dtype=torch.int32, device=self.device)
+            self.out_count = torch.zeros(g.n_chunks, dtype=torch.int32, device=self.device)
+            self.out_cap = cap
+        s = stream_handle(self.device)
+        deq = self.deq
+        dq = _lib.dtype_code(deq.dtype) if deq is not None else 0
+        check(lib().lq_e8_quantize_outliers(ptr(x), _lib.dtype_code(x.dtype), g.n_chunks, g.n_heads, g.bph,
+                                            ptr(self.scale_f32), g.tile_blocks, ptr(self.sym_rows),
+                                            ptr(self.coset_words), ptr(self.tile_n0), ptr(self.hist), ptr(deq), dq,
+                                            ptr(q_out), OUTLIER_LIMIT, bpt, None, ptr(self.out_rec),
+                                            ptr(self.out_count), self.out_cap, ptr(self.err), s),
+              "lq_e8_quantize_outliers")
+
+    def quantize_with_tables(self, x: torch.Tensor, q_out: Optional[torch.Tensor] = None, bpt: int = 1) -> int:
+        """quantize + build_tables; when a table would exceed L symbols (or a
+        symbol leaves the histogram range), quantise again with the outlier
+        side channel.  Returns the number of outlier records (synchronises)."""
+        self.quantize(x, q_out)
+        self.build_tables()
+        flags = self.read_err()
+        if not flags & (_lib.EF_ALPHABET | _lib.EF_SYMRANGE | _lib.EF_NOCONVERGE):
+            self.n_outliers = 0
+            return 0
+        self.err.zero_()
+        self.quantize_outliers(x, q_out, bpt)
+        self.build_tables()
+        raise_flags(self.read_err(), "quantize (outlier pass)")
+        self.n_outliers = int(self.out_count[:1].item())
+        return self.n_outliers
 
     def build_tables(self):
         g = self.geom
@@ -248,10 +302,11 @@ def compress(x: torch.Tensor, bits: float, tile_blocks: Optional[int] = DEFAULT_
         sf = scale_f32.to(device=x.device, dtype=torch.float32).reshape(-1)
         cd.scale_f32.copy_(sf)
         cd.scale_f16.copy_(sf.to(torch.float16))
-    cd.quantize(x, q_out)
+    n_out = 0
     if freqs is None:
-        cd.build_tables()
+        n_out = cd.quantize_with_tables(x, q_out, blocks_per_token(x.shape[-1], geom.tile_blocks, bph))
     else:
+        cd.quantize(x, q_out)
         lo, ns, fr = freqs
         cd.tab_lo.copy_(torch.as_tensor(lo, dtype=torch.int32).reshape(-1))
         cd.tab_nsym.copy_(torch.as_tensor(ns, dtype=torch.int32).reshape(-1))
@@ -265,7 +320,9 @@ def compress(x: torch.Tensor, bits: float, tile_blocks: Optional[int] = DEFAULT_
                       scale_f32=cd.scale_f32, scale_f16=cd.scale_f16, coset_words=cd.coset_words,
                       tile_n0=cd.tile_n0, tab_lo=cd.tab_lo, tab_nsym=cd.tab_nsym, tab_freq=cd.tab_freq,
                       words=cd.words[:max(nw, 1)].clone(), lane_off=cd.lane_off, lane_nbits=cd.lane_nbits,
-                      lane_state=cd.lane_state, n_words=nw)
+                      lane_state=cd.lane_state, n_words=nw,
+                      outlier_rec=cd.out_rec[:n_out * 10].view(n_out, 10).clone() if n_out else None,
+                      n_outliers=n_out)
     deq = cd.deq.view(x.shape) if keep_deq else None
     return chunk, deq
 
@@ -300,8 +357,22 @@ def decompress(chunk: LaneChunk, out_dtype: Optional[torch.dtype] = None, want_s
                                ptr(chunk.tab_freq), ptr(dec), ptr(chunk.scale_f16), ptr(out),
                                _lib.dtype_code(od), ptr(sym), ptr(ws), ws.numel(), ptr(err), stream_handle(dev)),
           "lq_rans_decode")
+    if chunk.n_outliers:
+        patch_outliers(chunk, out, sym, err)
     raise_flags(int(err.item()) & 0xFFFFFFFF, "decompress")
     out = out.view(chunk.orig_shape)
     if want_symbols:
         return out, sym.view(-1, 8)
     return out
+
+
+def patch_outliers(chunk: LaneChunk, out: Optional[torch.Tensor], sym: Optional[torch.Tensor],
+                   err: torch.Tensor):
+    """Write a chunk's outlier records back into its decoded output / symbols."""
+    g = chunk.geom
+    dev = chunk.words.device
+    cnt = torch.tensor([chunk.n_outliers], dtype=torch.int32, device=dev)
+    rec = chunk.outlier_rec.contiguous()
+    check(lib().lq_patch_outliers(ptr(rec), ptr(cnt), 1, chunk.n_outliers, g.n_heads, g.bph, ptr(chunk.scale_f16),
+                                  ptr(out), _lib.dtype_code(out.dtype) if out is not None else 0, ptr(sym), ptr(err),
+                                  stream_handle(dev)), "lq_patch_outliers")

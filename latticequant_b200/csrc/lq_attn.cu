@@ -48,6 +48,7 @@ struct AttnArgs {
     uint32_t warp_bytes;  // bytes of per-warp shared memory
     float qk_log2;        // sm_scale * log2(e)
     float *part;          // [heads][nct][G][D + 2]: o (unnormalised), m, l
+    const uint32_t *tok_mask;  // optional [heads][ceil(seq/32)] tokens to leave out
     uint32_t *err;
 };
 
@@ -169,11 +170,19 @@ __global__ void __launch_bounds__(attn_threads<G, BPT>(), 1) attn_partial_kernel
     // ---- softmax statistics of this warp's tokens (base 2)
     const float ck = a.scale_tok ? a.qk_log2 : __half2float(__ushort_as_half(a.k.scale_f16[head])) * a.qk_log2;
     const uint32_t ntok = 2 * a.tpt;
-    // per-token scales: token i of the warp is token (2*pair + i/tpt)*tpt + i%tpt of the head
-    auto tok_scale = [&](const uint16_t *sc16, uint32_t i) {
+    // token i of the warp is token (2*pair + i/tpt)*tpt + i%tpt of the head
+    auto tok_of = [&](uint32_t i) {
         const uint32_t t = i < a.tpt ? 0u : 1u;
-        const uint32_t tok = (2 * pair + t) * a.tpt + (i - t * a.tpt);
-        return __half2float(__ushort_as_half(sc16[(size_t)head * a.seq + tok]));
+        return (2 * pair + t) * a.tpt + (i - t * a.tpt);
+    };
+    auto tok_scale = [&](const uint16_t *sc16, uint32_t i) {
+        return __half2float(__ushort_as_half(sc16[(size_t)head * a.seq + tok_of(i)]));
+    };
+    const uint32_t mwords = (a.seq + 31) >> 5;
+    auto masked = [&](uint32_t i) {
+        if (!a.tok_mask) return false;
+        const uint32_t tok = tok_of(i);
+        return ((a.tok_mask[(size_t)head * mwords + (tok >> 5)] >> (tok & 31)) & 1u) != 0u;
     };
     float m[G], l[G];
 #pragma unroll
@@ -183,7 +192,7 @@ __global__ void __launch_bounds__(attn_threads<G, BPT>(), 1) attn_partial_kernel
     }
     for (uint32_t i = lane; i < ntok; i += 32) {
         const bool v = i < a.tpt ? act0 : act1;
-        if (!v) continue;
+        if (!v || masked(i)) continue;
         const float cki = a.scale_tok ? ck * tok_scale(a.k.scale_f16, i) : ck;
 #pragma unroll
         for (int g = 0; g < G; ++g) {
@@ -199,6 +208,11 @@ __global__ void __launch_bounds__(attn_threads<G, BPT>(), 1) attn_partial_kernel
     for (uint32_t i = lane; i < ntok; i += 32) {
         const bool v = i < a.tpt ? act0 : act1;
         if (!v) continue;
+        if (masked(i)) {  // left out: zero weight
+#pragma unroll
+            for (int g = 0; g < G; ++g) sc[i * GP + g] = 0.f;
+            continue;
+        }
         // with per-token V scales the token's scale rides on its weight p
         const float cvi = a.scale_tok ? tok_scale(a.v.scale_f16, i) : 1.0f;
 #pragma unroll
@@ -453,8 +467,9 @@ extern "C" size_t lq_attn_decode_workspace(int64_t n_heads, int64_t bph, int64_t
 
 extern "C" int lq_attn_decode(const lq_chunk_view *k, const lq_chunk_view *v, const void *q, int q_dtype,
                               int64_t batch, int64_t n_kv_heads, int64_t seq_len, int scale_per_token, int group,
-                              int head_dim, float sm_scale, void *out, int out_dtype, float *lse, void *workspace,
-                              size_t workspace_bytes, uint32_t *err, void *stream) {
+                              int head_dim, float sm_scale, void *out, int out_dtype, float *lse,
+                              const uint32_t *tok_mask, void *workspace, size_t workspace_bytes, uint32_t *err,
+                              void *stream) {
     if (!view_ok(k) || !view_ok(v) || !q || !out || !workspace || batch <= 0 || n_kv_heads <= 0 || seq_len <= 0)
         return LQ_ERR_INVALID;
     if (k->n_heads != v->n_heads || k->bph != v->bph || k->tile_blocks != v->tile_blocks) return LQ_ERR_INVALID;
@@ -486,6 +501,7 @@ extern "C" int lq_attn_decode(const lq_chunk_view *k, const lq_chunk_view *v, co
     a.warp_bytes = p.warp_bytes;
     a.qk_log2 = sm_scale * kLog2e;
     a.part = static_cast<float *>(workspace);
+    a.tok_mask = tok_mask;
     a.err = err;
     const uint32_t nh = (uint32_t)heads;
     int r;

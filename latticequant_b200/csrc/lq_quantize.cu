@@ -29,12 +29,26 @@ __device__ __forceinline__ void red_shared_add1(uint32_t addr) {
     asm volatile("red.shared.add.u32 [%0], 1;" ::"r"(addr) : "memory");
 }
 
+// Outlier side channel (off when limit == 0): a token (bpt consecutive
+// blocks) with a symbol outside [-limit, limit] goes whole to a record list
+// (block index, coset, 8 symbols per block) and is coded as zero blocks, so
+// every stream's alphabet stays within 2*limit + 5 values.  The reference has
+// no such path: its table build never ends for alphabets over L.
+struct OutlierArgs {
+    int limit;           // 0 = off
+    uint32_t bpt;        // blocks per token (1, 2, 4, 8, 16 or 32)
+    uint32_t *words;     // [n_chunks][ceil(N/32)] bitmap of extracted blocks (may be NULL)
+    int32_t *rec;        // [n_chunks][cap][10]
+    uint32_t *count;     // [n_chunks]
+    uint32_t cap;
+};
+
 template <int DT, int DQ, bool QO>
 __global__ void __launch_bounds__(32 * kQWarps, 4) quantize_kernel(
     const void *__restrict__ x, uint32_t n_heads, uint32_t bph, FastDiv bph_div, const float *__restrict__ scale_f32,
     uint32_t TB, uint32_t n_tiles, int16_t *__restrict__ sym_rows, uint32_t *__restrict__ coset_words,
     uint32_t *__restrict__ tile_n0, uint32_t *__restrict__ hist, void *__restrict__ deq, float *__restrict__ q_out,
-    uint32_t *__restrict__ err) {
+    OutlierArgs oa, uint32_t *__restrict__ err) {
     __shared__ uint32_t sh_hist[LQ_NSTREAMS * kSmemBins];
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t warp = threadIdx.x >> 5;
@@ -92,6 +106,35 @@ __global__ void __launch_bounds__(32 * kQWarps, 4) quantize_kernel(
                     qp[1] = make_float4(q[4], q[5], q[6], q[7]);
                 }
             }
+            if (oa.limit > 0) {  // uniform
+                bool out = false;
+                if (active) {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) out |= (sym[i] > oa.limit) || (sym[i] < -oa.limit);
+                }
+                const uint32_t ob = __ballot_sync(0xffffffffu, out);
+                if (ob) {
+                    const uint32_t tm = (oa.bpt >= 32 ? 0xffffffffu : ((1u << oa.bpt) - 1u)) << ((lane / oa.bpt) * oa.bpt);
+                    out = active && (ob & tm) != 0u;  // the whole token
+                    if (out) {
+                        const uint32_t idx = atomicAdd(&oa.count[chunk], 1u);
+                        if (idx < oa.cap) {
+                            int32_t *r = oa.rec + ((size_t)chunk * oa.cap + idx) * 10;
+                            r[0] = (int32_t)(b0 + off + lane);
+                            r[1] = coset;
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) r[2 + i] = sym[i];
+                        } else {
+                            flags |= LQ_EF_CAPACITY;
+                        }
+                        coset = 0;
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) sym[i] = 0;
+                    }
+                }
+                const uint32_t ow = __ballot_sync(0xffffffffu, out);
+                if (oa.words && lane == 0) oa.words[(int64_t)chunk * words_per_chunk + (b0 + off) / 32] = ow;
+            }
             const uint32_t ball = __ballot_sync(0xffffffffu, active && coset);
             const uint32_t act = __ballot_sync(0xffffffffu, active);
             if (lane == 0) cw[off / 32] = ball;
@@ -141,33 +184,33 @@ __global__ void __launch_bounds__(32 * kQWarps, 4) quantize_kernel(
 template <int DT, int DQ, bool QO>
 int launch_quantize(const void *x, int64_t n_chunks, int64_t n_heads, int64_t bph, const float *scale_f32, int64_t TB,
                     int16_t *sym_rows, uint32_t *coset_words, uint32_t *tile_n0, uint32_t *hist, void *deq,
-                    float *q_out, uint32_t *err, cudaStream_t st) {
+                    float *q_out, const OutlierArgs &oa, uint32_t *err, cudaStream_t st) {
     const int64_t N = n_heads * bph;
     const int64_t n_tiles = ceil_div(N, TB);
     dim3 grid((unsigned)ceil_div(n_tiles, kQWarps), (unsigned)n_chunks);
     quantize_kernel<DT, DQ, QO><<<grid, 32 * kQWarps, 0, st>>>(x, (uint32_t)n_heads, (uint32_t)bph, FastDiv((uint32_t)bph),
                                                             scale_f32, (uint32_t)TB, (uint32_t)n_tiles, sym_rows,
-                                                            coset_words, tile_n0, hist, deq, q_out, err);
+                                                            coset_words, tile_n0, hist, deq, q_out, oa, err);
     return check_launch();
 }
 
 template <int DT, bool QO>
 int dispatch_deq(int deq_dtype, const void *x, int64_t n_chunks, int64_t n_heads, int64_t bph, const float *sc,
                  int64_t TB, int16_t *sym_rows, uint32_t *cw, uint32_t *tn0, uint32_t *hist, void *deq, float *q_out,
-                 uint32_t *err, cudaStream_t st) {
+                 const OutlierArgs &oa, uint32_t *err, cudaStream_t st) {
     if (deq == nullptr)
         return launch_quantize<DT, -1, QO>(x, n_chunks, n_heads, bph, sc, TB, sym_rows, cw, tn0, hist, deq, q_out,
-                                           err, st);
+                                           oa, err, st);
     switch (deq_dtype) {
         case LQ_F32:
             return launch_quantize<DT, LQ_F32, QO>(x, n_chunks, n_heads, bph, sc, TB, sym_rows, cw, tn0, hist, deq,
-                                                   q_out, err, st);
+                                                   q_out, oa, err, st);
         case LQ_F16:
             return launch_quantize<DT, LQ_F16, QO>(x, n_chunks, n_heads, bph, sc, TB, sym_rows, cw, tn0, hist, deq,
-                                                   q_out, err, st);
+                                                   q_out, oa, err, st);
         case LQ_BF16:
             return launch_quantize<DT, LQ_BF16, QO>(x, n_chunks, n_heads, bph, sc, TB, sym_rows, cw, tn0, hist, deq,
-                                                    q_out, err, st);
+                                                    q_out, oa, err, st);
         default:
             return LQ_ERR_INVALID;
     }
@@ -176,11 +219,11 @@ int dispatch_deq(int deq_dtype, const void *x, int64_t n_chunks, int64_t n_heads
 template <int DT>
 int dispatch_q(int deq_dtype, const void *x, int64_t n_chunks, int64_t n_heads, int64_t bph, const float *sc,
                int64_t TB, int16_t *sym_rows, uint32_t *cw, uint32_t *tn0, uint32_t *hist, void *deq, float *q_out,
-               uint32_t *err, cudaStream_t st) {
+               const OutlierArgs &oa, uint32_t *err, cudaStream_t st) {
     return q_out ? dispatch_deq<DT, true>(deq_dtype, x, n_chunks, n_heads, bph, sc, TB, sym_rows, cw, tn0, hist, deq,
-                                          q_out, err, st)
+                                          q_out, oa, err, st)
                  : dispatch_deq<DT, false>(deq_dtype, x, n_chunks, n_heads, bph, sc, TB, sym_rows, cw, tn0, hist, deq,
-                                           q_out, err, st);
+                                           q_out, oa, err, st);
 }
 
 __global__ void encode_e8_kernel(const float *__restrict__ x, int64_t n, float *__restrict__ out, int d8_only) {
@@ -198,10 +241,11 @@ __global__ void encode_e8_kernel(const float *__restrict__ x, int64_t n, float *
 }  // namespace
 }  // namespace lq
 
-extern "C" int lq_e8_quantize(const void *x, int dtype, int64_t n_chunks, int64_t n_heads, int64_t bph,
-                              const float *scale_f32, int64_t tile_blocks, int16_t *sym_rows, uint32_t *coset_words,
-                              uint32_t *tile_n0, uint32_t *hist, void *deq, int deq_dtype, float *q_out,
-                              uint32_t *err, void *stream) {
+namespace lq {
+namespace {
+int quantize_entry(const void *x, int dtype, int64_t n_chunks, int64_t n_heads, int64_t bph, const float *scale_f32,
+                   int64_t tile_blocks, int16_t *sym_rows, uint32_t *coset_words, uint32_t *tile_n0, uint32_t *hist,
+                   void *deq, int deq_dtype, float *q_out, const OutlierArgs &oa, uint32_t *err, void *stream) {
     if (n_chunks < 0 || n_heads < 0 || bph < 0) return LQ_ERR_INVALID;
     if (tile_blocks <= 0 || (tile_blocks % 32) != 0) return LQ_ERR_INVALID;
     if (n_chunks == 0 || n_heads * bph == 0) return LQ_OK;
@@ -211,22 +255,115 @@ extern "C" int lq_e8_quantize(const void *x, int dtype, int64_t n_chunks, int64_
         return LQ_ERR_INVALID;
     if (n_chunks > 65535) return LQ_ERR_INVALID;
     if (n_heads * bph >= (int64_t)1 << 31) return LQ_ERR_INVALID;  // blocks per chunk are indexed in 32 bits
-    cudaStream_t st = lq::as_stream(stream);
+    cudaStream_t st = as_stream(stream);
     if (cudaMemsetAsync(hist, 0, sizeof(uint32_t) * (size_t)n_chunks * LQ_NSTREAMS * LQ_HIST_BINS, st) != cudaSuccess)
         return LQ_ERR_CUDA;
     switch (dtype) {
         case LQ_F32:
-            return lq::dispatch_q<LQ_F32>(deq_dtype, x, n_chunks, n_heads, bph, scale_f32, tile_blocks, sym_rows,
-                                            coset_words, tile_n0, hist, deq, q_out, err, st);
+            return dispatch_q<LQ_F32>(deq_dtype, x, n_chunks, n_heads, bph, scale_f32, tile_blocks, sym_rows,
+                                      coset_words, tile_n0, hist, deq, q_out, oa, err, st);
         case LQ_F16:
-            return lq::dispatch_q<LQ_F16>(deq_dtype, x, n_chunks, n_heads, bph, scale_f32, tile_blocks, sym_rows,
-                                            coset_words, tile_n0, hist, deq, q_out, err, st);
+            return dispatch_q<LQ_F16>(deq_dtype, x, n_chunks, n_heads, bph, scale_f32, tile_blocks, sym_rows,
+                                      coset_words, tile_n0, hist, deq, q_out, oa, err, st);
         case LQ_BF16:
-            return lq::dispatch_q<LQ_BF16>(deq_dtype, x, n_chunks, n_heads, bph, scale_f32, tile_blocks, sym_rows,
-                                             coset_words, tile_n0, hist, deq, q_out, err, st);
+            return dispatch_q<LQ_BF16>(deq_dtype, x, n_chunks, n_heads, bph, scale_f32, tile_blocks, sym_rows,
+                                       coset_words, tile_n0, hist, deq, q_out, oa, err, st);
         default:
             return LQ_ERR_INVALID;
     }
+}
+
+// One thread per record: the extracted block's point (symbols_to_e8) times
+// its head's fp16 scale, into the decoded output (and its symbols into sym_out).
+template <int DO>
+__global__ void patch_outliers_kernel(const int32_t *__restrict__ rec, const uint32_t *__restrict__ count,
+                                      uint32_t cap, uint32_t n_heads, uint32_t bph, const uint16_t *__restrict__ scale,
+                                      void *__restrict__ out, int32_t *__restrict__ sym_out, uint32_t *err) {
+    const uint32_t chunk = blockIdx.y;
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    const uint32_t n = min(count[chunk], cap);
+    if (i >= n) return;
+    const int32_t *r = rec + ((size_t)chunk * cap + i) * 10;
+    const uint32_t blk = (uint32_t)r[0];
+    const uint32_t N = n_heads * bph;
+    if (blk >= N) {
+        raise_flag(err, LQ_EF_BITSTREAM);
+        return;
+    }
+    int sym[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) sym[k] = r[2 + k];
+    const size_t gb = (size_t)chunk * N + blk;
+    if (sym_out) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) sym_out[8 * gb + k] = sym[k];
+    }
+    if constexpr (DO >= 0) {
+        float q[8];
+        e8_from_symbols(r[1], sym, q);
+        const float sc = __half2float(__ushort_as_half(scale[(size_t)chunk * n_heads + blk / bph]));
+#pragma unroll
+        for (int k = 0; k < 8; ++k) q[k] = __fmul_rn(q[k], sc);
+        store_block8<DO>(out, gb, q);
+    }
+}
+}  // namespace
+}  // namespace lq
+
+extern "C" int lq_e8_quantize(const void *x, int dtype, int64_t n_chunks, int64_t n_heads, int64_t bph,
+                              const float *scale_f32, int64_t tile_blocks, int16_t *sym_rows, uint32_t *coset_words,
+                              uint32_t *tile_n0, uint32_t *hist, void *deq, int deq_dtype, float *q_out,
+                              uint32_t *err, void *stream) {
+    const lq::OutlierArgs off{0, 1, nullptr, nullptr, nullptr, 0};
+    return lq::quantize_entry(x, dtype, n_chunks, n_heads, bph, scale_f32, tile_blocks, sym_rows, coset_words, tile_n0,
+                              hist, deq, deq_dtype, q_out, off, err, stream);
+}
+
+extern "C" int lq_e8_quantize_outliers(const void *x, int dtype, int64_t n_chunks, int64_t n_heads, int64_t bph,
+                                       const float *scale_f32, int64_t tile_blocks, int16_t *sym_rows,
+                                       uint32_t *coset_words, uint32_t *tile_n0, uint32_t *hist, void *deq,
+                                       int deq_dtype, float *q_out, int limit, int blocks_per_token,
+                                       uint32_t *outlier_words, int32_t *outlier_rec, uint32_t *outlier_count,
+                                       int64_t outlier_cap, uint32_t *err, void *stream) {
+    if (limit <= 0 || limit > 0x3fffffff || blocks_per_token <= 0 || blocks_per_token > 32 ||
+        (blocks_per_token & (blocks_per_token - 1)) || (tile_blocks % blocks_per_token) || (bph % blocks_per_token) ||
+        !outlier_rec || !outlier_count || outlier_cap < 0 || outlier_cap > 0x7fffffff)
+        return LQ_ERR_INVALID;
+    if (n_chunks > 0 &&
+        cudaMemsetAsync(outlier_count, 0, sizeof(uint32_t) * (size_t)n_chunks, lq::as_stream(stream)) != cudaSuccess)
+        return LQ_ERR_CUDA;
+    const lq::OutlierArgs oa{limit, (uint32_t)blocks_per_token, outlier_words, outlier_rec, outlier_count,
+                             (uint32_t)outlier_cap};
+    return lq::quantize_entry(x, dtype, n_chunks, n_heads, bph, scale_f32, tile_blocks, sym_rows, coset_words, tile_n0,
+                              hist, deq, deq_dtype, q_out, oa, err, stream);
+}
+
+extern "C" int lq_patch_outliers(const int32_t *outlier_rec, const uint32_t *outlier_count, int64_t n_chunks,
+                                 int64_t outlier_cap, int64_t n_heads, int64_t bph, const uint16_t *scale_f16,
+                                 void *out, int out_dtype, int32_t *sym_out, uint32_t *err, void *stream) {
+    if (n_chunks < 0 || outlier_cap < 0 || n_heads < 0 || bph <= 0 || outlier_cap > 0x7fffffff) return LQ_ERR_INVALID;
+    if (n_chunks == 0 || outlier_cap == 0 || n_heads == 0) return LQ_OK;
+    if (!outlier_rec || !outlier_count || (!out && !sym_out) || (out && !scale_f16) || n_chunks > 65535 ||
+        n_heads * bph >= ((int64_t)1 << 31))
+        return LQ_ERR_INVALID;
+    if (out && (reinterpret_cast<uintptr_t>(out) & 15)) return LQ_ERR_INVALID;
+    dim3 grid((unsigned)lq::ceil_div(outlier_cap, 128), (unsigned)n_chunks);
+    cudaStream_t st = lq::as_stream(stream);
+    const uint32_t cap = (uint32_t)outlier_cap, nh = (uint32_t)n_heads, b = (uint32_t)bph;
+    if (!out) lq::patch_outliers_kernel<-1><<<grid, 128, 0, st>>>(outlier_rec, outlier_count, cap, nh, b, scale_f16,
+                                                                   out, sym_out, err);
+    else if (out_dtype == LQ_F32)
+        lq::patch_outliers_kernel<LQ_F32><<<grid, 128, 0, st>>>(outlier_rec, outlier_count, cap, nh, b, scale_f16, out,
+                                                                sym_out, err);
+    else if (out_dtype == LQ_F16)
+        lq::patch_outliers_kernel<LQ_F16><<<grid, 128, 0, st>>>(outlier_rec, outlier_count, cap, nh, b, scale_f16, out,
+                                                                sym_out, err);
+    else if (out_dtype == LQ_BF16)
+        lq::patch_outliers_kernel<LQ_BF16><<<grid, 128, 0, st>>>(outlier_rec, outlier_count, cap, nh, b, scale_f16,
+                                                                 out, sym_out, err);
+    else
+        return LQ_ERR_INVALID;
+    return lq::check_launch();
 }
 
 extern "C" int lq_encode_e8(const float *x, int64_t n, float *out, int d8_only, void *stream) {

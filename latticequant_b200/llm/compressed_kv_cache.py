@@ -166,6 +166,8 @@ class CompressedKVLayer:
             total += c.gpu_bitstream.nelement() * c.gpu_bitstream.element_size()
             total += c.coset_packed.nelement() * c.coset_packed.element_size()
             total += c.scales.nelement() * c.scales.element_size()
+            if c.lanes is not None and c.lanes.n_outliers:
+                total += codec.OUTLIER_REC_BYTES * c.lanes.n_outliers
         return total
 
     @property
@@ -282,7 +284,11 @@ class CompressedKVCache(DynamicCache):
         geom = codec.Geometry(1, n_heads, bph, codec.round_tile(self.tile_blocks, n_vectors))
         cd = codec.Codec(geom, x.device, keep_deq=True, deq_dtype=orig_dtype)
         cd.scales(x, self.bits)
-        cd.quantize(x)
+        n_out = 0
+        if self.eval_only_no_entropy or self.table_mode == "numpy":
+            cd.quantize(x)
+        else:  # device tables; chunks whose alphabet would exceed L get the outlier side channel
+            n_out = cd.quantize_with_tables(x, None, codec.blocks_per_token(hd, geom.tile_blocks, bph))
         deq = cd.deq.view(tensor.shape)
         if self.eval_only_no_entropy:
             flags = cd.read_err()
@@ -302,8 +308,6 @@ class CompressedKVCache(DynamicCache):
             cd.tab_lo.copy_(torch.from_numpy(lo))
             cd.tab_nsym.copy_(torch.from_numpy(ns))
             cd.tab_freq.copy_(torch.from_numpy(fr.astype(np.int16)))
-        else:
-            cd.build_tables()
         cd.expand_tables(enc=True, dec=False)
         cd.entropy_encode()
         from .._lib import raise_flags
@@ -314,7 +318,9 @@ class CompressedKVCache(DynamicCache):
                                 scale_f32=cd.scale_f32, scale_f16=cd.scale_f16, coset_words=cd.coset_words,
                                 tile_n0=cd.tile_n0, tab_lo=cd.tab_lo, tab_nsym=cd.tab_nsym, tab_freq=cd.tab_freq,
                                 words=cd.words[:max(nw, 1)].clone(), lane_off=cd.lane_off,
-                                lane_nbits=cd.lane_nbits, lane_state=cd.lane_state, n_words=nw)
+                                lane_nbits=cd.lane_nbits, lane_state=cd.lane_state, n_words=nw,
+                                outlier_rec=cd.out_rec[:n_out * 10].view(n_out, 10).clone() if n_out else None,
+                                n_outliers=n_out)
         self.total_vectors += n_vectors
         coset_bytes = cd.coset_words.view(torch.uint8)[: (n_vectors + 7) // 8]
         chunk = OptimizedChunk(gpu_bitstream=lanes.words[:nw] if nw else torch.zeros(0, dtype=torch.int32,

@@ -35,6 +35,8 @@ def chunk_state(ch: LaneChunk) -> Dict[str, Any]:
          "words": ch.words[:max(ch.n_words, 1)].detach().cpu().clone()}
     for k in _ARRAYS:
         d[k] = getattr(ch, k).detach().cpu().clone()
+    d["n_outliers"] = int(ch.n_outliers)
+    d["outlier_rec"] = ch.outlier_rec.detach().cpu().clone() if ch.n_outliers else None
     return d
 
 
@@ -47,9 +49,13 @@ def chunk_from_state(d: Dict[str, Any], device="cuda") -> LaneChunk:
         raise ValueError("chunk record does not match its geometry")
     if int(d["n_words"]) > d["words"].numel() or int(arrs["lane_off"][-1].item()) > max(int(d["n_words"]), 1):
         raise ValueError("chunk record: lane offsets run past the words")
+    n_out = int(d.get("n_outliers", 0))
+    rec = d.get("outlier_rec")
+    if n_out and (rec is None or tuple(rec.shape) != (n_out, 10)):
+        raise ValueError("chunk record: outlier records do not match their count")
     return LaneChunk(geom=g, bits=float(d["bits"]), orig_shape=tuple(d["orig_shape"]),
                      orig_dtype=_DT_INV[d["orig_dtype"]], words=d["words"].to(device), n_words=int(d["n_words"]),
-                     **arrs)
+                     outlier_rec=rec.to(device) if n_out else None, n_outliers=n_out, **arrs)
 
 
 def save_chunk(ch: LaneChunk, path: str):
@@ -123,6 +129,8 @@ def _rebuild_resident(lanes: LaneChunk, dtype):
     cw = lanes.coset_words.view(torch.int32)
     bits = (cw.view(-1, 1) >> torch.arange(32, device=q.device, dtype=torch.int32)) & 1
     cos[:] = bits.reshape(-1)[:n]
+    if lanes.n_outliers:  # extracted blocks keep their coset in the records
+        cos[lanes.outlier_rec[:, 0].long()] = lanes.outlier_rec[:, 1]
     pts = symbols_to_e8(cos, q[:, :7], q[:, 7])
     g = lanes.geom
     sc = lanes.scale_f32.view(g.n_heads, 1, 1)

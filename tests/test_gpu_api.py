@@ -256,8 +256,10 @@ def test_variable_rate_cache_and_uncompressible():
 
 
 # ---------------------------------------------------------------- error paths
-def test_alphabet_over_L_raises_value_error():
-    """The reference loops forever here; the device coder reports it."""
+def test_alphabet_over_L():
+    """The reference loops forever here.  With numpy tables (the reference's own
+    normalisation) it is reported as ValueError; with device tables the chunk
+    takes the outlier side channel and decodes exactly."""
     from latticequant_b200.llm.compressed_kv_cache import CompressedKVCache
 
     # one head of 1085 blocks, two spikes of +-1: they land on lattice values +-510 of the same
@@ -265,9 +267,13 @@ def test_alphabet_over_L_raises_value_error():
     x = torch.zeros(1, 1, 1085, 8, device="cuda")
     x[0, 0, 0, 0] = 1.0
     x[0, 0, 1, 0] = -1.0
-    cache = CompressedKVCache(bits_per_dim=5)
     with pytest.raises(ValueError):
-        cache._compress_tensor(x)
+        CompressedKVCache(bits_per_dim=5, table_mode="numpy")._compress_tensor(x)
+    cache = CompressedKVCache(bits_per_dim=5)
+    chunk, deq = cache._compress_tensor(x)
+    assert chunk.lanes.n_outliers == 2  # head_dim 8: one block per token
+    dec = cache._decompress_chunk(chunk)  # fp16 scale; update()'s deq uses the fp32 scale
+    assert torch.allclose(dec, deq, rtol=1e-3, atol=0) and bool((dec.abs().amax() > 0.99).item())
 
 
 def test_nonfinite_input_raises():
