@@ -21,6 +21,14 @@ lane metadata + q + o) per second.  At N GPUs the context is sequence-sharded:
 each rank attends over its slice and one NCCL all-gather of (o, lse) plus the
 LSE merge completes the step (strong scaling of one decode step).
 
+"config4" carries BASELINE config 4: a Qwen2.5-7B-shaped mixed-rate cache
+(28 layers x 4 KV heads x head_dim 128, batch 4, context 131072; per-layer
+bits from {3, 4, 5} with exactly 3 layers at 5; K ~ Student-t(3), V ~ N(0,1)),
+whole-model encode and one fused decode-attention step over every layer,
+sharded by (layer, KV head) units over the ranks with no collective.  The
+line reports how many tokens went to the outlier side channel (chunks whose
+alphabet would exceed L = 1024 symbols).
+
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 """
 import argparse
@@ -46,6 +54,8 @@ UNIT = "Gvec/s"
 # config 3 (fused dequant + decode attention)
 A_B, A_HKV, A_G, A_S, A_D = 16, 8, 4, 32768, 128
 A_METRIC = "fused dequant-attn HBM GB/s"
+# config 4 (Qwen2.5-7B-shaped mixed-rate cache)
+C4_LAYERS, C4_KV, C4_B, C4_S, C4_D, C4_G = 28, 4, 4, 131072, 128, 7
 # DRAM bytes (read + write) per E8 block of each codec phase and per
 # compressed byte of the attention kernel, measured with ncu
 # (dram__bytes_read.sum + dram__bytes_write.sum) on the 8-layer config-2 case
@@ -314,6 +324,115 @@ def bench_attention(dev, rank, world, steps, warmup, barrier):
             "gpu_launches": steps * (2 + (1 if world > 1 else 0)), "cpu_baseline": cpu}
 
 
+def c4_bits():
+    """Per-layer (K, V) bits: seeded draw from {3, 4, 5} with exactly 3 layers at 5."""
+    import numpy as np
+
+    rng = np.random.default_rng(44)
+    five = set(rng.choice(C4_LAYERS, 3, replace=False).tolist())
+    return [5 if l in five else int(rng.choice([3, 4])) for l in range(C4_LAYERS)]
+
+
+def c4_tensor(dev, seed, heads, student):
+    import torch
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    shape = (C4_B, heads, C4_S, C4_D)
+    z = torch.randn(shape, generator=g, device=dev)
+    if student:  # t(3) = z / sqrt(chi2(3) / 3)
+        chi = sum(torch.randn(shape, generator=g, device=dev) ** 2 for _ in range(3))
+        z = z / torch.sqrt(chi / 3)
+    return z.to(torch.bfloat16)
+
+
+def bench_config4(dev, rank, world, steps, barrier):
+    """Config 4 on `world` ranks: (layer, KV head) units round-robin, encode of
+    every owned unit, then decode-attention steps over every owned layer."""
+    import torch
+    import torch.distributed as dist
+
+    from latticequant_b200 import attention as A
+    from latticequant_b200 import codec as C
+    from latticequant_b200 import sharding as SH
+
+    bits = c4_bits()
+    units = SH.shard_units(C4_LAYERS, C4_KV, world, rank)
+    layers = {}
+    for l, h in units:
+        layers.setdefault(l, []).append(h)
+    st = torch.cuda.current_stream(dev)
+    chunks, blocks, comp, meta, n_out = [], 0, 0, 0, 0
+    enc_ms = 0.0
+    for l, heads in sorted(layers.items()):
+        # the owned heads of this layer, generated per (layer, head) so shards do not depend on N
+        k = torch.cat([c4_tensor(dev, 5000 + 16 * l + h, 1, True) for h in heads], 1)
+        v = torch.cat([c4_tensor(dev, 9000 + 16 * l + h, 1, False) for h in heads], 1)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        kc, _ = C.compress(k, bits[l], tile_blocks=TILE)
+        vc, _ = C.compress(v, bits[l], tile_blocks=TILE)
+        e1.record(st)
+        torch.cuda.synchronize()
+        enc_ms += e0.elapsed_time(e1)
+        blocks += 2 * k.numel() // 8
+        comp += kc.compressed_bytes() + vc.compressed_bytes()
+        meta += kc.metadata_bytes() + vc.metadata_bytes()
+        n_out += kc.n_outliers + vc.n_outliers
+        chunks.append((l, len(heads), A.DecodeAttention(kc, vc, C4_G)))
+        del k, v
+    g = torch.Generator(device=dev)
+    g.manual_seed(6006)
+    qs = {l: (torch.randn(C4_B, nh * C4_G, C4_D, generator=g, device=dev) / C4_D ** 0.5).to(torch.bfloat16)
+          for l, nh, _ in chunks}
+    outs = {l: torch.empty(C4_B, nh * C4_G, C4_D, dtype=torch.bfloat16, device=dev) for l, nh, _ in chunks}
+
+    def step():
+        for l, nh, op in chunks:
+            op(qs[l], outs[l])
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    for _, _, op in chunks:
+        if op.flags():
+            raise RuntimeError(f"config-4 attention error flags {op.flags():#x}")
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(steps):
+        step()
+    e1.record(st)
+    torch.cuda.synchronize()
+    att_ms = e0.elapsed_time(e1) / steps
+    vals = torch.tensor([enc_ms, att_ms, float(blocks), float(comp), float(meta), float(n_out)], dtype=torch.float64,
+                        device=dev)
+    if world > 1:
+        mx, sm = vals[:2].clone(), vals[2:].clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        vals = torch.cat([mx, sm])
+    enc_ms, att_ms, blocks, comp, meta, n_out = vals.tolist()
+    if rank != 0:
+        return None
+    peak, peak_kind = measured_peaks()
+    att_bytes = comp + meta + 2 * 2 * C4_B * C4_LAYERS * C4_KV * C4_G * C4_D
+    return {"workload": "config4: Qwen2.5-7B KV 28L x 4 kv-heads x D128, B4, ctx 131072, bits per layer "
+                        f"{bits} (K Student-t(3), V N(0,1))",
+            "parallelism": f"(layer, kv-head) units round-robin over {world} ranks, no collective",
+            "encode": {"metric": "E8+rANS encode Gvec/s", "value": blocks / (enc_ms * 1e-3) / 1e9, "unit": "Gvec/s",
+                       "ms": enc_ms, "note": "whole model, through codec.compress (includes its host syncs)"},
+            "attention": {"metric": A_METRIC, "value": att_bytes / (att_ms * 1e-3) / 1e9, "unit": "GB/s",
+                          "ms_per_step": att_ms, "tokens_per_s": C4_B * 1e3 / att_ms,
+                          "roofline": {"bound": "hbm", "achieved": att_bytes / (att_ms * 1e-3) / 1e9 / world,
+                                       "peak": peak, "unit": "GB/s per GPU",
+                                       "frac": att_bytes / (att_ms * 1e-3) / 1e9 / world / peak,
+                                       "peak_kind": peak_kind}},
+            "bits_per_dim": comp * 8 / (blocks * 8), "outlier_records": int(n_out),
+            "gpu_launches": steps * 2 * len(chunks) * world}
+
+
 def run_reference(args):
     """--impl reference: the reference's CPU path (C oracle port) on the host cores."""
     rank = int(os.environ.get("RANK", "0"))
@@ -358,6 +477,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-attn", action="store_true", help="skip the config-3 attention measurement")
     ap.add_argument("--e2e-group", type=int, default=E2E_GROUP, help="chunks per pipelined e2e transfer group")
+    ap.add_argument("--no-c4", action="store_true", help="skip the config-4 mixed-rate measurement")
     ap.add_argument("--layers", type=int, default=N_LAYERS,
                     help="layers of the cache (profiling runs use fewer; bench lines use 32)")
     args = ap.parse_args()
@@ -554,6 +674,10 @@ def main():
         cd = None
         torch.cuda.empty_cache()
         attn = bench_attention(dev, rank, world, args.steps, args.warmup, barrier)
+    c4 = None
+    if not args.no_c4:
+        torch.cuda.empty_cache()
+        c4 = bench_config4(dev, rank, world, max(2, min(args.steps, 5)), barrier)
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -571,7 +695,7 @@ def main():
                              "traffic": (TRAFFIC_PER_BLOCK[dom] * BLOCKS / 1e9) if dom in TRAFFIC_PER_BLOCK else None,
                              "traffic_unit": "GB per launch", "algorithmic_GB": alg[dom] / 1e9},
                 "clocks": clocks, "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
-                "cpu_baseline": cpu, "attention": attn}
+                "cpu_baseline": cpu, "attention": attn, "config4": c4}
         print(json.dumps(line), flush=True)
     if graph is not None:
         del graph
