@@ -49,6 +49,7 @@ struct AttnArgs {
     float qk_log2;        // sm_scale * log2(e)
     float *part;          // [heads][nct][G][D + 2]: o (unnormalised), m, l
     const uint32_t *tok_mask;  // optional [heads][ceil(seq/32)] tokens to leave out
+    uint32_t *redo;            // [heads][nct]: 1 where a lane of the CTA read past its bits
     uint32_t *err;
 };
 
@@ -62,9 +63,14 @@ __host__ __device__ constexpr int attn_threads() {
     return G <= 2 ? 768 : G <= 4 ? 640 : 512;
 }
 
-// Fused attention partials.  BPT = blocks per token = head_dim / 8.
-template <int G, int BPT, int QDT>
-__global__ void __launch_bounds__(attn_threads<G, BPT>(), 1) attn_partial_kernel(AttnArgs a) {
+// Fused attention partial of CTA `cx` of head `head`.  BPT = blocks per
+// token = head_dim / 8.  CHECKED = false decodes optimistically and records
+// in a.redo whether a lane read past its bits (only a malformed stream
+// does); attn_redo_kernel then recomputes those CTAs with CHECKED = true.
+// Keeping the exact decode out of the main kernel keeps that kernel to one
+// copy of the decoder and within its registers.
+template <int G, int BPT, int QDT, bool CHECKED>
+__device__ __forceinline__ void attn_partial_cta(const AttnArgs &a, uint32_t cx, uint32_t head) {
     static_assert(BPT == 8 || BPT == 16, "head_dim 64 or 128");
     static_assert(G >= 1 && G <= 8, "query group 1..8");
     constexpr int D = 8 * BPT, GP = padded_g<G>(), TPG = 16 / BPT;
@@ -77,9 +83,8 @@ __global__ void __launch_bounds__(attn_threads<G, BPT>(), 1) attn_partial_kernel
     const uint32_t dta = smem_addr(dtab);
     float *sc = reinterpret_cast<float *>(wb + (kAttnRing + 2) * kRingStride * 2);
 
-    const uint32_t head = blockIdx.y;
-    const uint32_t pb = (uint32_t)(((uint64_t)blockIdx.x * a.n_pairs) / a.nct);
-    const uint32_t pe = (uint32_t)(((uint64_t)(blockIdx.x + 1) * a.n_pairs) / a.nct);
+    const uint32_t pb = (uint32_t)(((uint64_t)cx * a.n_pairs) / a.nct);
+    const uint32_t pe = (uint32_t)(((uint64_t)(cx + 1) * a.n_pairs) / a.nct);
     const uint32_t pair = pb + (uint32_t)warp;
     const bool wact = pair < pe;
     const bool act0 = wact, act1 = wact && 2 * pair + 1 < a.tph;
@@ -107,63 +112,65 @@ __global__ void __launch_bounds__(attn_threads<G, BPT>(), 1) attn_partial_kernel
     }
 
     // ---- phase K: scores
+    // set when a lane of the CTA read past its bits (optimistic decode only)
+    __shared__ uint32_t s_overrun;
+    if (threadIdx.x == 0) s_overrun = 0u;
     stage_tables(a.k, 0, dtab);
     __syncthreads();
     if (wact) {
-        decode_two_tiles_ordered<kAttnRing>(
-            a.k, 0, tile0, act0, act1, dta, ring,
-            [&](bool ok, int t, uint32_t grp, uint32_t j, uint32_t cc, const uint4 blk) {
-                float kq[8];
-                ring_point(blk, kq);
-                // per-lane partial dots over its 8 channels, i in order, two heads per fma.rn.f32x2
-                float dot[G];
+        auto epi_k = [&](bool ok, int t, uint32_t grp, uint32_t j, uint32_t cc, const uint4 blk) {
+            float kq[8];
+            ring_point(blk, kq);
+            // per-lane partial dots over its 8 channels, i in order, two heads per fma.rn.f32x2
+            float dot[G];
 #pragma unroll
-                for (int g = 0; g + 1 < G; g += 2) {
-                    unsigned long long s2 = f2_mul(q2[g / 2][0], f2_pack(kq[0], kq[0]));
+            for (int g = 0; g + 1 < G; g += 2) {
+                unsigned long long s2 = f2_mul(q2[g / 2][0], f2_pack(kq[0], kq[0]));
 #pragma unroll
-                    for (int i = 1; i < 8; ++i) s2 = f2_fma(q2[g / 2][i], f2_pack(kq[i], kq[i]), s2);
-                    f2_unpack(s2, dot[g], dot[g + 1]);
+                for (int i = 1; i < 8; ++i) s2 = f2_fma(q2[g / 2][i], f2_pack(kq[i], kq[i]), s2);
+                f2_unpack(s2, dot[g], dot[g + 1]);
+            }
+            if constexpr (G % 2) {
+                float s = __fmul_rn(qlast[0], kq[0]);
+#pragma unroll
+                for (int i = 1; i < 8; ++i) s = __fmaf_rn(qlast[i], kq[i], s);
+                dot[G - 1] = s;
+            }
+#pragma unroll
+            for (int g = 0; g < G; ++g) dot[g] = ok ? dot[g] : 0.f;
+            const uint32_t jc = j % BPT;
+            const uint32_t tok = grp * TPG + j / BPT;
+            float *row = sc + ((uint32_t)t * a.tpt + tok) * GP;
+            if constexpr (G == 4 && BPT == 16) {
+                // transposing reduction over the token's 16 lanes: halve the
+                // heads a lane carries at each of the first two steps
+                const bool h8 = (jc & 8u) != 0, h4 = (jc & 4u) != 0;
+                float a0 = h8 ? dot[2] : dot[0], a1 = h8 ? dot[3] : dot[1];
+                const float s0 = h8 ? dot[0] : dot[2], s1 = h8 ? dot[1] : dot[3];
+                a0 += __shfl_xor_sync(0xffffffffu, s0, 8);
+                a1 += __shfl_xor_sync(0xffffffffu, s1, 8);
+                float bsum = h4 ? a1 : a0;
+                bsum += __shfl_xor_sync(0xffffffffu, h4 ? a0 : a1, 4);
+                bsum += __shfl_xor_sync(0xffffffffu, bsum, 2);
+                bsum += __shfl_xor_sync(0xffffffffu, bsum, 1);
+                // lane jc holds head (jc >> 2) & 3 (bit 3 picked heads 2-3, bit 2 the odd one)
+                if (ok && (jc & 3u) == 0) row[jc >> 2] = bsum;
+            } else {
+#pragma unroll
+                for (int off = BPT / 2; off >= 1; off >>= 1) {
+#pragma unroll
+                    for (int g = 0; g < G; ++g) dot[g] += __shfl_xor_sync(0xffffffffu, dot[g], off);
                 }
-                if constexpr (G % 2) {
-                    float s = __fmul_rn(qlast[0], kq[0]);
+                if (ok && jc < (uint32_t)G) {
+                    float v = dot[0];
 #pragma unroll
-                    for (int i = 1; i < 8; ++i) s = __fmaf_rn(qlast[i], kq[i], s);
-                    dot[G - 1] = s;
+                    for (int g = 1; g < G; ++g) v = (jc == (uint32_t)g) ? dot[g] : v;
+                    row[jc] = v;
                 }
-#pragma unroll
-                for (int g = 0; g < G; ++g) dot[g] = ok ? dot[g] : 0.f;
-                const uint32_t jc = j % BPT;
-                const uint32_t tok = grp * TPG + j / BPT;
-                float *row = sc + ((uint32_t)t * a.tpt + tok) * GP;
-                if constexpr (G == 4 && BPT == 16) {
-                    // transposing reduction over the token's 16 lanes: halve the
-                    // heads a lane carries at each of the first two steps
-                    const bool h8 = (jc & 8u) != 0, h4 = (jc & 4u) != 0;
-                    float a0 = h8 ? dot[2] : dot[0], a1 = h8 ? dot[3] : dot[1];
-                    const float s0 = h8 ? dot[0] : dot[2], s1 = h8 ? dot[1] : dot[3];
-                    a0 += __shfl_xor_sync(0xffffffffu, s0, 8);
-                    a1 += __shfl_xor_sync(0xffffffffu, s1, 8);
-                    float bsum = h4 ? a1 : a0;
-                    bsum += __shfl_xor_sync(0xffffffffu, h4 ? a0 : a1, 4);
-                    bsum += __shfl_xor_sync(0xffffffffu, bsum, 2);
-                    bsum += __shfl_xor_sync(0xffffffffu, bsum, 1);
-                    // lane jc holds head (jc >> 2) & 3 (bit 3 picked heads 2-3, bit 2 the odd one)
-                    if (ok && (jc & 3u) == 0) row[jc >> 2] = bsum;
-                } else {
-#pragma unroll
-                    for (int off = BPT / 2; off >= 1; off >>= 1) {
-#pragma unroll
-                        for (int g = 0; g < G; ++g) dot[g] += __shfl_xor_sync(0xffffffffu, dot[g], off);
-                    }
-                    if (ok && jc < (uint32_t)G) {
-                        float v = dot[0];
-#pragma unroll
-                        for (int g = 1; g < G; ++g) v = (jc == (uint32_t)g) ? dot[g] : v;
-                        row[jc] = v;
-                    }
-                }
-            },
-            a.err);
+            }
+        };
+        if (decode_two_tiles_ordered<kAttnRing, CHECKED>(a.k, 0, tile0, act0, act1, dta, ring, epi_k, a.err))
+            s_overrun = 1u;
     }
     __syncwarp();
 
@@ -240,34 +247,33 @@ __global__ void __launch_bounds__(attn_threads<G, BPT>(), 1) attn_partial_kernel
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc2[g][i] = 0ull;
     if (wact) {
-        decode_two_tiles_ordered<kAttnRing>(
-            a.v, 0, tile0, act0, act1, dta, ring,
-            [&](bool ok, int t, uint32_t grp, uint32_t j, uint32_t cc, const uint4 blk) {
-                if (!ok) return;
-                float vq[8];
-                ring_point(blk, vq);
-                const uint32_t tok = grp * TPG + j / BPT;
-                const float *pp = sc + ((uint32_t)t * a.tpt + tok) * GP;
-                float p[GP];
+        auto epi_v = [&](bool ok, int t, uint32_t grp, uint32_t j, uint32_t cc, const uint4 blk) {
+            if (!ok) return;
+            float vq[8];
+            ring_point(blk, vq);
+            const uint32_t tok = grp * TPG + j / BPT;
+            const float *pp = sc + ((uint32_t)t * a.tpt + tok) * GP;
+            float p[GP];
 #pragma unroll
-                for (int g4 = 0; g4 < GP; g4 += 4) {
-                    const float4 f = *reinterpret_cast<const float4 *>(pp + g4);
-                    p[g4] = f.x;
-                    p[g4 + 1] = f.y;
-                    p[g4 + 2] = f.z;
-                    p[g4 + 3] = f.w;
-                }
-                unsigned long long v2[4];
+            for (int g4 = 0; g4 < GP; g4 += 4) {
+                const float4 f = *reinterpret_cast<const float4 *>(pp + g4);
+                p[g4] = f.x;
+                p[g4 + 1] = f.y;
+                p[g4 + 2] = f.z;
+                p[g4 + 3] = f.w;
+            }
+            unsigned long long v2[4];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) v2[i] = f2_pack(vq[2 * i], vq[2 * i + 1]);
+            for (int i = 0; i < 4; ++i) v2[i] = f2_pack(vq[2 * i], vq[2 * i + 1]);
 #pragma unroll
-                for (int g = 0; g < G; ++g) {
-                    const unsigned long long pg = f2_pack(p[g], p[g]);
+            for (int g = 0; g < G; ++g) {
+                const unsigned long long pg = f2_pack(p[g], p[g]);
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) acc2[g][i] = f2_fma(pg, v2[i], acc2[g][i]);
-                }
-            },
-            a.err);
+                for (int i = 0; i < 4; ++i) acc2[g][i] = f2_fma(pg, v2[i], acc2[g][i]);
+            }
+        };
+        if (decode_two_tiles_ordered<kAttnRing, CHECKED>(a.v, 0, tile0, act0, act1, dta, ring, epi_v, a.err))
+            s_overrun = 1u;
     }
     float acc[G][8];
 #pragma unroll
@@ -285,6 +291,7 @@ __global__ void __launch_bounds__(attn_threads<G, BPT>(), 1) attn_partial_kernel
 
     // ---- merge the warps in a fixed order
     __syncthreads();  // every warp is done with the V tables: the region holds the merge buffer
+    if (!CHECKED && threadIdx.x == 0) a.redo[head * a.nct + cx] = s_overrun;
     float *mrg = reinterpret_cast<float *>(smem);
     const int rs = D + 2;
     if (lane < (uint32_t)BPT) {
@@ -302,7 +309,7 @@ __global__ void __launch_bounds__(attn_threads<G, BPT>(), 1) attn_partial_kernel
     }
     __syncthreads();
     const float cv = a.scale_tok ? 1.0f : __half2float(__ushort_as_half(a.v.scale_f16[head]));
-    float *out = a.part + ((size_t)head * a.nct + blockIdx.x) * G * rs;
+    float *out = a.part + ((size_t)head * a.nct + cx) * G * rs;
     for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
         const int g = e / D, dd = e % D;
         float mx = -INFINITY;
@@ -320,6 +327,22 @@ __global__ void __launch_bounds__(attn_threads<G, BPT>(), 1) attn_partial_kernel
             out[g * rs + D] = mx;
             out[g * rs + D + 1] = ls;
         }
+    }
+}
+
+template <int G, int BPT, int QDT>
+__global__ void __launch_bounds__(attn_threads<G, BPT>(), 1) attn_partial_kernel(AttnArgs a) {
+    attn_partial_cta<G, BPT, QDT, false>(a, blockIdx.x, blockIdx.y);
+}
+
+// The CTAs the optimistic pass flagged, again with the exact decode (their
+// partials are overwritten); a grid of at most one CTA per SM walks them.
+template <int G, int BPT, int QDT>
+__global__ void __launch_bounds__(attn_threads<G, BPT>(), 1) attn_redo_kernel(AttnArgs a, uint32_t n_cta) {
+    for (uint32_t c = blockIdx.x; c < n_cta; c += gridDim.x) {
+        if (a.redo[c] == 0u) continue;  // the same for every thread of the CTA
+        __syncthreads();                // the previous CTA's merge buffer is read out
+        attn_partial_cta<G, BPT, QDT, true>(a, c % a.nct, c / a.nct);
     }
 }
 
@@ -383,6 +406,7 @@ struct AttnPlan {
     int nwarps;
     uint32_t nct, n_pairs, tph, tpt, region0, warp_bytes;
     size_t smem, part_floats;
+    size_t redo_off, ws_bytes;  // workspace: partials, then the redo flags
 };
 
 size_t attn_warp_bytes(int G, uint32_t tpt) {
@@ -412,6 +436,8 @@ int attn_plan(int64_t n_heads, int64_t bph, int64_t tile_blocks, int G, int D, A
     p->smem = p->region0 + (size_t)nw * wb;
     p->nct = (uint32_t)ceil_div(p->n_pairs, nw);
     p->part_floats = (size_t)n_heads * p->nct * G * (D + 2);
+    p->redo_off = (p->part_floats * 4 + 255) & ~(size_t)255;
+    p->ws_bytes = p->redo_off + (((size_t)n_heads * p->nct * 4 + 255) & ~(size_t)255);
     return LQ_OK;
 }
 
@@ -421,6 +447,16 @@ int launch_partial(const AttnArgs &a, const AttnPlan &p, uint32_t n_heads, cudaS
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem) != cudaSuccess)
         return LQ_ERR_CUDA;
     kern<<<dim3(p.nct, n_heads), 32 * p.nwarps, p.smem, st>>>(a);
+    int rc = check_launch();
+    if (rc != LQ_OK) return rc;
+    auto redo = attn_redo_kernel<G, BPT, QDT>;
+    if (cudaFuncSetAttribute(redo, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem) != cudaSuccess)
+        return LQ_ERR_CUDA;
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return LQ_ERR_CUDA;
+    const uint32_t n_cta = p.nct * n_heads;
+    redo<<<std::min<uint32_t>(n_cta, (uint32_t)std::max(sms, 1)), 32 * p.nwarps, p.smem, st>>>(a, n_cta);
     return check_launch();
 }
 
@@ -462,7 +498,7 @@ extern "C" size_t lq_attn_decode_workspace(int64_t n_heads, int64_t bph, int64_t
                                            int head_dim) {
     AttnPlan p;
     if (attn_plan(n_heads, bph, tile_blocks, group, head_dim, &p) != LQ_OK) return 0;
-    return (p.part_floats * 4 + 255) & ~(size_t)255;
+    return p.ws_bytes;
 }
 
 extern "C" int lq_attn_decode(const lq_chunk_view *k, const lq_chunk_view *v, const void *q, int q_dtype,
@@ -483,7 +519,7 @@ extern "C" int lq_attn_decode(const lq_chunk_view *k, const lq_chunk_view *v, co
     AttnPlan p;
     const int rc = attn_plan(heads, bph, k->tile_blocks, group, head_dim, &p);
     if (rc != LQ_OK) return rc;
-    if (workspace_bytes < p.part_floats * 4) return LQ_ERR_CAPACITY;
+    if (workspace_bytes < p.ws_bytes) return LQ_ERR_CAPACITY;
     if (out_dtype != LQ_F32 && out_dtype != LQ_F16 && out_dtype != LQ_BF16) return LQ_ERR_INVALID;
     cudaStream_t st = as_stream(stream);
     AttnArgs a;
@@ -502,6 +538,7 @@ extern "C" int lq_attn_decode(const lq_chunk_view *k, const lq_chunk_view *v, co
     a.qk_log2 = sm_scale * kLog2e;
     a.part = static_cast<float *>(workspace);
     a.tok_mask = tok_mask;
+    a.redo = reinterpret_cast<uint32_t *>(static_cast<unsigned char *>(workspace) + p.redo_off);
     a.err = err;
     const uint32_t nh = (uint32_t)heads;
     int r;

@@ -433,29 +433,30 @@ __global__ void __launch_bounds__(1024, 1) decode_fused_kernel(ChunkDev a, FastD
     const uint32_t tile0 = (blockIdx.x * nwarps + (threadIdx.x >> 5)) * 2;
     if (tile0 >= a.n_tiles) return;
     const uint32_t N = a.n_heads * a.bph;
-    decode_two_tiles_ordered<kDecR>(
-        a, chunk, tile0, true, true, smem_addr(dtab), ring,
-        [&](bool ok, int t, uint32_t grp, uint32_t j, uint32_t cc, const uint4 blk) {
-            if (!ok) return;
-            const uint32_t b = (tile0 + t) * a.TB + grp * 16 + j;
-            const size_t gb = (size_t)chunk * N + b;
-            if (sym_out) {
-                int sym[8];
-                ring_symbols(blk, cc, sym);
-                int4 *so = reinterpret_cast<int4 *>(sym_out) + 2 * gb;
-                so[0] = make_int4(sym[0], sym[1], sym[2], sym[3]);
-                so[1] = make_int4(sym[4], sym[5], sym[6], sym[7]);
-            }
-            if constexpr (DO >= 0) {
-                float q[8];
-                ring_point(blk, q);
-                const float sc = __half2float(__ushort_as_half(a.scale_f16[chunk * a.n_heads + bph_div.div(b)]));
+    auto epi = [&](bool ok, int t, uint32_t grp, uint32_t j, uint32_t cc, const uint4 blk) {
+        if (!ok) return;
+        const uint32_t b = (tile0 + t) * a.TB + grp * 16 + j;
+        const size_t gb = (size_t)chunk * N + b;
+        if (sym_out) {
+            int sym[8];
+            ring_symbols(blk, cc, sym);
+            int4 *so = reinterpret_cast<int4 *>(sym_out) + 2 * gb;
+            so[0] = make_int4(sym[0], sym[1], sym[2], sym[3]);
+            so[1] = make_int4(sym[4], sym[5], sym[6], sym[7]);
+        }
+        if constexpr (DO >= 0) {
+            float q[8];
+            ring_point(blk, q);
+            const float sc = __half2float(__ushort_as_half(a.scale_f16[chunk * a.n_heads + bph_div.div(b)]));
 #pragma unroll
-                for (int i = 0; i < 8; ++i) q[i] = __fmul_rn(q[i], sc);
-                store_block8<DO>(out, gb, q);
-            }
-        },
-        err);
+            for (int i = 0; i < 8; ++i) q[i] = __fmul_rn(q[i], sc);
+            store_block8<DO>(out, gb, q);
+        }
+    };
+    // optimistic decode; a warp whose lanes read past their bits writes its
+    // blocks again from the exact decode (every block is overwritten)
+    if (decode_two_tiles_ordered<kDecR, false>(a, chunk, tile0, true, true, smem_addr(dtab), ring, epi, err))
+        decode_two_tiles_ordered<kDecR, true>(a, chunk, tile0, true, true, smem_addr(dtab), ring, epi, err);
 }
 
 // ---------------------------------------------------------------- reference streams

@@ -312,14 +312,21 @@ struct LaneDec {
     }
 
     // decode `cnt` symbols to shared addresses dst, dst + sb, dst + 2*sb, ...
-    // (sb = one ring row)
+    // (sb = one ring row).  CHECKED: a group runs table-driven only while all
+    // three steps stay inside the lane, the rest literally, so every stream
+    // decodes exactly as the reference decodes it.  Unchecked: table-driven
+    // groups throughout (single steps for a remainder of one or two), which
+    // is exact for every stream whose decode never reads past n_bits -- every
+    // stream an encoder wrote; consumed() > nb after the lane's last symbol
+    // tells afterwards that it did not hold.
+    template <bool CHECKED>
     __device__ __forceinline__ void run(int cnt, uint32_t dst) {
         constexpr uint32_t sb = kRingStride * 2;
         int j = 0;
         if (fast_ok) {
-            // groups of three table-driven steps while all three stay inside the lane
-            const int lim = (int)nb - 30;
-            for (; j + 3 <= cnt && consumed() <= lim; j += 3) {
+            const int lim = CHECKED ? (int)nb - 30 : 0x7fffffff;
+#pragma unroll 1
+            for (; j + 3 <= cnt && (!CHECKED || consumed() <= lim); j += 3) {
                 fast_group(dst);
                 dst += 3 * sb;
             }
@@ -337,14 +344,19 @@ struct LaneDec {
 // new symbols within R (at least one group, since a group holds 16 blocks):
 // the 8 lanes of each coset own exactly the symbols of those groups in ring
 // rows 0.., and then every lane j of the half takes block 16*group + j.
-// Lanes decode in whole groups of three steps; the one or two symbols a lane
-// decodes past the round's need are carried to rows 0.. of the next round.
+// Lanes decode in whole groups of three steps (except at the lane's end); the
+// one or two symbols a lane decodes past the round's need are carried to rows
+// 0.. of the next round.
 // All 32 lanes call epi(ok, t, group, j, coset, block) together once per
 // group step (ok = false for a lane without a block), so the epilogue may
 // use warp shuffles; blocks reach it in increasing position order per lane.
+// CHECKED = false decodes optimistically (LaneDec::run) and returns whether
+// any lane of the warp read past its n_bits, in which case the blocks it
+// handed out may differ from the reference decode and the caller decodes the
+// same tiles again with CHECKED = true (which always returns false).
 // `ring` is (R + 2) rows of kRingStride u16.
-template <int R, class Epi>
-__device__ __forceinline__ void decode_two_tiles_ordered(const ChunkDev &a, uint32_t chunk, uint32_t tile0, bool act0,
+template <int R, bool CHECKED, class Epi>
+__device__ __forceinline__ bool decode_two_tiles_ordered(const ChunkDev &a, uint32_t chunk, uint32_t tile0, bool act0,
                                                          bool act1, uint32_t dtab, uint32_t ring, Epi &&epi,
                                                          uint32_t *err) {
     static_assert(R >= 16 && (R + 2) * kRingStride * 2 < 65536, "ring rows");
@@ -360,7 +372,9 @@ __device__ __forceinline__ void decode_two_tiles_ordered(const ChunkDev &a, uint
     const uint32_t *cw = a.coset_words + (size_t)chunk * wpc + (size_t)(act ? tile : 0u) * (TB >> 5);
     const uint32_t col = ring + lane * 2;
     LaneDec d;
-    const int n = d.init(a, chunk, act ? tile : 0u, j, dtab, act ? (int)(c ? tb - n0 : n0) : 0, err);
+    // symbols of the lane not yet decoded (0 for a lane without symbols or
+    // with a bad table or word range: it decodes nothing)
+    int left = d.init(a, chunk, act ? tile : 0u, j, dtab, act ? (int)(c ? tb - n0 : n0) : 0, err);
     uint32_t gpos = 0;
     int ahead = 0, prev = 0;  // symbols decoded past the last round's need, at rows prev..
     for (;;) {
@@ -392,15 +406,19 @@ __device__ __forceinline__ void decode_two_tiles_ordered(const ChunkDev &a, uint
         const int last = (int)hb + max(ng, 1) - 1;
         const int n1r = __shfl_sync(0xffffffffu, p1, last);
         const int n0r = __shfl_sync(0xffffffffu, p0, last);
-        const int cnt = (ng > 0 && n > 0) ? (c ? n1r : n0r) : 0;
+        // a lane with symbols still to decode or to hand out takes its coset's count
+        const int cnt = (ng > 0 && (left > 0 || ahead > 0)) ? (c ? n1r : n0r) : 0;
         if (ahead > 0 && prev > 0) {  // carried symbols to rows 0, 1 (forward copy)
             sts_u16(col, lds_u16(col + (uint32_t)prev * kRow));
             if (ahead > 1) sts_u16(col + kRow, lds_u16(col + (uint32_t)(prev + 1) * kRow));
         }
         const int need = cnt - ahead;
         if (need > 0) {
-            const int dec = (need + 2) / 3 * 3;
-            d.run(dec, col + (uint32_t)ahead * kRow);
+            // whole groups of three, but never past the lane's last symbol,
+            // so a lane reads no bit beyond its stream unless it is malformed
+            const int dec = min((need + 2) / 3 * 3, left);
+            d.run<CHECKED>(dec, col + (uint32_t)ahead * kRow);
+            left -= dec;
             ahead += dec - cnt;
         } else {
             ahead = -need;
@@ -424,6 +442,8 @@ __device__ __forceinline__ void decode_two_tiles_ordered(const ChunkDev &a, uint
         __syncwarp();
         gpos += (uint32_t)ng;
     }
+    // (a lane without symbols has consumed 0 bits)
+    return !CHECKED && __any_sync(0xffffffffu, d.consumed() > (int)d.nb);
 }
 
 }  // namespace lq
