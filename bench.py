@@ -433,6 +433,97 @@ def bench_config4(dev, rank, world, steps, barrier):
             "gpu_launches": steps * 3 * len(chunks) * world}
 
 
+C5_METRIC = "decode tok/s"
+
+
+def bench_config5(dev, rank, world, args, barrier):
+    """a random-init Llama-3.1-8B-architecture model (bf16
+    weights N(0, 0.02), replicated on every rank) decoding through
+    CompressedAttentionKVCache at 4 bits/dim: prefill of seeded random ids,
+    then greedy tokens, each decode step attending over the compressed cache
+    with the fused kernels.  At N > 1 the cache is sharded by KV head
+    (sharding.head_slice); every layer all-gathers the heads' outputs.  The
+    timed region covers the decode steps after `warmup` of them, including a
+    per-step copy of the new token ids to pinned host memory."""
+    import time
+
+    import torch
+    import torch.distributed as dist
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    from latticequant_b200 import sharding as SH
+    from latticequant_b200.llm.compressed_attention import CompressedAttentionKVCache
+
+    L, B, P, T, W = args.c5_layers, args.c5_batch, args.c5_prefill, args.c5_gen, args.warmup
+    if T <= W:
+        raise ValueError("--c5-gen must exceed --warmup")
+    cfg = LlamaConfig(vocab_size=128256, hidden_size=4096, intermediate_size=14336, num_hidden_layers=L,
+                      num_attention_heads=32, num_key_value_heads=8, max_position_embeddings=131072,
+                      rope_theta=500000.0, initializer_range=0.02, rms_norm_eps=1e-5, tie_word_embeddings=False)
+    torch.manual_seed(5005)  # the same weights on every rank
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        with torch.device(dev):
+            model = LlamaForCausalLM(cfg)
+    finally:
+        torch.set_default_dtype(prev)
+    model.eval()
+    g = torch.Generator(device=dev)
+    g.manual_seed(5006)
+    ids = torch.randint(0, cfg.vocab_size, (B, P), generator=g, device=dev)
+    hr = SH.head_slice(cfg.num_key_value_heads, world, rank) if world > 1 else None
+    cache = CompressedAttentionKVCache(4, tail_tokens=64, head_range=hr).bind(model)
+    host = torch.empty(T, B, dtype=torch.int64, pin_memory=True)
+    st = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.no_grad():
+        barrier()
+        torch.cuda.synchronize()
+        t0 = time.time()
+        out = model(ids, past_key_values=cache, use_cache=True, logits_to_keep=1)
+        nxt = out.logits[:, -1].argmax(-1, keepdim=True)
+        del out
+        torch.cuda.synchronize()
+        prefill_s = time.time() - t0
+        for i in range(T):
+            if i == W:
+                barrier()
+                torch.cuda.synchronize()
+                e0.record(st)
+            out = model(nxt, past_key_values=cache, use_cache=True)
+            nxt = out.logits[:, -1].argmax(-1, keepdim=True)
+            host[i].copy_(nxt.view(-1), non_blocking=True)
+            del out
+        e1.record(st)
+        torch.cuda.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    flags = cache.flags()
+    if flags:
+        raise RuntimeError(f"config-5 attention error flags {flags:#x}")
+    steps = T - W
+    comp = sum(l.total_bytes for l in cache._comp_keys + cache._comp_values if l is not None)
+    mem = torch.cuda.max_memory_allocated(dev)
+    if rank != 0:
+        return None
+    return {"metric": C5_METRIC, "value": B * steps * 1e3 / ms, "unit": "tok/s", "n_gpus": world, "steps": steps,
+            "warmup": W, "ms_per_step": ms / steps, "higher_is_better": True, "scaling": "strong",
+            "dtype": "bf16", "data": "synthetic (random-init weights N(0,0.02), seeded random token ids)",
+            "config": {"workload": f"config5: Llama-3.1-8B architecture ({L} layers, 4096 hidden, 32 q / 8 kv heads), "
+                                   f"batch {B}, prefill {P} random ids, {T} generated tokens, 4 b/dim KV",
+                       "parallelism": f"KV-head-sharded cache over {world} GPUs (weights replicated, per-layer "
+                                      "all-gather of attention heads)" if world > 1 else "single GPU",
+                       "global_batch": B, "seq_len": P + T},
+            "prefill_s": prefill_s, "compressed_cache_GB_rank0": comp / 1e9,
+            "max_memory_GB_rank0": mem / 1e9,
+            "e2e": {"value": B * steps * 1e3 / ms, "unit": "tok/s", "h2d_bytes_per_step": B * 8,
+                    "d2h_bytes_per_step": B * 8,
+                    "note": "decode steps with the token ids copied to pinned host memory each step"}}
+
+
 def run_reference(args):
     """--impl reference: the reference's CPU path (C oracle port) on the host cores."""
     rank = int(os.environ.get("RANK", "0"))
@@ -478,6 +569,12 @@ def main():
     ap.add_argument("--no-attn", action="store_true", help="skip the config-3 attention measurement")
     ap.add_argument("--e2e-group", type=int, default=E2E_GROUP, help="chunks per pipelined e2e transfer group")
     ap.add_argument("--no-c4", action="store_true", help="skip the config-4 mixed-rate measurement")
+    ap.add_argument("--only-c5", action="store_true",
+                    help="run only config 5 (Llama-3.1-8B-shaped decode through the compressed cache) and print its line")
+    ap.add_argument("--c5-layers", type=int, default=32)
+    ap.add_argument("--c5-batch", type=int, default=32)
+    ap.add_argument("--c5-prefill", type=int, default=16384)
+    ap.add_argument("--c5-gen", type=int, default=256)
     ap.add_argument("--layers", type=int, default=N_LAYERS,
                     help="layers of the cache (profiling runs use fewer; bench lines use 32)")
     args = ap.parse_args()
@@ -502,6 +599,14 @@ def main():
     def barrier():
         if world > 1:
             dist.barrier()
+
+    if args.only_c5:
+        line = bench_config5(dev, rank, world, args, barrier)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return 0
 
     global N_CHUNKS, BLOCKS
     N_CHUNKS = 2 * args.layers

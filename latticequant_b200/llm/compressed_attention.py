@@ -25,7 +25,7 @@ over the dequantised K/V that update() returns.
 from __future__ import annotations
 
 import math
-from typing import List, Optional
+from typing import List, Optional, Tuple
 
 import torch
 
@@ -80,13 +80,20 @@ class CompressedAttentionKVCache(CompressedKVCache):
     """
 
     def __init__(self, bits_per_dim: int = 4, tail_tokens: int = 64,
-                 tile_blocks: Optional[int] = codec.DEFAULT_TILE_BLOCKS, table_mode: str = "device"):
+                 tile_blocks: Optional[int] = codec.DEFAULT_TILE_BLOCKS, table_mode: str = "device",
+                 head_range: Optional[Tuple[int, int]] = None, group=None):
         super().__init__(bits_per_dim=bits_per_dim, eval_only_no_entropy=False, tile_blocks=tile_blocks,
                          table_mode=table_mode)
         if tail_tokens < 2 or tail_tokens % 2:
             raise ValueError("tail_tokens must be an even number >= 2")
         self.tail_tokens = int(tail_tokens)
         self._state: List[_LayerState] = []
+        # KV-head sharding: keep only KV heads [h0, h1) of every layer; the
+        # attention function attends with their query heads and all-gathers
+        # the heads' outputs over `group` (torch.distributed; None = default)
+        self.head_range = None if head_range is None else (int(head_range[0]), int(head_range[1]))
+        self.group = group
+        self.n_kv_heads_total = None
 
     # ---- storage -----------------------------------------------------------
     def _layer(self, i: int) -> _LayerState:
@@ -120,6 +127,11 @@ class CompressedAttentionKVCache(CompressedKVCache):
     def update(self, key_states, value_states, layer_idx, cache_kwargs=None):
         if self._model_dtype is None:
             self._model_dtype = key_states.dtype
+        if self.head_range is not None:
+            self.n_kv_heads_total = key_states.shape[1]
+            h0, h1 = self.head_range
+            key_states = key_states[:, h0:h1].contiguous()
+            value_states = value_states[:, h0:h1].contiguous()
         st = self._layer(layer_idx)
         B, H, S, D = key_states.shape
         if D % 8 != 0 or D not in (64, 128):
@@ -295,8 +307,22 @@ def lq_compressed_attention(module, query, key, value, attention_mask, scaling=N
     """transformers attention function.  A decode step (one query position) of a
     module bound to a CompressedAttentionKVCache reads the compressed cache;
     every other call runs SDPA over the K/V it is given (what update()
-    returned: the dequantised tokens)."""
+    returned: the dequantised tokens).  With a KV-head-sharded cache the
+    module's K/V are this rank's heads: it attends with their query heads and
+    all-gathers every rank's heads (sharding.gather_heads)."""
     cache = getattr(module, "_lq_cache", None)
+    if cache is not None and cache.head_range is not None:
+        h0, h1 = cache.head_range
+        g = query.shape[1] // cache.n_kv_heads_total
+        o = _attend(module, cache, query[:, h0 * g:h1 * g], key, value, attention_mask, scaling)
+        from ..sharding import gather_heads
+
+        return gather_heads(o, cache.group), None
+    return _attend(module, cache, query, key, value, attention_mask, scaling), None
+
+
+def _attend(module, cache, query, key, value, attention_mask, scaling):
+    """(B, Q, Hq, D) attention output of one module call (see lq_compressed_attention)."""
     st = None
     if cache is not None and query.shape[2] == 1 and module.layer_idx < len(cache._state):
         st = cache._state[module.layer_idx]
@@ -305,17 +331,14 @@ def lq_compressed_attention(module, query, key, value, attention_mask, scaling=N
     if st is not None:
         masked = attention_mask is not None and bool((attention_mask < 0).any())
         if not masked:
-            o = cache.decode_attention(module.layer_idx, query, scaling)
-            return o.transpose(1, 2).contiguous(), None
+            o = cache.decode_attention(module.layer_idx, query.contiguous(), scaling)
+            return o.transpose(1, 2).contiguous()
         key, value = cache._materialise(st)  # padding masks: attend over the dequantised cache
-    groups = query.shape[1] // key.shape[1]
-    if groups > 1:
-        key = key.repeat_interleave(groups, 1)
-        value = value.repeat_interleave(groups, 1)
+    # grouped query heads read their KV head in place (no repeat_kv copies)
     o = torch.nn.functional.scaled_dot_product_attention(
         query, key, value, attn_mask=attention_mask, is_causal=attention_mask is None and query.shape[2] > 1,
-        scale=scaling)
-    return o.transpose(1, 2).contiguous(), None
+        scale=scaling, enable_gqa=query.shape[1] != key.shape[1])
+    return o.transpose(1, 2).contiguous()
 
 
 def register_attention():

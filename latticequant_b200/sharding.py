@@ -35,6 +35,29 @@ def sequence_slice(seq_len: int, world: int, rank: int, align: int = 1) -> Tuple
     return min(lo_u * align, seq_len), min(hi_u * align, seq_len)
 
 
+def head_slice(n_kv_heads: int, world: int, rank: int) -> Tuple[int, int]:
+    """KV heads [h0, h1) of this rank when a cache is sharded by KV head (equal
+    slices: the KV head count must be a multiple of the world size)."""
+    if world <= 0 or not 0 <= rank < world or n_kv_heads % world:
+        raise ValueError(f"{n_kv_heads} KV heads cannot be split evenly over {world} ranks")
+    per = n_kv_heads // world
+    return rank * per, (rank + 1) * per
+
+
+def gather_heads(o_local: torch.Tensor, group: Optional[dist.ProcessGroup] = None) -> torch.Tensor:
+    """(B, Q, H_local, D) attention outputs of every rank's head slice ->
+    (B, Q, world * H_local, D), rank r's heads at [r * H_local, (r+1) * H_local)."""
+    world = dist.get_world_size(group)
+    o = o_local.contiguous()
+    buf = torch.empty((world,) + tuple(o.shape), dtype=o.dtype, device=o.device)
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(buf, o, group=group)
+    else:
+        dist.all_gather(list(buf.unbind(0)), o, group=group)
+    B, Q, H, D = o.shape
+    return buf.permute(1, 2, 0, 3, 4).reshape(B, Q, world * H, D)
+
+
 def gather_partials(o_local: torch.Tensor, lse_local: torch.Tensor,
                     group: Optional[dist.ProcessGroup] = None) -> Tuple[torch.Tensor, torch.Tensor]:
     """All-gather the per-rank attention partials: (world, *o.shape), (world, *lse.shape)."""

@@ -86,3 +86,58 @@ def test_sequence_sharded_merge_gloo_world2():
             p.join(120)
         assert all(p.exitcode == 0 for p in procs)
         assert len(result) == 2 and max(result.values()) < 1e-12
+
+
+class _Stub:
+    """An attention module bound to a head-sharded cache with no compressed
+    state yet, so lq_compressed_attention takes its SDPA path."""
+
+    def __init__(self, head_range, n_kv):
+        self.layer_idx = 0
+        self._lq_cache = type("C", (), {})()
+        self._lq_cache.head_range = head_range
+        self._lq_cache.n_kv_heads_total = n_kv
+        self._lq_cache.group = None
+        self._lq_cache._state = []
+
+
+def _head_worker(rank, world, port, result):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from latticequant_b200.llm.compressed_attention import lq_compressed_attention
+
+        g = torch.Generator().manual_seed(9)
+        B, Hkv, G, Q, S, D = 2, 4, 3, 5, 5, 16
+        q = torch.randn(B, Hkv * G, Q, D, generator=g, dtype=torch.float64)
+        k = torch.randn(B, Hkv, S, D, generator=g, dtype=torch.float64)
+        v = torch.randn(B, Hkv, S, D, generator=g, dtype=torch.float64)
+        h0, h1 = sharding.head_slice(Hkv, world, rank)
+        # what update() hands the module on this rank: its KV heads only
+        o, _ = lq_compressed_attention(_Stub((h0, h1), Hkv), q, k[:, h0:h1], v[:, h0:h1], None, scaling=0.25)
+        ref = torch.nn.functional.scaled_dot_product_attention(
+            q, k.repeat_interleave(G, 1), v.repeat_interleave(G, 1), is_causal=True, scale=0.25).transpose(1, 2)
+        result[rank] = float((o - ref).abs().max()) if o.shape == ref.shape else float("inf")
+    finally:
+        dist.destroy_process_group()
+
+
+def test_head_slices_cover():
+    assert [sharding.head_slice(8, 4, r) for r in range(4)] == [(0, 2), (2, 4), (4, 6), (6, 8)]
+    with pytest.raises(ValueError):
+        sharding.head_slice(8, 3, 0)
+
+
+def test_kv_head_sharded_attention_gloo_world2():
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as m:
+        result = m.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_head_worker, args=(r, 2, port, result)) for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(120)
+        assert all(p.exitcode == 0 for p in procs)
+        assert len(result) == 2 and max(result.values()) < 1e-12
