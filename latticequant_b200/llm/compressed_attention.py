@@ -118,7 +118,9 @@ class CompressedAttentionKVCache(CompressedKVCache):
     def _quantise_only(self, x: torch.Tensor) -> torch.Tensor:
         """update()'s dequantised output for x (q * fp32 scale in x's dtype), no coding."""
         b, h, s, d = x.shape
-        geom = codec.Geometry(1, b * h, s * d // 8, codec.round_tile(None, b * h * s * d // 8))
+        # 32-block tiles: a tile is one warp's work, and a decode step's tokens
+        # are few blocks (the values do not depend on the tiling)
+        geom = codec.Geometry(1, b * h, s * d // 8, codec.round_tile(32, b * h * s * d // 8))
         cd = codec.Codec(geom, x.device, keep_deq=True, deq_dtype=x.dtype)
         cd.scales(x.contiguous(), self.bits)
         cd.quantize(x.contiguous())

@@ -62,7 +62,9 @@ def compress_compact(tensor: torch.Tensor, bits_per_dim: int = 4):
     if D % 8:
         raise ValueError("head_dim must be a multiple of 8")
     n_heads, bph = B * H, S * D // 8
-    geom = codec.Geometry(1, n_heads, bph, codec.round_tile(None, n_heads * bph))
+    # tiles of the codec's default size: a tile is one warp's work (no
+    # bitstream is made here, so the tiling does not change any output)
+    geom = codec.Geometry(1, n_heads, bph, codec.round_tile(codec.DEFAULT_TILE_BLOCKS, n_heads * bph))
     cd = codec.Codec(geom, x.device, keep_deq=True, deq_dtype=x.dtype)
     cd.scales(x, bits_per_dim)
     q = torch.empty(n_heads * bph, 8, dtype=torch.float32, device=x.device)
