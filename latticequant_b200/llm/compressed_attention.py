@@ -94,6 +94,7 @@ class CompressedAttentionKVCache(CompressedKVCache):
         self.head_range = None if head_range is None else (int(head_range[0]), int(head_range[1]))
         self.group = group
         self.n_kv_heads_total = None
+        self._qcodecs = {}  # decode-step quantisers, one per token shape (buffers reused every step)
 
     # ---- storage -----------------------------------------------------------
     def _layer(self, i: int) -> _LayerState:
@@ -118,10 +119,13 @@ class CompressedAttentionKVCache(CompressedKVCache):
     def _quantise_only(self, x: torch.Tensor) -> torch.Tensor:
         """update()'s dequantised output for x (q * fp32 scale in x's dtype), no coding."""
         b, h, s, d = x.shape
-        # 32-block tiles: a tile is one warp's work, and a decode step's tokens
-        # are few blocks (the values do not depend on the tiling)
-        geom = codec.Geometry(1, b * h, s * d // 8, codec.round_tile(32, b * h * s * d // 8))
-        cd = codec.Codec(geom, x.device, keep_deq=True, deq_dtype=x.dtype)
+        key = (b, h, s, d, x.dtype, x.device)
+        cd = self._qcodecs.get(key)
+        if cd is None:
+            # 32-block tiles: a tile is one warp's work, and a decode step's
+            # tokens are few blocks (the values do not depend on the tiling)
+            geom = codec.Geometry(1, b * h, s * d // 8, codec.round_tile(32, b * h * s * d // 8))
+            cd = self._qcodecs[key] = codec.Codec(geom, x.device, keep_deq=True, deq_dtype=x.dtype)
         cd.scales(x.contiguous(), self.bits)
         cd.quantize(x.contiguous())
         return cd.deq.view(x.shape).clone()
@@ -171,8 +175,10 @@ class CompressedAttentionKVCache(CompressedKVCache):
             st.tail_raw_v = torch.empty_like(st.tail_raw_k)
             st.tail_deq_k = torch.empty_like(st.tail_raw_k)
             st.tail_deq_v = torch.empty_like(st.tail_raw_k)
-        kd = self._quantise_only(k)
-        vd = self._quantise_only(v)
+        # K and V of the token in one call: each (batch, head) row has its own
+        # scale, so stacking them along the heads changes no value
+        kvd = self._quantise_only(torch.cat([k, v], 1))
+        kd, vd = kvd[:, :H], kvd[:, H:]
         i = st.n_tail
         st.tail_raw_k[:, :, i] = k[:, :, 0]
         st.tail_raw_v[:, :, i] = v[:, :, 0]
