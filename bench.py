@@ -346,6 +346,88 @@ def c4_tensor(dev, seed, heads, student):
     return z.to(torch.bfloat16)
 
 
+def bench_attention_compact(dev, rank, world, steps, warmup, barrier):
+    """Config 3 with K/V in the compact fixed-rate layout at 4 bits (the
+    reference's llm/fused_triton_merge.py format: 4-byte codes + fp16
+    fallback rows) and lq_attn_decode_compact, sequence-sharded at N > 1 like
+    the rANS step.  Kernel-only timing through the C ABI with preallocated
+    buffers; algorithmic bytes = codes + fallback rows + mask words + ranks +
+    scales + q + o."""
+    import ctypes
+
+    import torch
+    import torch.distributed as dist
+
+    from latticequant_b200 import _lib
+    from latticequant_b200 import attention as A
+    from latticequant_b200 import sharding as SH
+    from latticequant_b200.llm.fused_triton_merge import compress_compact
+
+    lo, hi = SH.sequence_slice(A_S, world, rank, 64)
+    S = hi - lo
+    k = attention_kv(dev, 4000 + 2 * rank, S)
+    kc, _ = compress_compact(k, 4)
+    del k
+    v = attention_kv(dev, 4001 + 2 * rank, S)
+    vc, _ = compress_compact(v, 4)
+    del v
+    q = attention_query(dev)
+    rows = A_B * A_HKV * A_G
+    kv, vv = A.compact_view(kc), A.compact_view(vc)
+    ws = torch.empty(int(_lib.lib().lq_attn_compact_workspace(A_B * A_HKV, S, A_G, A_D)), dtype=torch.uint8,
+                     device=dev)
+    o = torch.empty(rows, A_D, dtype=torch.float32 if world > 1 else torch.bfloat16, device=dev)
+    lse = torch.empty(rows, dtype=torch.float32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    P = _lib.ptr
+    st = torch.cuda.current_stream(dev)
+
+    def step():
+        rc = _lib.lib().lq_attn_decode_compact(ctypes.byref(kv), ctypes.byref(vv), P(q), _lib.LQ_BF16, A_B, A_HKV, S,
+                                               A_G, A_D, 1 / A_D ** 0.5, P(o), _lib.dtype_code(o.dtype), P(lse),
+                                               P(ws), ws.numel(), P(err), _lib.stream_handle(dev))
+        if rc != 0:
+            raise RuntimeError(f"lq_attn_decode_compact returned {rc}")
+
+    for _ in range(max(warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    if int(err.item()):
+        raise RuntimeError(f"compact attention error flags {int(err.item()):#x}")
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(steps):
+        step()
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    words, rank_t = A.compact_index(kc)
+    words_v, rank_v = A.compact_index(vc)
+    nbytes = (kc.packed.numel() + vc.packed.numel() + 2 * (kc.fallback.numel() + vc.fallback.numel())
+              + 4 * (words.numel() + rank_t.numel() + words_v.numel() + rank_v.numel())
+              + 4 * (kc.scales.numel() + vc.scales.numel()) + q.numel() * 2 + rows * A_D * o.element_size())
+    vals = torch.tensor([ms, float(nbytes), kc.oor_rate + vc.oor_rate], dtype=torch.float64, device=dev)
+    if world > 1:
+        mx, sm = vals[:1].clone(), vals[1:].clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        vals = torch.cat([mx, sm])
+    ms, tot_bytes, oor2 = vals.tolist()
+    if rank != 0:
+        return None
+    peak, peak_kind = measured_peaks()
+    gbps = tot_bytes / (ms * 1e-3) / 1e9
+    return {"metric": A_METRIC, "value": gbps, "unit": "GB/s", "ms_per_step": ms,
+            "layout": "compact fixed-rate, 4 bits: 4-byte codes + fp16 fallback rows "
+                      "(llm/fused_triton_merge.py format)",
+            "fallback_share": oor2 / (2 * world), "bytes_per_step_GB": tot_bytes / 1e9,
+            "roofline": {"bound": "hbm", "kernel": "attn_compact_kernel + attn_combine_kernel",
+                         "achieved": gbps / world, "peak": peak, "unit": "GB/s per GPU",
+                         "frac": gbps / world / peak, "peak_kind": peak_kind},
+            "gpu_launches": steps * 2}
+
+
 def bench_config4(dev, rank, world, steps, barrier):
     """Config 4 on `world` ranks: (layer, KV head) units round-robin, encode of
     every owned unit, then decode-attention steps over every owned layer."""
@@ -779,6 +861,10 @@ def main():
         cd = None
         torch.cuda.empty_cache()
         attn = bench_attention(dev, rank, world, args.steps, args.warmup, barrier)
+        torch.cuda.empty_cache()
+        attn_c = bench_attention_compact(dev, rank, world, args.steps, args.warmup, barrier)
+        if rank == 0:
+            attn["compact_layout"] = attn_c
     c4 = None
     if not args.no_c4:
         torch.cuda.empty_cache()

@@ -248,6 +248,41 @@ int lq_attn_decode(const lq_chunk_view *k, const lq_chunk_view *v, const void *q
                    void *out, int out_dtype, float *lse, const uint32_t *tok_mask, void *workspace,
                    size_t workspace_bytes, uint32_t *err, void *stream);
 
+/* ------------------------------------------------------------------------
+ * Decode attention over the compact fixed-rate layout.  Replaces the
+ * reference's merge of the compact chunk into an fp16 buffer
+ * (llm/fused_triton_merge.py:33-177, fused_decompress_chunk) followed by
+ * SDPA with repeat_kv: the kernel reads each block from the packed codes or
+ * the fp16 fallback rows and attends in registers.
+ *   packed      [n_repr][bits] bytes, the representable blocks in block
+ *               order, big-endian [coset | u0..u6 (bits) | u7 >> 1 (bits-1)]
+ *               (core/compact_storage.py:87-222); 4-byte aligned for bits 4
+ *   fallback    [n_fallback][8] fp16, the other blocks' values (scaled),
+ *               16-byte aligned
+ *   mask_words  [ceil(n_heads*bph/32)] u32: bit i of word w set when block
+ *               32w+i is representable
+ *   word_rank   [same] int32: representable blocks before word w
+ *   scales      [n_heads] fp32 head scales of the representable blocks
+ * Blocks are (B*Hkv, seq*head_dim/8) in head-major order; seq*head_dim/8
+ * must be a multiple of 32.  Results as lq_attn_decode (o, optional lse). */
+typedef struct lq_compact_view {
+    const uint8_t *packed;
+    int64_t n_repr;
+    const uint16_t *fallback;
+    int64_t n_fallback;
+    const uint32_t *mask_words;
+    const int32_t *word_rank;
+    const float *scales;
+    int64_t n_heads, bph;
+    int bits;
+} lq_compact_view;
+
+size_t lq_attn_compact_workspace(int64_t n_heads, int64_t seq_len, int group, int head_dim);
+int lq_attn_decode_compact(const lq_compact_view *k, const lq_compact_view *v, const void *q, int q_dtype,
+                           int64_t batch, int64_t n_kv_heads, int64_t seq_len, int group, int head_dim,
+                           float sm_scale, void *out, int out_dtype, float *lse, void *workspace,
+                           size_t workspace_bytes, uint32_t *err, void *stream);
+
 /* Merge attention parts over disjoint key sets (the all-gathered sequence
  * shards, or several chunks of one layer): o = sum_i o_i exp(lse_i - lse),
  * lse = ln sum_i exp(lse_i).

@@ -53,6 +53,16 @@ class ChunkView(ctypes.Structure):
                 ("n_heads", ctypes.c_int64), ("bph", ctypes.c_int64), ("tile_blocks", ctypes.c_int64)]
 
 
+class CompactView(ctypes.Structure):
+    """struct lq_compact_view: a compact-layout chunk (packed codes, fp16
+    fallback rows, mask words with per-word ranks, head scales)."""
+
+    _fields_ = [("packed", ctypes.c_void_p), ("n_repr", ctypes.c_int64),
+                ("fallback", ctypes.c_void_p), ("n_fallback", ctypes.c_int64),
+                ("mask_words", ctypes.c_void_p), ("word_rank", ctypes.c_void_p), ("scales", ctypes.c_void_p),
+                ("n_heads", ctypes.c_int64), ("bph", ctypes.c_int64), ("bits", ctypes.c_int)]
+
+
 def _declare(lib):
     vp, i64, i32, f32, sz = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_size_t
     sig = {
@@ -78,6 +88,9 @@ def _declare(lib):
         "lq_attn_decode": ([ctypes.POINTER(ChunkView), ctypes.POINTER(ChunkView), vp, i32, i64, i64, i64, i32, i32,
                             i32, f32, vp, i32, vp, vp, vp, sz, vp, vp], i32),
         "lq_attn_merge": ([vp, vp, i64, i64, i32, vp, i32, vp, vp], i32),
+        "lq_attn_compact_workspace": ([i64, i64, i32, i32], sz),
+        "lq_attn_decode_compact": ([ctypes.POINTER(CompactView), ctypes.POINTER(CompactView), vp, i32, i64, i64, i64,
+                                    i32, i32, f32, vp, i32, vp, vp, sz, vp, vp], i32),
         "lq_fwht": ([vp, i64, i32, vp, vp, vp, vp], i32),
         "lq_compact_merge": ([vp, i64, i32, vp, vp, vp, vp, i64, vp, i64, i64, vp, vp, vp], i32),
         "lq_e8_quantize_outliers": ([vp, i32, i64, i64, i64, vp, i64, vp, vp, vp, vp, vp, i32, vp, i32, i32, vp, vp,

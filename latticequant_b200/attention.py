@@ -195,6 +195,74 @@ def decode_attention(q: torch.Tensor, k_chunk: LaneChunk, v_chunk: LaneChunk, sm
     return (o, lse) if return_lse else o
 
 
+def compact_index(chunk) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(mask_words, word_rank) of a compact chunk (llm.fused_triton_merge.
+    CompressedChunk): bit i of word w marks block 32w+i representable; the
+    rank is the representable blocks before word w.  Cached on the chunk."""
+    cached = getattr(chunk, "_lq_index", None)
+    if cached is not None:
+        return cached
+    m = chunk.repr_mask.reshape(-1)
+    n = m.numel()
+    nw = (n + 31) // 32
+    bits = torch.zeros(nw * 32, dtype=torch.int64, device=m.device)
+    bits[:n] = m.to(torch.int64)
+    bits = bits.view(nw, 32)
+    words = (bits << torch.arange(32, device=m.device, dtype=torch.int64)).sum(1)
+    words = torch.where(words >= 2 ** 31, words - 2 ** 32, words).to(torch.int32).contiguous()
+    cnt = bits.sum(1)
+    rank = (torch.cumsum(cnt, 0) - cnt).to(torch.int32).contiguous()
+    chunk._lq_index = (words, rank)
+    return chunk._lq_index
+
+
+def compact_view(chunk) -> "_lib.CompactView":
+    words, rank = compact_index(chunk)
+    B, H, S, D = chunk.orig_shape
+    packed = chunk.packed.contiguous()
+    fb = chunk.fallback.contiguous()
+    return _lib.CompactView(packed.data_ptr() if packed.numel() else None, packed.shape[0],
+                            fb.data_ptr() if fb.numel() else None, fb.shape[0], words.data_ptr(), rank.data_ptr(),
+                            chunk.scales.data_ptr(), B * H, S * D // 8, int(chunk.bits_per_dim))
+
+
+def decode_attention_compact(q: torch.Tensor, k_chunk, v_chunk, sm_scale: Optional[float] = None,
+                             out_dtype: Optional[torch.dtype] = None, return_lse: bool = False,
+                             out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None):
+    """decode_attention over compact-layout chunks (llm.fused_triton_merge.
+    CompressedChunk of a (B, Hkv, S, D) tensor each): the reference merges
+    them into fp16 K/V for SDPA (llm/fused_triton_merge.py:137-177); here one
+    kernel reads the codes and fallback rows and attends.  Same arguments and
+    results as decode_attention."""
+    _lib.require_cuda(q)
+    kshape = tuple(k_chunk.orig_shape)
+    if tuple(v_chunk.orig_shape) != kshape:
+        raise ValueError("K and V chunks differ in shape")
+    q3 = _q3(q, kshape).contiguous()
+    B, Hkv, S, D = kshape
+    G = q3.shape[1] // Hkv
+    dev = q.device
+    need = int(lib().lq_attn_compact_workspace(B * Hkv, S, G, D))
+    if need == 0:
+        raise ValueError(f"compact attention does not take shape {kshape} with group {G} "
+                         "(head_dim 64/128, seq*head_dim/8 a multiple of 32, group 1..8)")
+    ws = torch.empty(need, dtype=torch.uint8, device=dev)
+    if out is None:
+        out = torch.empty(q3.shape, dtype=out_dtype or q.dtype, device=dev)
+    if return_lse and lse is None:
+        lse = torch.empty(q3.shape[:2], dtype=torch.float32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    kv, vv = compact_view(k_chunk), compact_view(v_chunk)
+    scale = (1.0 / math.sqrt(D)) if sm_scale is None else float(sm_scale)
+    check(lib().lq_attn_decode_compact(ctypes.byref(kv), ctypes.byref(vv), ptr(q3), _lib.dtype_code(q3.dtype), B,
+                                       Hkv, S, G, D, scale, ptr(out), _lib.dtype_code(out.dtype),
+                                       ptr(lse) if return_lse else None, ptr(ws), ws.numel(), ptr(err),
+                                       stream_handle(dev)), "lq_attn_decode_compact")
+    raise_flags(int(err.item()) & 0xFFFFFFFF, "decode_attention_compact")
+    o = out.view(tuple(q.shape[:-1]) + (D,)) if q.dim() == 4 else out
+    return (o, lse) if return_lse else o
+
+
 def merge_attention(o_parts: Sequence[torch.Tensor] | torch.Tensor, lse_parts: Sequence[torch.Tensor] | torch.Tensor,
                     out_dtype: Optional[torch.dtype] = None, out: Optional[torch.Tensor] = None,
                     lse: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:

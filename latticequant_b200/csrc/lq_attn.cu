@@ -346,6 +346,344 @@ __global__ void __launch_bounds__(attn_threads<G, BPT>(), 1) attn_redo_kernel(At
     }
 }
 
+// ---------------------------------------------------------------- compact layout
+// Decode attention straight from the compact fixed-rate layout
+// (core/compact_storage.py:87-222; the reference merges it into an fp16
+// buffer for SDPA, llm/fused_triton_merge.py:33-177).  A block is either
+// representable -- `bits` bytes big-endian [coset | u0..u6 | u7 >> 1] -- or
+// an fp16 fallback row (already scaled).  Its place in either array follows
+// from a bit per block and the count of representable blocks before each
+// 32-block word, so a warp step covering 32 consecutive blocks (2 tokens of
+// head_dim 128, 4 of 64) finds every lane's block with one popcount.
+// Nothing is serial per block, so the kernel streams HBM.
+struct CompactDev {
+    const uint8_t *packed;
+    const uint4 *fallback;
+    const uint32_t *mask_words;
+    const int32_t *word_rank;
+    const float *scales;
+    uint32_t n_repr, n_fallback;
+    int bits;
+};
+
+struct CompactArgs {
+    CompactDev k, v;
+    const void *q;
+    uint32_t n_kv_heads, seq, bph;
+    uint32_t nct, tok_per_cta, tok_per_warp;
+    float qk_log2;
+    float *part;
+    uint32_t *err;
+};
+
+constexpr int kCompactThreads = 512;
+
+// One lane's block of a warp step: its raw bytes (the code of a
+// representable block in .x (.y), or the fp16 fallback row) and which.
+struct CompactBlock {
+    uint4 raw;
+    bool repr, ok;
+};
+
+// Fetch the block at bit `bit` of mask word w (r0 representable blocks
+// before it, word index wi).  Out-of-range ranks raise the BITSTREAM flag
+// and give a zero block.
+__device__ __forceinline__ CompactBlock compact_fetch(const CompactDev &c, uint32_t w, int r0, uint32_t wi,
+                                                      uint32_t bit, bool ok, uint32_t *err) {
+    CompactBlock k;
+    k.raw = make_uint4(0u, 0u, 0u, 0u);
+    k.repr = false;
+    k.ok = false;
+    if (!ok) return k;
+    const uint32_t below = w & ((1u << bit) - 1u);
+    if ((w >> bit) & 1u) {
+        const uint32_t p = (uint32_t)r0 + (uint32_t)__popc(below);
+        if (p >= c.n_repr) {
+            raise_flag(err, LQ_EF_BITSTREAM);
+            return k;
+        }
+        if (c.bits == 4) {
+            k.raw.x = __ldg(reinterpret_cast<const uint32_t *>(c.packed) + p);
+        } else {
+            uint64_t acc = 0;
+            for (int i = 0; i < c.bits; ++i) acc = (acc << 8) | __ldg(c.packed + (size_t)p * c.bits + i);
+            k.raw.x = (uint32_t)acc;
+            k.raw.y = (uint32_t)(acc >> 32);
+        }
+        k.repr = true;
+    } else {
+        const uint32_t f = wi * 32u - (uint32_t)r0 + (bit - (uint32_t)__popc(below));
+        if (f >= c.n_fallback) {
+            raise_flag(err, LQ_EF_BITSTREAM);
+            return k;
+        }
+        k.raw = __ldg(c.fallback + f);
+    }
+    k.ok = true;
+    return k;
+}
+
+// Values of a fetched block: for a representable block the scale-free E8
+// point (u - R + coset/2, coordinate 7 with the parity bit of the other
+// seven) and sc = the head scale; for a fallback row its fp16 values and
+// sc = 1; zeros for none.
+__device__ __forceinline__ void compact_values(const CompactBlock &k, int bits, float head_scale, float x[8],
+                                               float &sc) {
+    sc = 1.f;
+    if (!k.ok) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] = 0.f;
+        return;
+    }
+    if (k.repr) {
+        const int R = 1 << (bits - 1);
+        uint32_t u[7], c7u, coset, par;
+        if (bits == 4) {
+            const uint32_t v = __byte_perm(k.raw.x, 0u, 0x0123u);  // big-endian code
+            coset = v >> 31;
+#pragma unroll
+            for (int i = 0; i < 7; ++i) u[i] = (v >> (27 - 4 * i)) & 15u;
+            c7u = v & 7u;
+            par = __popc(v & 0x08888888u) & 1u;  // low bits of u0..u6
+        } else {
+            uint64_t acc = ((uint64_t)k.raw.y << 32) | k.raw.x;
+            c7u = (uint32_t)(acc & ((1ull << (bits - 1)) - 1));
+            acc >>= (bits - 1);
+            par = 0;
+#pragma unroll
+            for (int i = 6; i >= 0; --i) {
+                u[i] = (uint32_t)(acc & ((1ull << bits) - 1));
+                par ^= u[i];
+                acc >>= bits;
+            }
+            par &= 1u;
+            coset = (uint32_t)(acc & 1u);
+        }
+        // u - R + coset/2 exactly: 2u + coset in the mantissa of 2^22 (spacing
+        // 1/2) reads 2^22 + u + coset/2; 2^22 + R is exact, so is the difference
+        const uint32_t base = 0x4A800000u | coset;
+        const float bias = 4194304.0f + (float)R;
+#pragma unroll
+        for (int i = 0; i < 7; ++i) x[i] = __int_as_float((u[i] << 1) | base) - bias;
+        // coordinate 7 = 2*c7u + parity(sum of the signed others) - R; R is even, so that parity is par
+        x[7] = __int_as_float(((2u * c7u + par) << 1) | base) - bias;
+        sc = head_scale;
+    } else {
+        const uint32_t hw[4] = {k.raw.x, k.raw.y, k.raw.z, k.raw.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f2 = __half22float2(*reinterpret_cast<const __half2 *>(&hw[i]));
+            x[2 * i] = f2.x;
+            x[2 * i + 1] = f2.y;
+        }
+    }
+}
+
+template <int G, int BPT, int QDT>
+__global__ void __launch_bounds__(kCompactThreads, 1) attn_compact_kernel(CompactArgs a) {
+    static_assert(BPT == 8 || BPT == 16, "head_dim 64 or 128");
+    constexpr int D = 8 * BPT, GP = padded_g<G>(), TPS = 32 / BPT;  // tokens per warp step
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const uint32_t lane = threadIdx.x & 31, dc = lane % BPT, tl = lane / BPT;
+    const uint32_t head = blockIdx.y;
+    const uint32_t t0 = blockIdx.x * a.tok_per_cta + (uint32_t)warp * a.tok_per_warp;
+    const uint32_t t1 = min(t0 + a.tok_per_warp, a.seq);
+    float *sc = reinterpret_cast<float *>(smem) + (size_t)warp * a.tok_per_warp * GP;
+    const uint32_t b = head / a.n_kv_heads, kvh = head % a.n_kv_heads;
+    const float sk = a.k.scales[head], sv = a.v.scales[head];
+
+    constexpr int GH = G / 2;
+    unsigned long long q2[GH > 0 ? GH : 1][8];
+    float qlast[8];
+#pragma unroll
+    for (int g = 0; g < G; g += 2) {
+        const int64_t row = (int64_t)b * a.n_kv_heads * G + (int64_t)kvh * G + g;
+        float x0[8], x1[8];
+        load_block8<QDT>(a.q, row * BPT + dc, x0);
+        if (g + 1 < G) {
+            load_block8<QDT>(a.q, (row + 1) * BPT + dc, x1);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) q2[g / 2][i] = f2_pack(x0[i], x1[i]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) qlast[i] = x0[i];
+        }
+    }
+
+    // A warp step covers 32 consecutive blocks (TPS tokens) = one mask
+    // word; lane i holds the word and rank of step i, read at the start.
+    const uint32_t nsteps = t1 > t0 ? (t1 - t0 + TPS - 1) / TPS : 0u;
+    const uint32_t w0 = (head * a.bph + t0 * BPT) >> 5;
+    auto fetch = [&](const CompactDev &c, uint32_t mw, int mr, uint32_t it) {
+        const uint32_t w = __shfl_sync(0xffffffffu, mw, it);
+        const int r0 = __shfl_sync(0xffffffffu, mr, it);
+        const uint32_t tok = t0 + it * TPS + tl;
+        return compact_fetch(c, w, r0, w0 + it, lane, tok < t1, a.err);
+    };
+    uint32_t kw = 0, vw = 0;
+    int kr = 0, vr = 0;
+    if (lane < nsteps) {
+        kw = __ldg(a.k.mask_words + w0 + lane);
+        kr = __ldg(a.k.word_rank + w0 + lane);
+        vw = __ldg(a.v.mask_words + w0 + lane);
+        vr = __ldg(a.v.word_rank + w0 + lane);
+    }
+
+    // ---- phase K: scores (base 2) of the warp's tokens into shared memory
+    CompactBlock cur = fetch(a.k, kw, kr, 0);
+    for (uint32_t it = 0; it < nsteps; ++it) {
+        const uint32_t tok = t0 + it * TPS + tl;
+        const bool ok = tok < t1;
+        // the next step's block is requested before this one is used
+        CompactBlock nxt = cur;
+        if (it + 1 < nsteps) nxt = fetch(a.k, kw, kr, it + 1);
+        float kx[8], s;
+        compact_values(cur, a.k.bits, sk, kx, s);
+        cur = nxt;
+        float dot[G];
+#pragma unroll
+        for (int g = 0; g + 1 < G; g += 2) {
+            unsigned long long s2 = f2_mul(q2[g / 2][0], f2_pack(kx[0], kx[0]));
+#pragma unroll
+            for (int i = 1; i < 8; ++i) s2 = f2_fma(q2[g / 2][i], f2_pack(kx[i], kx[i]), s2);
+            f2_unpack(s2, dot[g], dot[g + 1]);
+        }
+        if constexpr (G % 2) {
+            float d = __fmul_rn(qlast[0], kx[0]);
+#pragma unroll
+            for (int i = 1; i < 8; ++i) d = __fmaf_rn(qlast[i], kx[i], d);
+            dot[G - 1] = d;
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) dot[g] *= s;
+#pragma unroll
+        for (int off = BPT / 2; off >= 1; off >>= 1) {
+#pragma unroll
+            for (int g = 0; g < G; ++g) dot[g] += __shfl_xor_sync(0xffffffffu, dot[g], off);
+        }
+        if (ok && dc < (uint32_t)G) {
+            float v = dot[0];
+#pragma unroll
+            for (int g = 1; g < G; ++g) v = (dc == (uint32_t)g) ? dot[g] : v;
+            sc[(tok - t0) * GP + dc] = v * a.qk_log2;
+        }
+    }
+    __syncwarp();
+
+    // ---- softmax statistics of the warp's tokens
+    const uint32_t ntok = t1 > t0 ? t1 - t0 : 0u;
+    float m[G], l[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        m[g] = -INFINITY;
+        l[g] = 0.f;
+    }
+    for (uint32_t i = lane; i < ntok; i += 32) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) m[g] = fmaxf(m[g], sc[i * GP + g]);
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) m[g] = fmaxf(m[g], __shfl_xor_sync(0xffffffffu, m[g], off));
+    }
+    for (uint32_t i = lane; i < ntok; i += 32) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float p = exp2f(sc[i * GP + g] - m[g]);
+            sc[i * GP + g] = p;
+            l[g] += p;
+        }
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) l[g] += __shfl_xor_sync(0xffffffffu, l[g], off);
+    }
+    __syncwarp();
+
+    // ---- phase V: p * v per lane over its 8 channels
+    unsigned long long acc2[G][4];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc2[g][i] = 0ull;
+    cur = fetch(a.v, vw, vr, 0);
+    for (uint32_t it = 0; it < nsteps; ++it) {
+        const uint32_t tok = t0 + it * TPS + tl;
+        const bool ok = tok < t1;
+        CompactBlock nxt = cur;
+        if (it + 1 < nsteps) nxt = fetch(a.v, vw, vr, it + 1);
+        float vx[8], s;
+        compact_values(cur, a.v.bits, sv, vx, s);
+        cur = nxt;
+        if (!ok) continue;
+        const float *pp = sc + (tok - t0) * GP;
+        unsigned long long v2[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v2[i] = f2_pack(vx[2 * i], vx[2 * i + 1]);
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float pg = pp[g] * s;
+            const unsigned long long p2 = f2_pack(pg, pg);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc2[g][i] = f2_fma(p2, v2[i], acc2[g][i]);
+        }
+    }
+    float acc[G][8];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) f2_unpack(acc2[g][i], acc[g][2 * i], acc[g][2 * i + 1]);
+    // lanes holding the same channels: the other tokens of a step
+#pragma unroll
+    for (int off = 16; off >= BPT; off >>= 1) {
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[g][i] += __shfl_xor_sync(0xffffffffu, acc[g][i], off);
+    }
+
+    // ---- merge the warps in a fixed order (the score region is done with)
+    __syncthreads();
+    float *mrg = reinterpret_cast<float *>(smem);
+    const int rs = D + 2;
+    if (lane < (uint32_t)BPT) {
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) mrg[(warp * G + g) * rs + 8 * (int)lane + i] = acc[g][i];
+    }
+    if (lane == 0) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            mrg[(warp * G + g) * rs + D] = m[g];
+            mrg[(warp * G + g) * rs + D + 1] = l[g];
+        }
+    }
+    __syncthreads();
+    float *out = a.part + ((size_t)head * a.nct + blockIdx.x) * G * rs;
+    for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
+        const int g = e / D, dd = e % D;
+        float mx = -INFINITY;
+        for (int w = 0; w < nwarps; ++w) mx = fmaxf(mx, mrg[(w * G + g) * rs + D]);
+        float o = 0.f, ls = 0.f;
+        for (int w = 0; w < nwarps; ++w) {
+            const float mw = mrg[(w * G + g) * rs + D];
+            if (mw == -INFINITY) continue;
+            const float f = exp2f(mw - mx);
+            o = fmaf(mrg[(w * G + g) * rs + dd], f, o);
+            ls = fmaf(mrg[(w * G + g) * rs + D + 1], f, ls);
+        }
+        out[g * rs + dd] = o;
+        if (dd == 0) {
+            out[g * rs + D] = mx;
+            out[g * rs + D + 1] = ls;
+        }
+    }
+}
+
 // One block per query row: merge the head's CTA partials into o = O / L and
 // lse = ln(sum exp(s)) (natural log of the unnormalised softmax mass).
 template <int ODT>
@@ -476,6 +814,66 @@ int launch_partial_g(const AttnArgs &a, const AttnPlan &p, uint32_t n_heads, int
                     : launch_partial_q<G, 8>(a, p, n_heads, q_dtype, st);
 }
 
+// ---- compact-layout attention: plan and launch
+struct CompactPlan {
+    uint32_t nct, tok_per_warp, tok_per_cta;
+    size_t smem, part_floats;
+};
+
+int compact_plan(int64_t n_heads, int64_t seq, int G, int D, CompactPlan *p) {
+    if (n_heads <= 0 || seq <= 0 || G < 1 || G > 8 || (D != 64 && D != 128)) return LQ_ERR_INVALID;
+    const int bpt = D / 8, tps = 32 / bpt;
+    if ((seq * bpt) % 32 != 0 || n_heads > 65535 || n_heads * seq * bpt >= ((int64_t)1 << 31)) return LQ_ERR_INVALID;
+    const int nw = kCompactThreads / 32;
+    p->tok_per_warp = 64u;  // a multiple of the tokens per step (2 or 4)
+    (void)tps;
+    p->tok_per_cta = p->tok_per_warp * nw;
+    p->nct = (uint32_t)ceil_div(seq, p->tok_per_cta);
+    const size_t gp = (size_t)((G + 3) & ~3);
+    p->smem = std::max<size_t>((size_t)nw * p->tok_per_warp * gp * 4, (size_t)nw * G * (D + 2) * 4);
+    p->part_floats = (size_t)n_heads * p->nct * G * (D + 2);
+    return LQ_OK;
+}
+
+template <int G, int BPT, int QDT>
+int launch_compact(const CompactArgs &a, const CompactPlan &p, uint32_t n_heads, cudaStream_t st) {
+    auto kern = attn_compact_kernel<G, BPT, QDT>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem) != cudaSuccess)
+        return LQ_ERR_CUDA;
+    kern<<<dim3(p.nct, n_heads), kCompactThreads, p.smem, st>>>(a);
+    return check_launch();
+}
+
+template <int G, int BPT>
+int launch_compact_q(const CompactArgs &a, const CompactPlan &p, uint32_t n_heads, int q_dtype, cudaStream_t st) {
+    switch (q_dtype) {
+        case LQ_F32: return launch_compact<G, BPT, LQ_F32>(a, p, n_heads, st);
+        case LQ_F16: return launch_compact<G, BPT, LQ_F16>(a, p, n_heads, st);
+        case LQ_BF16: return launch_compact<G, BPT, LQ_BF16>(a, p, n_heads, st);
+        default: return LQ_ERR_INVALID;
+    }
+}
+
+template <int G>
+int launch_compact_g(const CompactArgs &a, const CompactPlan &p, uint32_t n_heads, int q_dtype, int D, cudaStream_t st) {
+    return D == 128 ? launch_compact_q<G, 16>(a, p, n_heads, q_dtype, st)
+                    : launch_compact_q<G, 8>(a, p, n_heads, q_dtype, st);
+}
+
+bool compact_ok(const lq_compact_view *c, int64_t n_heads, int64_t bph) {
+    if (!c || !c->mask_words || !c->word_rank || !c->scales || c->n_heads != n_heads || c->bph != bph) return false;
+    if (c->bits < 3 || c->bits > 5 || c->n_repr < 0 || c->n_fallback < 0) return false;
+    if (c->n_repr > 0 && !c->packed) return false;
+    if (c->n_fallback > 0 && (!c->fallback || (reinterpret_cast<uintptr_t>(c->fallback) & 15))) return false;
+    if (c->bits == 4 && c->n_repr > 0 && (reinterpret_cast<uintptr_t>(c->packed) & 3)) return false;
+    return c->n_repr <= 0xffffffffLL && c->n_fallback <= 0xffffffffLL;
+}
+
+CompactDev to_compact(const lq_compact_view *c) {
+    return CompactDev{c->packed, reinterpret_cast<const uint4 *>(c->fallback), c->mask_words, c->word_rank, c->scales,
+                      (uint32_t)c->n_repr, (uint32_t)c->n_fallback, c->bits};
+}
+
 bool view_ok(const lq_chunk_view *c) {
     return c && c->lane_off && c->lane_nbits && c->lane_state && c->coset_words && c->tile_n0 && c->tab_lo &&
            c->tab_nsym && c->tab_freq && c->dec_tab && c->scale_f16 && c->n_words >= 0 && (c->n_words == 0 || c->words);
@@ -551,6 +949,64 @@ extern "C" int lq_attn_decode(const lq_chunk_view *k, const lq_chunk_view *v, co
         case 6: r = launch_partial_g<6>(a, p, nh, q_dtype, head_dim, st); break;
         case 7: r = launch_partial_g<7>(a, p, nh, q_dtype, head_dim, st); break;
         case 8: r = launch_partial_g<8>(a, p, nh, q_dtype, head_dim, st); break;
+        default: return LQ_ERR_INVALID;
+    }
+    if (r != LQ_OK) return r;
+    const unsigned rows = (unsigned)(heads * group);
+    const float *part = a.part;
+    const uint32_t hkv = (uint32_t)n_kv_heads, G = (uint32_t)group, D = (uint32_t)head_dim;
+    if (out_dtype == LQ_F32) attn_combine_kernel<LQ_F32><<<rows, D, 0, st>>>(part, hkv, G, D, p.nct, out, lse);
+    else if (out_dtype == LQ_F16) attn_combine_kernel<LQ_F16><<<rows, D, 0, st>>>(part, hkv, G, D, p.nct, out, lse);
+    else attn_combine_kernel<LQ_BF16><<<rows, D, 0, st>>>(part, hkv, G, D, p.nct, out, lse);
+    return check_launch();
+}
+
+extern "C" size_t lq_attn_compact_workspace(int64_t n_heads, int64_t seq_len, int group, int head_dim) {
+    CompactPlan p;
+    if (compact_plan(n_heads, seq_len, group, head_dim, &p) != LQ_OK) return 0;
+    return (p.part_floats * 4 + 255) & ~(size_t)255;
+}
+
+extern "C" int lq_attn_decode_compact(const lq_compact_view *k, const lq_compact_view *v, const void *q, int q_dtype,
+                                      int64_t batch, int64_t n_kv_heads, int64_t seq_len, int group, int head_dim,
+                                      float sm_scale, void *out, int out_dtype, float *lse, void *workspace,
+                                      size_t workspace_bytes, uint32_t *err, void *stream) {
+    if (!q || !out || !workspace || batch <= 0 || n_kv_heads <= 0 || seq_len <= 0) return LQ_ERR_INVALID;
+    if (head_dim != 64 && head_dim != 128) return LQ_ERR_INVALID;
+    const int64_t heads = batch * n_kv_heads, bph = seq_len * (head_dim / 8);
+    if (!compact_ok(k, heads, bph) || !compact_ok(v, heads, bph)) return LQ_ERR_INVALID;
+    if ((reinterpret_cast<uintptr_t>(q) & 15) || (reinterpret_cast<uintptr_t>(workspace) & 15)) return LQ_ERR_INVALID;
+    if (!(sm_scale > 0.f) || !isfinite(sm_scale)) return LQ_ERR_INVALID;
+    if (out_dtype != LQ_F32 && out_dtype != LQ_F16 && out_dtype != LQ_BF16) return LQ_ERR_INVALID;
+    CompactPlan p;
+    const int rc = compact_plan(heads, seq_len, group, head_dim, &p);
+    if (rc != LQ_OK) return rc;
+    if (workspace_bytes < p.part_floats * 4) return LQ_ERR_CAPACITY;
+    cudaStream_t st = as_stream(stream);
+    CompactArgs a;
+    a.k = to_compact(k);
+    a.v = to_compact(v);
+    a.q = q;
+    a.n_kv_heads = (uint32_t)n_kv_heads;
+    a.seq = (uint32_t)seq_len;
+    a.bph = (uint32_t)bph;
+    a.nct = p.nct;
+    a.tok_per_cta = p.tok_per_cta;
+    a.tok_per_warp = p.tok_per_warp;
+    a.qk_log2 = sm_scale * kLog2e;
+    a.part = static_cast<float *>(workspace);
+    a.err = err;
+    const uint32_t nh = (uint32_t)heads;
+    int r;
+    switch (group) {
+        case 1: r = launch_compact_g<1>(a, p, nh, q_dtype, head_dim, st); break;
+        case 2: r = launch_compact_g<2>(a, p, nh, q_dtype, head_dim, st); break;
+        case 3: r = launch_compact_g<3>(a, p, nh, q_dtype, head_dim, st); break;
+        case 4: r = launch_compact_g<4>(a, p, nh, q_dtype, head_dim, st); break;
+        case 5: r = launch_compact_g<5>(a, p, nh, q_dtype, head_dim, st); break;
+        case 6: r = launch_compact_g<6>(a, p, nh, q_dtype, head_dim, st); break;
+        case 7: r = launch_compact_g<7>(a, p, nh, q_dtype, head_dim, st); break;
+        case 8: r = launch_compact_g<8>(a, p, nh, q_dtype, head_dim, st); break;
         default: return LQ_ERR_INVALID;
     }
     if (r != LQ_OK) return r;

@@ -1,0 +1,101 @@
+"""Decode attention over the compact fixed-rate layout (lq_attn_decode_compact)
+against the oracle: every block's value from the chunk -- the oracle's
+unpack_e8 (core/compact_storage.py:140-222) times the fp32 head scale for a
+representable block, the stored fp16 row for a fallback block -- attended in
+float64 with repeat_kv (oracle.decode_attention_f64).  The reference's own
+path merges the chunk into fp16 K/V first (llm/fused_triton_merge.py:137-177);
+that rounding is the one difference, and the merged-fp16 attention is checked
+against the same bar.
+
+Tolerance: max |o - o_ref| <= 1e-3 * max |o_ref| per query row; lse within
+1e-3 absolute.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+RTOL = 1e-3
+
+
+def _exact_values(chunk):
+    from oracle import lq_oracle as O
+
+    mask = chunk.repr_mask.cpu().numpy().astype(bool)
+    n = mask.size
+    out = np.zeros((n, 8), np.float64)
+    q = O.unpack_e8(chunk.packed.cpu().numpy(), chunk.bits_per_dim)
+    head = np.arange(n) // chunk.blocks_per_head
+    sc = chunk.scales.cpu().numpy().astype(np.float64)
+    out[mask] = q.astype(np.float64) * sc[head[mask]][:, None]
+    out[~mask] = chunk.fallback.cpu().float().numpy()
+    return out.reshape(chunk.orig_shape)
+
+
+def _row_err(o, ref):
+    err = np.abs(o - ref).max(axis=-1)
+    scale = np.abs(ref).max(axis=-1)
+    return float((err / scale).max())
+
+
+def _kv(shape, seed):
+    g = torch.Generator().manual_seed(seed)
+    B, H, S, D = shape
+    return (torch.randn(shape, generator=g) * torch.exp(0.5 * torch.randn(B, H, S, 1, generator=g))).to(torch.bfloat16)
+
+
+CASES = [
+    # B, Hkv, G, S, D, bits, q dtype
+    (2, 2, 4, 256, 128, 4, torch.bfloat16),
+    (1, 3, 2, 128, 64, 4, torch.float16),
+    (2, 1, 1, 64, 128, 3, torch.float32),
+    (1, 2, 8, 96, 128, 5, torch.bfloat16),
+    (1, 4, 7, 1030, 128, 4, torch.bfloat16),   # tokens past the last full warp slab
+]
+
+
+@pytest.mark.parametrize("case", CASES, ids=[f"B{c[0]}H{c[1]}G{c[2]}S{c[3]}D{c[4]}b{c[5]}" for c in CASES])
+def test_compact_attention_matches_merge_then_attention(case):
+    from oracle import lq_oracle as O
+
+    from latticequant_b200 import attention
+    from latticequant_b200.llm.fused_triton_merge import compress_compact, fused_decompress_chunk
+
+    B, Hkv, G, S, D, bits, qdt = case
+    k = _kv((B, Hkv, S, D), 21).cuda()
+    v = _kv((B, Hkv, S, D), 22).cuda()
+    kc, _ = compress_compact(k, bits)
+    vc, _ = compress_compact(v, bits)
+    assert 0 < kc.oor_rate < 1 and 0 < vc.oor_rate < 1  # both paths of the kernel run
+    gq = torch.Generator().manual_seed(23)
+    q = (torch.randn(B, Hkv * G, D, generator=gq) / math.sqrt(D)).to(qdt)
+    sm = 1.0 / math.sqrt(D)
+    o, lse = attention.decode_attention_compact(q.cuda(), kc, vc, out_dtype=torch.float32, return_lse=True)
+    kd, vd = _exact_values(kc), _exact_values(vc)
+    ref = O.decode_attention_f64(q.float().numpy(), kd, vd, sm)
+    o = o.cpu().numpy().reshape(ref.shape)
+    assert _row_err(o, ref) <= RTOL, _row_err(o, ref)
+    # and within the same bar of the reference's merge-then-attend path
+    km = fused_decompress_chunk(kc).float().cpu().numpy()
+    vm = fused_decompress_chunk(vc).float().cpu().numpy()
+    assert _row_err(o, O.decode_attention_f64(q.float().numpy(), km, vm, sm)) <= RTOL
+    qf = q.double().numpy()
+    kf = np.repeat(kd.astype(np.float64), G, axis=1)
+    s = np.einsum("bhd,bhsd->bhs", qf, kf) * sm
+    mx = s.max(-1, keepdims=True)
+    lref = mx[..., 0] + np.log(np.exp(s - mx).sum(-1))
+    assert np.abs(lse.cpu().numpy() - lref).max() < 1e-3
+
+
+def test_compact_attention_rejects_unaligned_heads():
+    from latticequant_b200 import attention
+    from latticequant_b200.llm.fused_triton_merge import compress_compact
+
+    k = _kv((1, 1, 3, 128), 5).cuda()  # 48 blocks per head: not a multiple of 32
+    kc, _ = compress_compact(k, 4)
+    q = torch.randn(1, 1, 128, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError):
+        attention.decode_attention_compact(q, kc, kc)
