@@ -256,7 +256,7 @@ int lq_attn_decode(const lq_chunk_view *k, const lq_chunk_view *v, const void *q
  * the fp16 fallback rows and attends in registers.
  *   packed      [n_repr][bits] bytes, the representable blocks in block
  *               order, big-endian [coset | u0..u6 (bits) | u7 >> 1 (bits-1)]
- *               (core/compact_storage.py:87-222); 4-byte aligned for bits 4
+ *               (core/compact_storage.py:87-222); 16-byte aligned
  *   fallback    [n_fallback][8] fp16, the other blocks' values (scaled),
  *               16-byte aligned
  *   mask_words  [ceil(n_heads*bph/32)] u32: bit i of word w set when block

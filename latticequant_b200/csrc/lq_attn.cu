@@ -362,7 +362,7 @@ struct CompactDev {
     const uint32_t *mask_words;
     const int32_t *word_rank;
     const float *scales;
-    uint32_t n_repr, n_fallback;
+    uint32_t n_repr, n_fallback, n_words;
     int bits;
 };
 
@@ -370,91 +370,132 @@ struct CompactArgs {
     CompactDev k, v;
     const void *q;
     uint32_t n_kv_heads, seq, bph;
-    uint32_t nct, tok_per_cta, tok_per_warp;
+    uint32_t nct, tok_per_cta;
     float qk_log2;
     float *part;
     uint32_t *err;
 };
 
 constexpr int kCompactThreads = 512;
+constexpr int kCompactWarps = kCompactThreads / 32;
+constexpr int kCStageTok = 256;     // tokens per shared-memory stage
+constexpr int kCTokPerCta = 1024;   // tokens per CTA (4 stages)
 
-// One lane's block of a warp step: its raw bytes (the code of a
-// representable block in .x (.y), or the fp16 fallback row) and which.
-struct CompactBlock {
-    uint4 raw;
-    bool repr, ok;
+// Shared-memory stage of one chunk's blocks of kCStageTok tokens: mask words,
+// their ranks, the representable codes (from a 16-byte-aligned start) and the
+// fallback rows, copied in with cp.async.
+template <int BPT>
+struct CStage {
+    static constexpr int kBlocks = kCStageTok * BPT, kWords = kBlocks / 32;
+    static constexpr int kPackedBytes = (kBlocks * 5 + 16 + 15) & ~15;  // bits <= 5, + alignment slack
+    static constexpr int kWordsOff = 0, kRanksOff = kWords * 4, kPackedOff = kWords * 8;
+    static constexpr int kFallbackOff = kPackedOff + kPackedBytes;
+    static constexpr int kBytes = kFallbackOff + kBlocks * 16;
 };
 
-// Fetch the block at bit `bit` of mask word w (r0 representable blocks
-// before it, word index wi).  Out-of-range ranks raise the BITSTREAM flag
-// and give a zero block.
-__device__ __forceinline__ CompactBlock compact_fetch(const CompactDev &c, uint32_t w, int r0, uint32_t wi,
-                                                      uint32_t bit, bool ok, uint32_t *err) {
-    CompactBlock k;
-    k.raw = make_uint4(0u, 0u, 0u, 0u);
-    k.repr = false;
-    k.ok = false;
-    if (!ok) return k;
-    const uint32_t below = w & ((1u << bit) - 1u);
-    if ((w >> bit) & 1u) {
-        const uint32_t p = (uint32_t)r0 + (uint32_t)__popc(below);
-        if (p >= c.n_repr) {
-            raise_flag(err, LQ_EF_BITSTREAM);
-            return k;
-        }
-        if (c.bits == 4) {
-            k.raw.x = __ldg(reinterpret_cast<const uint32_t *>(c.packed) + p);
-        } else {
-            uint64_t acc = 0;
-            for (int i = 0; i < c.bits; ++i) acc = (acc << 8) | __ldg(c.packed + (size_t)p * c.bits + i);
-            k.raw.x = (uint32_t)acc;
-            k.raw.y = (uint32_t)(acc >> 32);
-        }
-        k.repr = true;
-    } else {
-        const uint32_t f = wi * 32u - (uint32_t)r0 + (bit - (uint32_t)__popc(below));
-        if (f >= c.n_fallback) {
-            raise_flag(err, LQ_EF_BITSTREAM);
-            return k;
-        }
-        k.raw = __ldg(c.fallback + f);
-    }
-    k.ok = true;
-    return k;
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// Values of a fetched block: for a representable block the scale-free E8
-// point (u - R + coset/2, coordinate 7 with the parity bit of the other
-// seven) and sc = the head scale; for a fallback row its fp16 values and
-// sc = 1; zeros for none.
-__device__ __forceinline__ void compact_values(const CompactBlock &k, int bits, float head_scale, float x[8],
-                                               float &sc) {
-    sc = 1.f;
-    if (!k.ok) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) x[i] = 0.f;
+// Where a stage's data starts in the chunk's arrays.
+struct CStageSpan {
+    uint32_t w0, nw;       // first mask word, words
+    uint32_t r0, r1;       // representable blocks before the stage / after it
+    uint32_t a0;           // byte of the packed array the staged copy starts at (16-byte aligned)
+    bool bad;              // ranks inconsistent with the arrays: nothing is copied, blocks read as zeros
+};
+
+__device__ __forceinline__ CStageSpan cstage_span(const CompactDev &c, uint32_t b0, uint32_t b1) {
+    CStageSpan s;
+    s.w0 = b0 >> 5;
+    s.nw = (b1 - b0) >> 5;
+    s.r0 = (uint32_t)__ldg(c.word_rank + s.w0);
+    s.r1 = s.w0 + s.nw < c.n_words ? (uint32_t)__ldg(c.word_rank + s.w0 + s.nw) : c.n_repr;
+    s.a0 = (s.r0 * (uint32_t)c.bits) & ~15u;
+    s.bad = !(s.r0 <= s.r1 && s.r1 - s.r0 <= 32u * s.nw && s.r1 <= c.n_repr && b0 >= s.r0 &&
+              b0 + 32u * s.nw - s.r1 <= c.n_fallback);
+    return s;
+}
+
+// All threads: copy one stage into shared memory at `buf` (and commit).
+template <int BPT>
+__device__ __forceinline__ void cstage_issue(const CompactDev &c, const CStageSpan &s, uint32_t b0, uint32_t buf) {
+    using S = CStage<BPT>;
+    if (s.bad) {  // the blocks raise the flag when read
+        cp_async_commit();
         return;
     }
-    if (k.repr) {
-        const int R = 1 << (bits - 1);
+    for (uint32_t i = threadIdx.x; i < s.nw; i += blockDim.x) {
+        cp_async4(buf + S::kWordsOff + 4 * i, c.mask_words + s.w0 + i);
+        cp_async4(buf + S::kRanksOff + 4 * i, c.word_rank + s.w0 + i);
+    }
+    const uint32_t total = c.n_repr * (uint32_t)c.bits, a1 = s.r1 * (uint32_t)c.bits;
+    for (uint32_t off = s.a0 + 16u * threadIdx.x; off < a1; off += 16u * blockDim.x)
+        cp_async16(buf + S::kPackedOff + (off - s.a0), c.packed + off, min(16u, total - off));
+    const uint32_t f0 = b0 - s.r0, f1 = b0 + 32u * s.nw - s.r1;
+    for (uint32_t r = f0 + threadIdx.x; r < f1; r += blockDim.x)
+        cp_async16(buf + S::kFallbackOff + 16u * (r - f0), c.fallback + r, 16u);
+    cp_async_commit();
+}
+
+// The lane's block of a warp step from a stage: 32 consecutive blocks =
+// mask word `wi` of the stage.  For a representable block the scale-free E8
+// point (u - R + coset/2, coordinate 7 with the parity bit of the other
+// seven) and sc = the head scale; for a fallback row its fp16 values, sc = 1.
+template <int BPT, bool B4>
+__device__ __forceinline__ void cstage_block(const CompactDev &c, const CStageSpan &s, uint32_t buf, uint32_t wi,
+                                             uint32_t lane, float head_scale, float x[8], float &sc, uint32_t *err) {
+    using S = CStage<BPT>;
+    if (s.bad) {
+        raise_flag(err, LQ_EF_BITSTREAM);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] = 0.f;
+        sc = 1.f;
+        return;
+    }
+    const uint32_t w = lds_u32(buf + S::kWordsOff + 4 * wi);
+    const uint32_t r0 = lds_u32(buf + S::kRanksOff + 4 * wi);
+    const uint32_t below = __popc(w & ((1u << lane) - 1u));
+    if ((w >> lane) & 1u) {
+        // stage-relative rank, compared unsigned: a rank below the stage's wraps
+        const uint32_t pr = r0 + below - s.r0;
+        if (pr >= s.r1 - s.r0) {
+            raise_flag(err, LQ_EF_BITSTREAM);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) x[i] = 0.f;
+            sc = 1.f;
+            return;
+        }
+        const int b = B4 ? 4 : c.bits, R = 1 << (b - 1);
         uint32_t u[7], c7u, coset, par;
-        if (bits == 4) {
-            const uint32_t v = __byte_perm(k.raw.x, 0u, 0x0123u);  // big-endian code
+        const uint32_t pbyte = pr * (uint32_t)b + (s.r0 * (uint32_t)b - s.a0);  // byte in the staged codes
+        if constexpr (B4) {
+            const uint32_t v = __byte_perm(lds_u32(buf + S::kPackedOff + pbyte), 0u, 0x0123u);
             coset = v >> 31;
 #pragma unroll
             for (int i = 0; i < 7; ++i) u[i] = (v >> (27 - 4 * i)) & 15u;
             c7u = v & 7u;
             par = __popc(v & 0x08888888u) & 1u;  // low bits of u0..u6
         } else {
-            uint64_t acc = ((uint64_t)k.raw.y << 32) | k.raw.x;
-            c7u = (uint32_t)(acc & ((1ull << (bits - 1)) - 1));
-            acc >>= (bits - 1);
+            const uint32_t o = buf + S::kPackedOff + pbyte;
+            uint64_t acc = 0;
+            for (int i = 0; i < b; ++i) acc = (acc << 8) | (lds_u32((o + i) & ~3u) >> (8 * ((o + i) & 3u)) & 0xffu);
+            c7u = (uint32_t)(acc & ((1ull << (b - 1)) - 1));
+            acc >>= (b - 1);
             par = 0;
 #pragma unroll
             for (int i = 6; i >= 0; --i) {
-                u[i] = (uint32_t)(acc & ((1ull << bits) - 1));
+                u[i] = (uint32_t)(acc & ((1ull << b) - 1));
                 par ^= u[i];
-                acc >>= bits;
+                acc >>= b;
             }
             par &= 1u;
             coset = (uint32_t)(acc & 1u);
@@ -469,29 +510,50 @@ __device__ __forceinline__ void compact_values(const CompactBlock &k, int bits, 
         x[7] = __int_as_float(((2u * c7u + par) << 1) | base) - bias;
         sc = head_scale;
     } else {
-        const uint32_t hw[4] = {k.raw.x, k.raw.y, k.raw.z, k.raw.w};
+        // fallback rows before this block: the stage's first row is b0 - r0 of the chunk
+        const uint32_t f = 32u * wi + lane - below - (r0 - s.r0);
+        if (f >= 32u * s.nw - (s.r1 - s.r0)) {
+            raise_flag(err, LQ_EF_BITSTREAM);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) x[i] = 0.f;
+            sc = 1.f;
+            return;
+        }
+        const uint4 h = lds_v4(buf + S::kFallbackOff + 16u * f);
+        const uint32_t hw[4] = {h.x, h.y, h.z, h.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const float2 f2 = __half22float2(*reinterpret_cast<const __half2 *>(&hw[i]));
             x[2 * i] = f2.x;
             x[2 * i + 1] = f2.y;
         }
+        sc = 1.f;
     }
 }
 
-template <int G, int BPT, int QDT>
+template <int G, int BPT, int QDT, bool B4>
 __global__ void __launch_bounds__(kCompactThreads, 1) attn_compact_kernel(CompactArgs a) {
     static_assert(BPT == 8 || BPT == 16, "head_dim 64 or 128");
+    using S = CStage<BPT>;
     constexpr int D = 8 * BPT, GP = padded_g<G>(), TPS = 32 / BPT;  // tokens per warp step
+    constexpr int kWarpTok = kCStageTok / kCompactWarps;           // tokens of a warp per stage
+    constexpr int kSteps = kWarpTok / TPS;
     extern __shared__ __align__(16) unsigned char smem[];
-    const int warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const int warp = threadIdx.x >> 5;
     const uint32_t lane = threadIdx.x & 31, dc = lane % BPT, tl = lane / BPT;
     const uint32_t head = blockIdx.y;
-    const uint32_t t0 = blockIdx.x * a.tok_per_cta + (uint32_t)warp * a.tok_per_warp;
-    const uint32_t t1 = min(t0 + a.tok_per_warp, a.seq);
-    float *sc = reinterpret_cast<float *>(smem) + (size_t)warp * a.tok_per_warp * GP;
+    const uint32_t T0 = blockIdx.x * a.tok_per_cta, T1 = min(T0 + a.tok_per_cta, a.seq);
+    const uint32_t nst = (T1 - T0 + kCStageTok - 1) / kCStageTok;
+    float *sc = reinterpret_cast<float *>(smem);  // [tok_per_cta][GP]
+    const uint32_t bufs = smem_addr(smem + (size_t)kCTokPerCta * GP * 4);
     const uint32_t b = head / a.n_kv_heads, kvh = head % a.n_kv_heads;
     const float sk = a.k.scales[head], sv = a.v.scales[head];
+    const uint32_t hb0 = head * a.bph;
+    auto stage_blocks = [&](uint32_t st, uint32_t &b0, uint32_t &b1) {
+        const uint32_t t0 = T0 + st * kCStageTok, t1 = min(t0 + kCStageTok, T1);
+        b0 = hb0 + t0 * BPT;
+        b1 = hb0 + t1 * BPT;
+    };
 
     constexpr int GH = G / 2;
     unsigned long long q2[GH > 0 ? GH : 1][8];
@@ -511,36 +573,55 @@ __global__ void __launch_bounds__(kCompactThreads, 1) attn_compact_kernel(Compac
         }
     }
 
-    // A warp step covers 32 consecutive blocks (TPS tokens) = one mask
-    // word; lane i holds the word and rank of step i, read at the start.
-    const uint32_t nsteps = t1 > t0 ? (t1 - t0 + TPS - 1) / TPS : 0u;
-    const uint32_t w0 = (head * a.bph + t0 * BPT) >> 5;
-    auto fetch = [&](const CompactDev &c, uint32_t mw, int mr, uint32_t it) {
-        const uint32_t w = __shfl_sync(0xffffffffu, mw, it);
-        const int r0 = __shfl_sync(0xffffffffu, mr, it);
-        const uint32_t tok = t0 + it * TPS + tl;
-        return compact_fetch(c, w, r0, w0 + it, lane, tok < t1, a.err);
-    };
-    uint32_t kw = 0, vw = 0;
-    int kr = 0, vr = 0;
-    if (lane < nsteps) {
-        kw = __ldg(a.k.mask_words + w0 + lane);
-        kr = __ldg(a.k.word_rank + w0 + lane);
-        vw = __ldg(a.v.mask_words + w0 + lane);
-        vr = __ldg(a.v.word_rank + w0 + lane);
+    // where every stage of both phases starts in the chunks' arrays, read
+    // once (8 threads in parallel) so no copy waits for a rank load
+    constexpr int kMaxStages = kCTokPerCta / kCStageTok;
+    __shared__ CStageSpan spans[2][kMaxStages];
+    if (threadIdx.x < 2 * kMaxStages) {
+        const uint32_t ph = threadIdx.x / kMaxStages, st = threadIdx.x % kMaxStages;
+        if (st < nst) {
+            uint32_t b0, b1;
+            stage_blocks(st, b0, b1);
+            spans[ph][st] = cstage_span(ph ? a.v : a.k, b0, b1);
+        }
     }
+    __syncthreads();
 
-    // ---- phase K: scores (base 2) of the warp's tokens into shared memory
-    CompactBlock cur = fetch(a.k, kw, kr, 0);
-    for (uint32_t it = 0; it < nsteps; ++it) {
-        const uint32_t tok = t0 + it * TPS + tl;
-        const bool ok = tok < t1;
-        // the next step's block is requested before this one is used
-        CompactBlock nxt = cur;
-        if (it + 1 < nsteps) nxt = fetch(a.k, kw, kr, it + 1);
-        float kx[8], s;
-        compact_values(cur, a.k.bits, sk, kx, s);
-        cur = nxt;
+    // one phase (K or V) over the CTA's stages, double-buffered
+    auto phase = [&](const CompactDev &c, const CStageSpan *sp, auto &&body) {
+        uint32_t b0, b1;
+        stage_blocks(0, b0, b1);
+        cstage_issue<BPT>(c, sp[0], b0, bufs);
+        if (nst > 1) {
+            stage_blocks(1, b0, b1);
+            cstage_issue<BPT>(c, sp[1], b0, bufs + S::kBytes);
+        }
+        for (uint32_t st = 0; st < nst; ++st) {
+            if (st + 1 < nst) cp_async_wait<1>();
+            else cp_async_wait<0>();
+            __syncthreads();
+            const uint32_t buf = bufs + (st & 1u) * S::kBytes;
+            const CStageSpan s = sp[st];
+            const uint32_t t0 = T0 + st * kCStageTok;
+#pragma unroll 2
+            for (int j = 0; j < kSteps; ++j) {
+                const uint32_t tb = t0 + (uint32_t)(warp * kWarpTok + j * TPS);  // step's first token
+                if (tb >= T1) break;
+                const uint32_t wi = (uint32_t)(warp * kWarpTok + j * TPS) * BPT / 32u;
+                body(s, buf, wi, tb + tl, tb + tl < T1);
+            }
+            __syncthreads();
+            if (st + 2 < nst) {
+                stage_blocks(st + 2, b0, b1);
+                cstage_issue<BPT>(c, sp[st + 2], b0, buf);
+            }
+        }
+    };
+
+    // ---- phase K: scores (base 2) of the CTA's tokens into shared memory
+    phase(a.k, spans[0], [&](const CStageSpan &s, uint32_t buf, uint32_t wi, uint32_t tok, bool ok) {
+        float kx[8], scl;
+        cstage_block<BPT, B4>(a.k, s, buf, wi, lane, sk, kx, scl, a.err);
         float dot[G];
 #pragma unroll
         for (int g = 0; g + 1 < G; g += 2) {
@@ -555,44 +636,67 @@ __global__ void __launch_bounds__(kCompactThreads, 1) attn_compact_kernel(Compac
             for (int i = 1; i < 8; ++i) d = __fmaf_rn(qlast[i], kx[i], d);
             dot[G - 1] = d;
         }
+        const float f = ok ? scl * a.qk_log2 : 0.f;
 #pragma unroll
-        for (int g = 0; g < G; ++g) dot[g] *= s;
+        for (int g = 0; g < G; ++g) dot[g] *= f;
+        float *row = sc + (tok - T0) * GP;
+        if constexpr (G == 4 && BPT == 16) {
+            // transposing reduction over the token's 16 lanes (as in the rANS kernel)
+            const bool h8 = (dc & 8u) != 0, h4 = (dc & 4u) != 0;
+            float a0 = h8 ? dot[2] : dot[0], a1 = h8 ? dot[3] : dot[1];
+            const float s0 = h8 ? dot[0] : dot[2], s1 = h8 ? dot[1] : dot[3];
+            a0 += __shfl_xor_sync(0xffffffffu, s0, 8);
+            a1 += __shfl_xor_sync(0xffffffffu, s1, 8);
+            float bsum = h4 ? a1 : a0;
+            bsum += __shfl_xor_sync(0xffffffffu, h4 ? a0 : a1, 4);
+            bsum += __shfl_xor_sync(0xffffffffu, bsum, 2);
+            bsum += __shfl_xor_sync(0xffffffffu, bsum, 1);
+            if (ok && (dc & 3u) == 0) row[dc >> 2] = bsum;
+        } else {
 #pragma unroll
-        for (int off = BPT / 2; off >= 1; off >>= 1) {
+            for (int off = BPT / 2; off >= 1; off >>= 1) {
 #pragma unroll
-            for (int g = 0; g < G; ++g) dot[g] += __shfl_xor_sync(0xffffffffu, dot[g], off);
+                for (int g = 0; g < G; ++g) dot[g] += __shfl_xor_sync(0xffffffffu, dot[g], off);
+            }
+            if (ok && dc < (uint32_t)G) {
+                float v = dot[0];
+#pragma unroll
+                for (int g = 1; g < G; ++g) v = (dc == (uint32_t)g) ? dot[g] : v;
+                row[dc] = v;
+            }
         }
-        if (ok && dc < (uint32_t)G) {
-            float v = dot[0];
-#pragma unroll
-            for (int g = 1; g < G; ++g) v = (dc == (uint32_t)g) ? dot[g] : v;
-            sc[(tok - t0) * GP + dc] = v * a.qk_log2;
-        }
-    }
-    __syncwarp();
+    });
 
-    // ---- softmax statistics of the warp's tokens
-    const uint32_t ntok = t1 > t0 ? t1 - t0 : 0u;
+    // ---- softmax statistics of the warp's tokens (its kWarpTok of each stage)
+    __syncwarp();
+    auto tok_rel = [&](uint32_t i) {  // i-th token of this warp, relative to T0
+        return (i / kWarpTok) * kCStageTok + (uint32_t)warp * kWarpTok + i % kWarpTok;
+    };
+    const uint32_t nmine = nst * kWarpTok;
     float m[G], l[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
         m[g] = -INFINITY;
         l[g] = 0.f;
     }
-    for (uint32_t i = lane; i < ntok; i += 32) {
+    for (uint32_t i = lane; i < nmine; i += 32) {
+        const uint32_t t = tok_rel(i);
+        if (T0 + t >= T1) continue;
 #pragma unroll
-        for (int g = 0; g < G; ++g) m[g] = fmaxf(m[g], sc[i * GP + g]);
+        for (int g = 0; g < G; ++g) m[g] = fmaxf(m[g], sc[t * GP + g]);
     }
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) {
 #pragma unroll
         for (int g = 0; g < G; ++g) m[g] = fmaxf(m[g], __shfl_xor_sync(0xffffffffu, m[g], off));
     }
-    for (uint32_t i = lane; i < ntok; i += 32) {
+    for (uint32_t i = lane; i < nmine; i += 32) {
+        const uint32_t t = tok_rel(i);
+        if (T0 + t >= T1) continue;
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-            const float p = exp2f(sc[i * GP + g] - m[g]);
-            sc[i * GP + g] = p;
+            const float p = exp2f(sc[t * GP + g] - m[g]);
+            sc[t * GP + g] = p;
             l[g] += p;
         }
     }
@@ -609,28 +713,22 @@ __global__ void __launch_bounds__(kCompactThreads, 1) attn_compact_kernel(Compac
     for (int g = 0; g < G; ++g)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc2[g][i] = 0ull;
-    cur = fetch(a.v, vw, vr, 0);
-    for (uint32_t it = 0; it < nsteps; ++it) {
-        const uint32_t tok = t0 + it * TPS + tl;
-        const bool ok = tok < t1;
-        CompactBlock nxt = cur;
-        if (it + 1 < nsteps) nxt = fetch(a.v, vw, vr, it + 1);
-        float vx[8], s;
-        compact_values(cur, a.v.bits, sv, vx, s);
-        cur = nxt;
-        if (!ok) continue;
-        const float *pp = sc + (tok - t0) * GP;
+    phase(a.v, spans[1], [&](const CStageSpan &s, uint32_t buf, uint32_t wi, uint32_t tok, bool ok) {
+        float vx[8], scl;
+        cstage_block<BPT, B4>(a.v, s, buf, wi, lane, sv, vx, scl, a.err);
+        if (!ok) return;
+        const float *pp = sc + (tok - T0) * GP;
         unsigned long long v2[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) v2[i] = f2_pack(vx[2 * i], vx[2 * i + 1]);
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-            const float pg = pp[g] * s;
+            const float pg = pp[g] * scl;
             const unsigned long long p2 = f2_pack(pg, pg);
 #pragma unroll
             for (int i = 0; i < 4; ++i) acc2[g][i] = f2_fma(p2, v2[i], acc2[g][i]);
         }
-    }
+    });
     float acc[G][8];
 #pragma unroll
     for (int g = 0; g < G; ++g)
@@ -645,9 +743,8 @@ __global__ void __launch_bounds__(kCompactThreads, 1) attn_compact_kernel(Compac
             for (int i = 0; i < 8; ++i) acc[g][i] += __shfl_xor_sync(0xffffffffu, acc[g][i], off);
     }
 
-    // ---- merge the warps in a fixed order (the score region is done with)
-    __syncthreads();
-    float *mrg = reinterpret_cast<float *>(smem);
+    // ---- merge the warps in a fixed order (the stage buffers are done with)
+    float *mrg = reinterpret_cast<float *>(smem + (size_t)kCTokPerCta * GP * 4);
     const int rs = D + 2;
     if (lane < (uint32_t)BPT) {
 #pragma unroll
@@ -667,9 +764,9 @@ __global__ void __launch_bounds__(kCompactThreads, 1) attn_compact_kernel(Compac
     for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
         const int g = e / D, dd = e % D;
         float mx = -INFINITY;
-        for (int w = 0; w < nwarps; ++w) mx = fmaxf(mx, mrg[(w * G + g) * rs + D]);
+        for (int w = 0; w < kCompactWarps; ++w) mx = fmaxf(mx, mrg[(w * G + g) * rs + D]);
         float o = 0.f, ls = 0.f;
-        for (int w = 0; w < nwarps; ++w) {
+        for (int w = 0; w < kCompactWarps; ++w) {
             const float mw = mrg[(w * G + g) * rs + D];
             if (mw == -INFINITY) continue;
             const float f = exp2f(mw - mx);
@@ -816,28 +913,27 @@ int launch_partial_g(const AttnArgs &a, const AttnPlan &p, uint32_t n_heads, int
 
 // ---- compact-layout attention: plan and launch
 struct CompactPlan {
-    uint32_t nct, tok_per_warp, tok_per_cta;
+    uint32_t nct, tok_per_cta;
     size_t smem, part_floats;
 };
 
 int compact_plan(int64_t n_heads, int64_t seq, int G, int D, CompactPlan *p) {
     if (n_heads <= 0 || seq <= 0 || G < 1 || G > 8 || (D != 64 && D != 128)) return LQ_ERR_INVALID;
-    const int bpt = D / 8, tps = 32 / bpt;
+    const int bpt = D / 8;
     if ((seq * bpt) % 32 != 0 || n_heads > 65535 || n_heads * seq * bpt >= ((int64_t)1 << 31)) return LQ_ERR_INVALID;
-    const int nw = kCompactThreads / 32;
-    p->tok_per_warp = 64u;  // a multiple of the tokens per step (2 or 4)
-    (void)tps;
-    p->tok_per_cta = p->tok_per_warp * nw;
+    p->tok_per_cta = kCTokPerCta;
     p->nct = (uint32_t)ceil_div(seq, p->tok_per_cta);
     const size_t gp = (size_t)((G + 3) & ~3);
-    p->smem = std::max<size_t>((size_t)nw * p->tok_per_warp * gp * 4, (size_t)nw * G * (D + 2) * 4);
+    const size_t stages = 2 * (size_t)(bpt == 16 ? CStage<16>::kBytes : CStage<8>::kBytes);
+    const size_t merge = (size_t)kCompactWarps * G * (D + 2) * 4;
+    p->smem = (size_t)kCTokPerCta * gp * 4 + std::max(stages, merge);
     p->part_floats = (size_t)n_heads * p->nct * G * (D + 2);
     return LQ_OK;
 }
 
-template <int G, int BPT, int QDT>
+template <int G, int BPT, int QDT, bool B4>
 int launch_compact(const CompactArgs &a, const CompactPlan &p, uint32_t n_heads, cudaStream_t st) {
-    auto kern = attn_compact_kernel<G, BPT, QDT>;
+    auto kern = attn_compact_kernel<G, BPT, QDT, B4>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem) != cudaSuccess)
         return LQ_ERR_CUDA;
     kern<<<dim3(p.nct, n_heads), kCompactThreads, p.smem, st>>>(a);
@@ -846,10 +942,17 @@ int launch_compact(const CompactArgs &a, const CompactPlan &p, uint32_t n_heads,
 
 template <int G, int BPT>
 int launch_compact_q(const CompactArgs &a, const CompactPlan &p, uint32_t n_heads, int q_dtype, cudaStream_t st) {
+    const bool b4 = a.k.bits == 4 && a.v.bits == 4;
     switch (q_dtype) {
-        case LQ_F32: return launch_compact<G, BPT, LQ_F32>(a, p, n_heads, st);
-        case LQ_F16: return launch_compact<G, BPT, LQ_F16>(a, p, n_heads, st);
-        case LQ_BF16: return launch_compact<G, BPT, LQ_BF16>(a, p, n_heads, st);
+        case LQ_F32:
+            return b4 ? launch_compact<G, BPT, LQ_F32, true>(a, p, n_heads, st)
+                      : launch_compact<G, BPT, LQ_F32, false>(a, p, n_heads, st);
+        case LQ_F16:
+            return b4 ? launch_compact<G, BPT, LQ_F16, true>(a, p, n_heads, st)
+                      : launch_compact<G, BPT, LQ_F16, false>(a, p, n_heads, st);
+        case LQ_BF16:
+            return b4 ? launch_compact<G, BPT, LQ_BF16, true>(a, p, n_heads, st)
+                      : launch_compact<G, BPT, LQ_BF16, false>(a, p, n_heads, st);
         default: return LQ_ERR_INVALID;
     }
 }
@@ -863,15 +966,24 @@ int launch_compact_g(const CompactArgs &a, const CompactPlan &p, uint32_t n_head
 bool compact_ok(const lq_compact_view *c, int64_t n_heads, int64_t bph) {
     if (!c || !c->mask_words || !c->word_rank || !c->scales || c->n_heads != n_heads || c->bph != bph) return false;
     if (c->bits < 3 || c->bits > 5 || c->n_repr < 0 || c->n_fallback < 0) return false;
-    if (c->n_repr > 0 && !c->packed) return false;
+    if (c->n_repr + c->n_fallback != n_heads * bph) return false;
+    if (c->n_repr > 0 && (!c->packed || (reinterpret_cast<uintptr_t>(c->packed) & 15))) return false;
     if (c->n_fallback > 0 && (!c->fallback || (reinterpret_cast<uintptr_t>(c->fallback) & 15))) return false;
-    if (c->bits == 4 && c->n_repr > 0 && (reinterpret_cast<uintptr_t>(c->packed) & 3)) return false;
-    return c->n_repr <= 0xffffffffLL && c->n_fallback <= 0xffffffffLL;
+    if ((reinterpret_cast<uintptr_t>(c->mask_words) & 3) || (reinterpret_cast<uintptr_t>(c->word_rank) & 3))
+        return false;
+    return c->n_repr * c->bits < 0xffffffffLL;
 }
 
 CompactDev to_compact(const lq_compact_view *c) {
-    return CompactDev{c->packed, reinterpret_cast<const uint4 *>(c->fallback), c->mask_words, c->word_rank, c->scales,
-                      (uint32_t)c->n_repr, (uint32_t)c->n_fallback, c->bits};
+    return CompactDev{c->packed,
+                      reinterpret_cast<const uint4 *>(c->fallback),
+                      c->mask_words,
+                      c->word_rank,
+                      c->scales,
+                      (uint32_t)c->n_repr,
+                      (uint32_t)c->n_fallback,
+                      (uint32_t)ceil_div(c->n_heads * c->bph, 32),
+                      c->bits};
 }
 
 bool view_ok(const lq_chunk_view *c) {
@@ -992,7 +1104,6 @@ extern "C" int lq_attn_decode_compact(const lq_compact_view *k, const lq_compact
     a.bph = (uint32_t)bph;
     a.nct = p.nct;
     a.tok_per_cta = p.tok_per_cta;
-    a.tok_per_warp = p.tok_per_warp;
     a.qk_log2 = sm_scale * kLog2e;
     a.part = static_cast<float *>(workspace);
     a.err = err;

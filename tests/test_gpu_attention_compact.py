@@ -99,3 +99,29 @@ def test_compact_attention_rejects_unaligned_heads():
     q = torch.randn(1, 1, 128, dtype=torch.bfloat16, device="cuda")
     with pytest.raises(ValueError):
         attention.decode_attention_compact(q, kc, kc)
+
+
+@pytest.mark.parametrize("how", ["rank_high", "rank_order", "mask_bits"])
+def test_compact_attention_flags_inconsistent_index(how):
+    """Mask words or ranks that disagree with the arrays (a damaged chunk) are
+    caught by the kernel's range checks: the BITSTREAM flag, no stray access."""
+    from latticequant_b200 import attention
+    from latticequant_b200.llm.fused_triton_merge import compress_compact
+
+    k = _kv((1, 2, 512, 128), 31).cuda()
+    kc, _ = compress_compact(k, 4)
+    vc, _ = compress_compact(_kv((1, 2, 512, 128), 32).cuda(), 4)
+    words, rank = attention.compact_index(kc)
+    words, rank = words.clone(), rank.clone()
+    if how == "rank_high":
+        rank[5:9] += 100000
+    elif how == "rank_order":
+        rank[40:] -= 7
+    else:
+        words[3:6] = -1  # every block representable: more codes than the ranks allow
+    kc._lq_index = (words, rank)
+    q = torch.randn(1, 8, 128, dtype=torch.bfloat16, device="cuda")
+    from latticequant_b200._lib import LatticeQuantError
+
+    with pytest.raises(LatticeQuantError, match="decode_attention_compact"):
+        attention.decode_attention_compact(q, kc, vc)
