@@ -226,6 +226,46 @@ def compact_view(chunk) -> "_lib.CompactView":
                             chunk.scales.data_ptr(), B * H, S * D // 8, int(chunk.bits_per_dim))
 
 
+class CompactDecodeAttention:
+    """decode_attention_compact prepared once for a (K chunk, V chunk) pair
+    (llm.fused_triton_merge.CompressedChunk each): workspace, error word and
+    chunk views allocated up front, launches without host syncs; flags()
+    reads the error word."""
+
+    def __init__(self, k_chunk, v_chunk, group: int):
+        kshape = tuple(k_chunk.orig_shape)
+        if tuple(v_chunk.orig_shape) != kshape:
+            raise ValueError("K and V chunks differ in shape")
+        self.k, self.v, self.group, self.shape = k_chunk, v_chunk, int(group), kshape
+        B, Hkv, S, D = kshape
+        dev = k_chunk.repr_mask.device
+        _lib.require_cuda(k_chunk.repr_mask)
+        need = int(lib().lq_attn_compact_workspace(B * Hkv, S, self.group, D))
+        if need == 0:
+            raise ValueError(f"compact attention does not take shape {kshape} with group {group} "
+                             "(head_dim 64/128, seq*head_dim/8 a multiple of 32, group 1..8)")
+        self.workspace = torch.empty(need, dtype=torch.uint8, device=dev)
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.kv, self.vv = compact_view(k_chunk), compact_view(v_chunk)
+
+    def __call__(self, q3: torch.Tensor, out: torch.Tensor, lse: Optional[torch.Tensor] = None,
+                 sm_scale: Optional[float] = None):
+        """q3 (B, Hq, D) contiguous -> out (B, Hq, D); lse (B, Hq) fp32 if given."""
+        B, Hkv, S, D = self.shape
+        if q3.shape != (B, Hkv * self.group, D) or not q3.is_contiguous():
+            raise ValueError(f"q must be a contiguous ({B}, {Hkv * self.group}, {D}) tensor")
+        scale = (1.0 / math.sqrt(D)) if sm_scale is None else float(sm_scale)
+        check(lib().lq_attn_decode_compact(ctypes.byref(self.kv), ctypes.byref(self.vv), ptr(q3),
+                                           _lib.dtype_code(q3.dtype), B, Hkv, S, self.group, D, scale, ptr(out),
+                                           _lib.dtype_code(out.dtype), ptr(lse) if lse is not None else None,
+                                           ptr(self.workspace), self.workspace.numel(), ptr(self.err),
+                                           stream_handle(q3.device)), "lq_attn_decode_compact")
+        return out
+
+    def flags(self) -> int:
+        return int(self.err.item()) & 0xFFFFFFFF
+
+
 def decode_attention_compact(q: torch.Tensor, k_chunk, v_chunk, sm_scale: Optional[float] = None,
                              out_dtype: Optional[torch.dtype] = None, return_lse: bool = False,
                              out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None):
@@ -240,25 +280,14 @@ def decode_attention_compact(q: torch.Tensor, k_chunk, v_chunk, sm_scale: Option
         raise ValueError("K and V chunks differ in shape")
     q3 = _q3(q, kshape).contiguous()
     B, Hkv, S, D = kshape
-    G = q3.shape[1] // Hkv
+    op = CompactDecodeAttention(k_chunk, v_chunk, q3.shape[1] // Hkv)
     dev = q.device
-    need = int(lib().lq_attn_compact_workspace(B * Hkv, S, G, D))
-    if need == 0:
-        raise ValueError(f"compact attention does not take shape {kshape} with group {G} "
-                         "(head_dim 64/128, seq*head_dim/8 a multiple of 32, group 1..8)")
-    ws = torch.empty(need, dtype=torch.uint8, device=dev)
     if out is None:
         out = torch.empty(q3.shape, dtype=out_dtype or q.dtype, device=dev)
     if return_lse and lse is None:
         lse = torch.empty(q3.shape[:2], dtype=torch.float32, device=dev)
-    err = torch.zeros(1, dtype=torch.int32, device=dev)
-    kv, vv = compact_view(k_chunk), compact_view(v_chunk)
-    scale = (1.0 / math.sqrt(D)) if sm_scale is None else float(sm_scale)
-    check(lib().lq_attn_decode_compact(ctypes.byref(kv), ctypes.byref(vv), ptr(q3), _lib.dtype_code(q3.dtype), B,
-                                       Hkv, S, G, D, scale, ptr(out), _lib.dtype_code(out.dtype),
-                                       ptr(lse) if return_lse else None, ptr(ws), ws.numel(), ptr(err),
-                                       stream_handle(dev)), "lq_attn_decode_compact")
-    raise_flags(int(err.item()) & 0xFFFFFFFF, "decode_attention_compact")
+    op(q3, out, lse if return_lse else None, sm_scale)
+    raise_flags(op.flags(), "decode_attention_compact")
     o = out.view(tuple(q.shape[:-1]) + (D,)) if q.dim() == 4 else out
     return (o, lse) if return_lse else o
 

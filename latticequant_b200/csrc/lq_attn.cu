@@ -378,7 +378,7 @@ struct CompactArgs {
 
 constexpr int kCompactThreads = 512;
 constexpr int kCompactWarps = kCompactThreads / 32;
-constexpr int kCStageTok = 256;     // tokens per shared-memory stage
+constexpr int kCStageTok = 128;     // tokens per shared-memory stage (two CTAs fit an SM)
 constexpr int kCTokPerCta = 1024;   // tokens per CTA (4 stages)
 
 // Shared-memory stage of one chunk's blocks of kCStageTok tokens: mask words,
@@ -532,7 +532,7 @@ __device__ __forceinline__ void cstage_block(const CompactDev &c, const CStageSp
 }
 
 template <int G, int BPT, int QDT, bool B4>
-__global__ void __launch_bounds__(kCompactThreads, 1) attn_compact_kernel(CompactArgs a) {
+__global__ void __launch_bounds__(kCompactThreads, G <= 4 ? 2 : 1) attn_compact_kernel(CompactArgs a) {
     static_assert(BPT == 8 || BPT == 16, "head_dim 64 or 128");
     using S = CStage<BPT>;
     constexpr int D = 8 * BPT, GP = padded_g<G>(), TPS = 32 / BPT;  // tokens per warp step
@@ -602,6 +602,14 @@ __global__ void __launch_bounds__(kCompactThreads, 1) attn_compact_kernel(Compac
             __syncthreads();
             const uint32_t buf = bufs + (st & 1u) * S::kBytes;
             const CStageSpan s = sp[st];
+            // the stage's index must chain: rank(w+1) - rank(w) = popcount(word w),
+            // from the stage's first rank to its last
+            for (uint32_t i = threadIdx.x; i < s.nw && !s.bad; i += blockDim.x) {
+                const uint32_t ri = lds_u32(buf + S::kRanksOff + 4 * i);
+                const uint32_t rn = i + 1 < s.nw ? lds_u32(buf + S::kRanksOff + 4 * (i + 1)) : s.r1;
+                if (rn - ri != (uint32_t)__popc(lds_u32(buf + S::kWordsOff + 4 * i)) || (i == 0 && ri != s.r0))
+                    raise_flag(a.err, LQ_EF_BITSTREAM);
+            }
             const uint32_t t0 = T0 + st * kCStageTok;
 #pragma unroll 2
             for (int j = 0; j < kSteps; ++j) {

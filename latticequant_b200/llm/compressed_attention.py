@@ -48,16 +48,20 @@ def _attn_tile(bph: int, limit: int) -> Optional[int]:
 
 
 class _Part:
-    """One compressed (K, V) chunk pair of a layer and its prepared attention."""
+    """One compressed (K, V) chunk pair of a layer and its prepared attention:
+    LaneChunks (rANS lanes) or, for layout "compact", CompressedChunks."""
 
-    def __init__(self, k: LaneChunk, v: LaneChunk, shape, per_token: bool):
-        self.k, self.v, self.shape, self.per_token = k, v, tuple(shape), per_token
+    def __init__(self, k, v, shape, per_token: bool, layout: str = "rans"):
+        self.k, self.v, self.shape, self.per_token, self.layout = k, v, tuple(shape), per_token, layout
         self.ops = {}
 
-    def op(self, group: int) -> A.DecodeAttention:
+    def op(self, group: int):
         if group not in self.ops:
-            self.ops[group] = A.DecodeAttention(self.k, self.v, group, shape=self.shape,
-                                                scale_per_token=self.per_token)
+            if self.layout == "compact":
+                self.ops[group] = A.CompactDecodeAttention(self.k, self.v, group)
+            else:
+                self.ops[group] = A.DecodeAttention(self.k, self.v, group, shape=self.shape,
+                                                    scale_per_token=self.per_token)
         return self.ops[group]
 
 
@@ -77,13 +81,23 @@ class CompressedAttentionKVCache(CompressedKVCache):
 
       tail_tokens  decode tokens encoded together (a multiple of 2; 64 makes
                    one 1024-block tile per (batch, KV head) at head_dim 128)
+      layout       "rans" (entropy-coded lanes, llm/compressed_kv_cache.py's
+                   format) or "compact" (the fixed-rate codes + fp16 fallback
+                   rows of llm/fused_triton_merge.py, bits 3..5): prefill
+                   chunks in that layout are attended with
+                   lq_attn_decode_compact; encoded tails stay dequantised
     """
 
     def __init__(self, bits_per_dim: int = 4, tail_tokens: int = 64,
                  tile_blocks: Optional[int] = codec.DEFAULT_TILE_BLOCKS, table_mode: str = "device",
-                 head_range: Optional[Tuple[int, int]] = None, group=None):
+                 head_range: Optional[Tuple[int, int]] = None, group=None, layout: str = "rans"):
         super().__init__(bits_per_dim=bits_per_dim, eval_only_no_entropy=False, tile_blocks=tile_blocks,
                          table_mode=table_mode)
+        if layout not in ("rans", "compact"):
+            raise ValueError("layout must be 'rans' or 'compact'")
+        if layout == "compact" and bits_per_dim not in (3, 4, 5):
+            raise ValueError("the compact layout takes 3, 4 or 5 bits per dimension")
+        self.layout = layout
         if tail_tokens < 2 or tail_tokens % 2:
             raise ValueError("tail_tokens must be an even number >= 2")
         self.tail_tokens = int(tail_tokens)
@@ -151,6 +165,23 @@ class CompressedAttentionKVCache(CompressedKVCache):
         B, H, S, D = k.shape
         history = self._materialise(st) if st.seq > 0 else None
         self._flush_tail(st, layer_idx, force=True)
+        if self.layout == "compact":
+            from .fused_triton_merge import compress_compact, fused_decompress_chunk
+
+            ck, kd = compress_compact(k, int(self.bits))
+            cv, vd = compress_compact(v, int(self.bits))
+            self.total_vectors += ck.n_vectors + cv.n_vectors
+            self._comp_keys[layer_idx].append_chunk(ck)
+            self._comp_values[layer_idx].append_chunk(cv)
+            if (S * D // 8) % 32 == 0:
+                st.parts.append(_Part(ck, cv, (B, H, S, D), per_token=False, layout="compact"))
+            else:  # heads not 32-block aligned: keep this chunk merged (fp16 values)
+                st.dense_k.append(fused_decompress_chunk(ck))
+                st.dense_v.append(fused_decompress_chunk(cv))
+            st.seq += S
+            if history is not None:
+                return torch.cat([history[0], kd], 2), torch.cat([history[1], vd], 2)
+            return kd, vd
         tile = _attn_tile(S * D // 8, self.tile_blocks or codec.DEFAULT_TILE_BLOCKS)
         ck, kd = self._compress_with_tile(k, tile or 32)
         cv, vd = self._compress_with_tile(v, tile or 32)
@@ -201,8 +232,17 @@ class CompressedAttentionKVCache(CompressedKVCache):
         vv = st.tail_raw_v[:, :, :n].reshape(B, H * n, 1, D)
         tile = _attn_tile(n * D // 8, self.tile_blocks or codec.DEFAULT_TILE_BLOCKS)
         saved = self.total_vectors
-        ck, _ = self._compress_with_tile(kk, tile or 32)
-        cv, _ = self._compress_with_tile(vv, tile or 32)
+        if self.layout == "compact":
+            # stored compact (one scale per token); attended from the dequantised
+            # tail, since a token's 16 blocks are not a 32-block-aligned head
+            from .fused_triton_merge import compress_compact
+
+            ck, _ = compress_compact(kk, int(self.bits))
+            cv, _ = compress_compact(vv, int(self.bits))
+            tile = None
+        else:
+            ck, _ = self._compress_with_tile(kk, tile or 32)
+            cv, _ = self._compress_with_tile(vv, tile or 32)
         self.total_vectors = saved  # counted when the tokens arrived
         self._comp_keys[layer_idx].append_chunk(ck)
         self._comp_values[layer_idx].append_chunk(cv)
@@ -219,6 +259,12 @@ class CompressedAttentionKVCache(CompressedKVCache):
         dt = dtype or self._model_dtype
         ks, vs = [], []
         for p in st.parts:
+            if p.layout == "compact":
+                from .fused_triton_merge import fused_decompress_chunk
+
+                ks.append(fused_decompress_chunk(p.k).to(dt))
+                vs.append(fused_decompress_chunk(p.v).to(dt))
+                continue
             ks.append(codec.decompress(p.k, out_dtype=dt).view(p.shape))
             vs.append(codec.decompress(p.v, out_dtype=dt).view(p.shape))
         ks += [t.to(dt) for t in st.dense_k]

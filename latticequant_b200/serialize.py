@@ -76,6 +76,8 @@ def cache_state(cache) -> Dict[str, Any]:
     from .llm.compressed_attention import CompressedAttentionKVCache
     from .llm.compressed_kv_cache import CompressedKVLayer, UncompressibleKVLayer
 
+    if getattr(cache, "layout", "rans") != "rans":
+        raise ValueError("caches in the compact layout cannot be saved (only rANS-lane chunks)")
     layers = []
     for lk, lv in zip(cache._comp_keys, cache._comp_values):
         if lk is None:

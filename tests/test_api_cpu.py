@@ -117,3 +117,31 @@ def test_rht_signs_match_reference():
     assert torch.equal(H @ H.T, 8 * torch.eye(8))
     w = torch.arange(32.0).reshape(2, 16)
     assert torch.equal(from_blocks(to_blocks(w)), w)
+
+
+def test_compact_index_words_and_ranks():
+    """attention.compact_index: bit i of word w = block 32w+i representable
+    (bit 31 included, as a negative int32), rank = representable blocks before
+    word w; a ragged last word."""
+    import types
+
+    import numpy as np
+    import torch
+
+    from latticequant_b200 import attention
+
+    rng = np.random.default_rng(3)
+    for n in (32, 70, 1000):
+        m = rng.random(n) < 0.7
+        m[31] = True
+        ch = types.SimpleNamespace(repr_mask=torch.from_numpy(m))
+        words, rank = attention.compact_index(ch)
+        nw = (n + 31) // 32
+        pad = np.zeros(nw * 32, bool)
+        pad[:n] = m
+        bits = pad.reshape(nw, 32)
+        ref_w = (bits.astype(np.uint64) << np.arange(32, dtype=np.uint64)).sum(1).astype(np.uint32)
+        assert np.array_equal(words.numpy().view(np.uint32), ref_w)
+        cnt = bits.sum(1)
+        assert np.array_equal(rank.numpy(), np.concatenate([[0], np.cumsum(cnt)[:-1]]).astype(np.int32))
+        assert attention.compact_index(ch) is ch._lq_index  # cached

@@ -93,3 +93,39 @@ def test_tiny_llama_decode_through_hook():
     assert cache.flags() == 0
     assert cache.get_seq_length(0) == 128 + steps
     assert worst < 2e-2, worst
+
+
+@pytest.mark.parametrize("bits", [4, 3])
+def test_compact_layout_decode_attention(bits):
+    """layout="compact": the prefill chunk in the compact fixed-rate layout
+    (llm/fused_triton_merge.py's format) attended with lq_attn_decode_compact,
+    decode tokens in the exact tail, flushed tails kept dequantised; against
+    float64 attention over every token dequantised (the merged fp16 values of
+    the compact chunk, the tail's fp32-scale values)."""
+    from latticequant_b200.llm.compressed_attention import CompressedAttentionKVCache
+
+    torch.manual_seed(4)
+    B, H, G, S0, D, steps = 2, 2, 4, 256, 128, 70
+    cache = CompressedAttentionKVCache(bits, tail_tokens=64, layout="compact")
+    k = torch.randn(B, H, S0, D, device="cuda", dtype=torch.bfloat16)
+    v = torch.randn(B, H, S0, D, device="cuda", dtype=torch.bfloat16)
+    cache.update(k, v, 0)
+    worst = 0.0
+    for _ in range(steps):
+        cache.update(torch.randn(B, H, 1, D, device="cuda", dtype=torch.bfloat16),
+                     torch.randn(B, H, 1, D, device="cuda", dtype=torch.bfloat16), 0)
+        q = torch.randn(B, H * G, 1, D, device="cuda", dtype=torch.float32) / math.sqrt(D)
+        o = cache.decode_attention(0, q)
+        kk, vv = cache._materialise(cache._state[0], torch.float32)
+        ref = _ref_attention(q, kk, vv, 1 / math.sqrt(D))
+        worst = max(worst, ((o.double() - ref).abs().amax(-1) / ref.abs().amax(-1)).max().item())
+    assert cache.flags() == 0
+    assert worst <= 1e-3, worst
+    st = cache._state[0]
+    assert len(st.parts) == 1 and st.parts[0].layout == "compact"
+    assert len(st.dense_k) == 1 and st.n_tail == steps - 64
+    assert cache.get_seq_length(0) == S0 + steps
+    with pytest.raises(ValueError):
+        from latticequant_b200 import serialize
+
+        serialize.cache_state(cache)
