@@ -454,29 +454,20 @@ template <int BPT, bool B4>
 __device__ __forceinline__ void cstage_block(const CompactDev &c, const CStageSpan &s, uint32_t buf, uint32_t wi,
                                              uint32_t lane, float head_scale, float x[8], float &sc, uint32_t *err) {
     using S = CStage<BPT>;
-    if (s.bad) {
-        raise_flag(err, LQ_EF_BITSTREAM);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) x[i] = 0.f;
-        sc = 1.f;
-        return;
-    }
+    // The stage's index was validated when it arrived (a mismatch raised the
+    // flag); here every index is only clamped into the staged arrays, so a
+    // damaged chunk reads garbage values but never outside shared memory.
+    (void)err;
     const uint32_t w = lds_u32(buf + S::kWordsOff + 4 * wi);
     const uint32_t r0 = lds_u32(buf + S::kRanksOff + 4 * wi);
     const uint32_t below = __popc(w & ((1u << lane) - 1u));
     if ((w >> lane) & 1u) {
         // stage-relative rank, compared unsigned: a rank below the stage's wraps
-        const uint32_t pr = r0 + below - s.r0;
-        if (pr >= s.r1 - s.r0) {
-            raise_flag(err, LQ_EF_BITSTREAM);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) x[i] = 0.f;
-            sc = 1.f;
-            return;
-        }
+        uint32_t pr = r0 + below - s.r0;
+        pr = pr < (s.bad ? 0u : s.r1 - s.r0) ? pr : 0u;
         const int b = B4 ? 4 : c.bits, R = 1 << (b - 1);
         uint32_t u[7], c7u, coset, par;
-        const uint32_t pbyte = pr * (uint32_t)b + (s.r0 * (uint32_t)b - s.a0);  // byte in the staged codes
+        const uint32_t pbyte = s.bad ? 0u : pr * (uint32_t)b + (s.r0 * (uint32_t)b - s.a0);  // byte in the staged codes
         if constexpr (B4) {
             const uint32_t v = __byte_perm(lds_u32(buf + S::kPackedOff + pbyte), 0u, 0x0123u);
             coset = v >> 31;
@@ -511,14 +502,8 @@ __device__ __forceinline__ void cstage_block(const CompactDev &c, const CStageSp
         sc = head_scale;
     } else {
         // fallback rows before this block: the stage's first row is b0 - r0 of the chunk
-        const uint32_t f = 32u * wi + lane - below - (r0 - s.r0);
-        if (f >= 32u * s.nw - (s.r1 - s.r0)) {
-            raise_flag(err, LQ_EF_BITSTREAM);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) x[i] = 0.f;
-            sc = 1.f;
-            return;
-        }
+        uint32_t f = 32u * wi + lane - below - (r0 - s.r0);
+        f = f < (s.bad ? 0u : 32u * s.nw - (s.r1 - s.r0)) ? f : 0u;
         const uint4 h = lds_v4(buf + S::kFallbackOff + 16u * f);
         const uint32_t hw[4] = {h.x, h.y, h.z, h.w};
 #pragma unroll
@@ -604,6 +589,7 @@ __global__ void __launch_bounds__(kCompactThreads, G <= 4 ? 2 : 1) attn_compact_
             const CStageSpan s = sp[st];
             // the stage's index must chain: rank(w+1) - rank(w) = popcount(word w),
             // from the stage's first rank to its last
+            if (s.bad && threadIdx.x == 0) raise_flag(a.err, LQ_EF_BITSTREAM);
             for (uint32_t i = threadIdx.x; i < s.nw && !s.bad; i += blockDim.x) {
                 const uint32_t ri = lds_u32(buf + S::kRanksOff + 4 * i);
                 const uint32_t rn = i + 1 < s.nw ? lds_u32(buf + S::kRanksOff + 4 * (i + 1)) : s.r1;
@@ -611,12 +597,15 @@ __global__ void __launch_bounds__(kCompactThreads, G <= 4 ? 2 : 1) attn_compact_
                     raise_flag(a.err, LQ_EF_BITSTREAM);
             }
             const uint32_t t0 = T0 + st * kCStageTok;
+            // the warp's steps in this stage (sequence lengths are whole steps,
+            // so every token of a step taken is in range)
+            const uint32_t tw = t0 + (uint32_t)(warp * kWarpTok);
+            const int nsteps = tw >= T1 ? 0 : (int)min((uint32_t)kSteps, (T1 - tw) / TPS);
 #pragma unroll 2
-            for (int j = 0; j < kSteps; ++j) {
-                const uint32_t tb = t0 + (uint32_t)(warp * kWarpTok + j * TPS);  // step's first token
-                if (tb >= T1) break;
+            for (int j = 0; j < nsteps; ++j) {
+                const uint32_t tb = tw + (uint32_t)(j * TPS);  // step's first token
                 const uint32_t wi = (uint32_t)(warp * kWarpTok + j * TPS) * BPT / 32u;
-                body(s, buf, wi, tb + tl, tb + tl < T1);
+                body(s, buf, wi, tb + tl, true);
             }
             __syncthreads();
             if (st + 2 < nst) {
