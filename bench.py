@@ -555,7 +555,7 @@ def bench_config5(dev, rank, world, args, barrier):
     g.manual_seed(5006)
     ids = torch.randint(0, cfg.vocab_size, (B, P), generator=g, device=dev)
     hr = SH.head_slice(cfg.num_key_value_heads, world, rank) if world > 1 else None
-    cache = CompressedAttentionKVCache(4, tail_tokens=64, head_range=hr).bind(model)
+    cache = CompressedAttentionKVCache(4, tail_tokens=64, head_range=hr, layout=args.c5_layout).bind(model)
     host = torch.empty(T, B, dtype=torch.int64, pin_memory=True)
     st = torch.cuda.current_stream(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -595,7 +595,8 @@ def bench_config5(dev, rank, world, args, barrier):
             "warmup": W, "ms_per_step": ms / steps, "higher_is_better": True, "scaling": "strong",
             "dtype": "bf16", "data": "synthetic (random-init weights N(0,0.02), seeded random token ids)",
             "config": {"workload": f"config5: Llama-3.1-8B architecture ({L} layers, 4096 hidden, 32 q / 8 kv heads), "
-                                   f"batch {B}, prefill {P} random ids, {T} generated tokens, 4 b/dim KV",
+                                   f"batch {B}, prefill {P} random ids, {T} generated tokens, 4 b/dim KV "
+                                   f"({'rANS lanes' if args.c5_layout == 'rans' else 'compact fixed-rate layout'})",
                        "parallelism": f"KV-head-sharded cache over {world} GPUs (weights replicated, per-layer "
                                       "all-gather of attention heads)" if world > 1 else "single GPU",
                        "global_batch": B, "seq_len": P + T},
@@ -657,6 +658,8 @@ def main():
     ap.add_argument("--c5-batch", type=int, default=32)
     ap.add_argument("--c5-prefill", type=int, default=16384)
     ap.add_argument("--c5-gen", type=int, default=256)
+    ap.add_argument("--c5-layout", default="rans", choices=["rans", "compact"],
+                    help="cache layout of config 5: entropy-coded lanes or the compact fixed-rate layout")
     ap.add_argument("--layers", type=int, default=N_LAYERS,
                     help="layers of the cache (profiling runs use fewer; bench lines use 32)")
     args = ap.parse_args()
