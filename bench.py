@@ -535,6 +535,7 @@ def bench_config5(dev, rank, world, args, barrier):
 
     from latticequant_b200 import sharding as SH
     from latticequant_b200.llm.compressed_attention import CompressedAttentionKVCache
+    from latticequant_b200.llm.graph_decode import GraphedDecodeStep
 
     L, B, P, T, W = args.c5_layers, args.c5_batch, args.c5_prefill, args.c5_gen, args.warmup
     if T <= W:
@@ -568,17 +569,24 @@ def bench_config5(dev, rank, world, args, barrier):
         del out
         torch.cuda.synchronize()
         prefill_s = time.time() - t0
+        stepper = None if args.c5_eager else GraphedDecodeStep(model, cache)
         for i in range(T):
             if i == W:
                 barrier()
                 torch.cuda.synchronize()
                 e0.record(st)
-            out = model(nxt, past_key_values=cache, use_cache=True)
-            nxt = out.logits[:, -1].argmax(-1, keepdim=True)
+            if stepper is not None:
+                nxt = stepper.step(nxt)
+            else:
+                out = model(nxt, past_key_values=cache, use_cache=True)
+                nxt = out.logits[:, -1].argmax(-1, keepdim=True)
+                del out
             host[i].copy_(nxt.view(-1), non_blocking=True)
-            del out
         e1.record(st)
         torch.cuda.synchronize()
+        captures = stepper.captures if stepper is not None else 0
+        if stepper is not None:
+            stepper.release()  # the graph holds collectives when sharded: gone before the process group
     ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
@@ -600,6 +608,8 @@ def bench_config5(dev, rank, world, args, barrier):
                        "parallelism": f"KV-head-sharded cache over {world} GPUs (weights replicated, per-layer "
                                       "all-gather of attention heads)" if world > 1 else "single GPU",
                        "global_batch": B, "seq_len": P + T},
+            "decode": "eager" if args.c5_eager else f"CUDA graph replays ({captures} captures, re-captured "
+                                                     "after each tail flush, inside the timed region)",
             "prefill_s": prefill_s, "compressed_cache_GB_rank0": comp / 1e9,
             "max_memory_GB_rank0": mem / 1e9,
             "e2e": {"value": B * steps * 1e3 / ms, "unit": "tok/s", "h2d_bytes_per_step": B * 8,
@@ -658,6 +668,7 @@ def main():
     ap.add_argument("--c5-batch", type=int, default=32)
     ap.add_argument("--c5-prefill", type=int, default=16384)
     ap.add_argument("--c5-gen", type=int, default=256)
+    ap.add_argument("--c5-eager", action="store_true", help="config 5 decode steps run eagerly (no CUDA graph)")
     ap.add_argument("--c5-layout", default="rans", choices=["rans", "compact"],
                     help="cache layout of config 5: entropy-coded lanes or the compact fixed-rate layout")
     ap.add_argument("--layers", type=int, default=N_LAYERS,

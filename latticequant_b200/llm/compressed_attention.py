@@ -109,6 +109,8 @@ class CompressedAttentionKVCache(CompressedKVCache):
         self.group = group
         self.n_kv_heads_total = None
         self._qcodecs = {}  # decode-step quantisers, one per token shape (buffers reused every step)
+        self._graph_idx: Optional[torch.Tensor] = None  # graph mode: the tail slot of the step, on the device
+        self._tail_ar: Optional[torch.Tensor] = None
 
     # ---- storage -----------------------------------------------------------
     def _layer(self, i: int) -> _LayerState:
@@ -201,11 +203,23 @@ class CompressedAttentionKVCache(CompressedKVCache):
         """A one-token update: quantise now (update()'s output), encode with the tail later."""
         B, H, S, D = k.shape
         T = self.tail_tokens
+        if self._graph_idx is not None:
+            # graph mode: the slot is a device index, the host bookkeeping is
+            # graph_advance()'s (a replayed step runs none of this Python)
+            kvd = self._quantise_only(torch.cat([k, v], 1))
+            idx = self._graph_idx
+            st.tail_raw_k.index_copy_(2, idx, k)
+            st.tail_raw_v.index_copy_(2, idx, v)
+            st.tail_deq_k.index_copy_(2, idx, kvd[:, :H].contiguous())
+            st.tail_deq_v.index_copy_(2, idx, kvd[:, H:].contiguous())
+            return kvd[:, :H], kvd[:, H:]
         if st.tail_raw_k is None or st.tail_raw_k.shape[:2] != (B, H):
-            st.tail_raw_k = torch.empty(B, H, T, D, dtype=k.dtype, device=k.device)
-            st.tail_raw_v = torch.empty_like(st.tail_raw_k)
-            st.tail_deq_k = torch.empty_like(st.tail_raw_k)
-            st.tail_deq_v = torch.empty_like(st.tail_raw_k)
+            # zeroed: a graph-mode step attends over every slot, and its mask
+            # gives the unwritten ones weight 0, which must not meet a NaN
+            st.tail_raw_k = torch.zeros(B, H, T, D, dtype=k.dtype, device=k.device)
+            st.tail_raw_v = torch.zeros_like(st.tail_raw_k)
+            st.tail_deq_k = torch.zeros_like(st.tail_raw_k)
+            st.tail_deq_v = torch.zeros_like(st.tail_raw_k)
         # K and V of the token in one call: each (batch, head) row has its own
         # scale, so stacking them along the heads changes no value
         kvd = self._quantise_only(torch.cat([k, v], 1))
@@ -295,7 +309,11 @@ class CompressedAttentionKVCache(CompressedKVCache):
             o_parts.append(o)
             l_parts.append(lse)
         dense_k, dense_v = list(st.dense_k), list(st.dense_v)
-        if st.n_tail:
+        graph = self._graph_idx is not None
+        if graph:  # the whole tail, its slots past the step's masked below
+            dense_k.append(st.tail_deq_k)
+            dense_v.append(st.tail_deq_v)
+        elif st.n_tail:
             dense_k.append(st.tail_deq_k[:, :, :st.n_tail])
             dense_v.append(st.tail_deq_v[:, :, :st.n_tail])
         if dense_k:
@@ -304,6 +322,9 @@ class CompressedAttentionKVCache(CompressedKVCache):
             H = k.shape[1]
             qg = q3.float().view(B, H, Hq // H, D)
             s = torch.einsum("bhgd,bhsd->bhgs", qg, k) * scaling
+            if graph:
+                T = st.tail_deq_k.shape[2]
+                s[..., -T:] = s[..., -T:].masked_fill(self._tail_ar > self._graph_idx, float("-inf"))
             lse = torch.logsumexp(s, -1)
             o = torch.einsum("bhgs,bhsd->bhgd", torch.exp(s - lse[..., None]), v)
             o_parts.append(o.reshape(B, Hq, D))
@@ -313,6 +334,42 @@ class CompressedAttentionKVCache(CompressedKVCache):
         else:
             out, _ = A.merge_attention(o_parts, l_parts, out_dtype=query.dtype)
         return out.view(B, Hq, 1, D)
+
+    # ---- CUDA-graph decode steps (llm.graph_decode) --------------------------
+    def enter_graph(self, idx: torch.Tensor):
+        """Decode-step updates write the token into tail slot `idx` (a (1,)
+        int64 device tensor the captured step advances) and attend over the
+        whole tail with a mask past that slot, with no host bookkeeping, so a
+        step can be captured in a CUDA graph and replayed; graph_advance() is
+        the bookkeeping of each replay.  Needs the tail buffers (one eager
+        decode step) and a tail that is not full."""
+        for st in self._state:
+            if st.tail_raw_k is None:
+                raise RuntimeError("graph mode needs one eager decode step first")
+            if st.n_tail >= self.tail_tokens:
+                raise RuntimeError("flush the full tails before entering graph mode")
+        self._graph_idx = idx
+        self._tail_ar = torch.arange(self.tail_tokens, device=idx.device)
+
+    def exit_graph(self):
+        self._graph_idx = None
+
+    def graph_advance(self, n: int = 1):
+        """Host bookkeeping of n replayed decode steps."""
+        for st in self._state:
+            B, H, _, D = st.tail_raw_k.shape
+            st.n_tail += n
+            st.seq += n
+            self.total_vectors += n * 2 * B * H * D // 8
+
+    def tail_full(self) -> bool:
+        return any(st.n_tail >= self.tail_tokens for st in self._state)
+
+    def flush_tails(self):
+        """Encode every full tail (what an eager update does at the 64th token)."""
+        for li, st in enumerate(self._state):
+            if st.n_tail >= self.tail_tokens:
+                self._flush_tail(st, li)
 
     def flags(self) -> int:
         """OR of the fused attention kernels' error words (synchronises)."""
