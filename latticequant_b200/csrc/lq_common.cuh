@@ -83,6 +83,50 @@ __device__ inline void load_block8(const void *x, int64_t blk, float v[8]) {
     }
 }
 
+// The raw bytes of one block (16-bit types use `a` only), split from the
+// conversion so that a loop can issue the next block's load before it works
+// on the current one.
+struct RawBlock8 {
+    uint4 a, b;
+};
+
+template <int DT>
+__device__ __forceinline__ RawBlock8 load_raw8(const void *x, int64_t blk) {
+    RawBlock8 r;
+    if constexpr (DT == LQ_F32) {
+        const uint4 *p = reinterpret_cast<const uint4 *>(x) + 2 * blk;
+        r.a = __ldg(p);
+        r.b = __ldg(p + 1);
+    } else {
+        r.a = __ldg(reinterpret_cast<const uint4 *>(x) + blk);
+        r.b = make_uint4(0, 0, 0, 0);
+    }
+    return r;
+}
+
+template <int DT>
+__device__ __forceinline__ void raw8_to_float(const RawBlock8 &r, float v[8]) {
+    if constexpr (DT == LQ_F32) {
+        v[0] = __uint_as_float(r.a.x); v[1] = __uint_as_float(r.a.y);
+        v[2] = __uint_as_float(r.a.z); v[3] = __uint_as_float(r.a.w);
+        v[4] = __uint_as_float(r.b.x); v[5] = __uint_as_float(r.b.y);
+        v[6] = __uint_as_float(r.b.z); v[7] = __uint_as_float(r.b.w);
+    } else {
+        const uint32_t w[4] = {r.a.x, r.a.y, r.a.z, r.a.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint16_t lo = (uint16_t)(w[i] & 0xffffu), hi = (uint16_t)(w[i] >> 16);
+            if constexpr (DT == LQ_F16) {
+                v[2 * i] = __half2float(__ushort_as_half(lo));
+                v[2 * i + 1] = __half2float(__ushort_as_half(hi));
+            } else {
+                v[2 * i] = __bfloat162float(__ushort_as_bfloat16(lo));
+                v[2 * i + 1] = __bfloat162float(__ushort_as_bfloat16(hi));
+            }
+        }
+    }
+}
+
 template <int DT>
 __device__ inline void store_block8(void *y, int64_t blk, const float v[8]) {
     if constexpr (DT == LQ_F32) {
@@ -152,21 +196,33 @@ __device__ __forceinline__ float div_by_scale(float a, float b, float y, bool b_
 // The eight quotients of a block.  The FMA path is exact when every nonzero
 // |v| of the block lies in [2^-40, 2^40] (a NaN passes through it as NaN);
 // otherwise each value takes div_by_scale.  One range test per block keeps
-// the common case free of per-value branches.
+// the common case free of per-value branches.  The select on v == 0 only
+// keeps the sign of a zero quotient (a zero input gives r == +0, and
+// fma(+0, y, -0) is +0); callers that use the quotient only through the E8
+// search, where -0 and +0 give the same lattice point and symbols, pass
+// SIGNED_ZERO = false and skip it.
+template <bool SIGNED_ZERO = true>
 __device__ __forceinline__ void div_block_by_scale(const float v[8], float b, float y, bool b_ok, float xs[8]) {
-    float amax = 0.0f, amin = INFINITY;
+    // |v| <= 2^40 as a float maximum; 0 < |v| < 2^-40 as an unsigned test
+    // on the bits with the sign shifted out: 2*bits - 2 wraps a zero to the
+    // top of the range, and a nonzero |v| lands below 2*bits(2^-40) - 2
+    // exactly when it is smaller than 2^-40
+    float amax = 0.0f;
+    uint32_t tmin = 0xffffffffu;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        const float a = fabsf(v[i]);
-        amax = fmaxf(amax, a);
-        amin = fminf(amin, a == 0.0f ? INFINITY : a);
+        amax = fmaxf(amax, fabsf(v[i]));
+        tmin = min(tmin, __float_as_uint(v[i]) * 2u - 2u);
     }
-    if (b_ok && amax <= 1.0995116e12f && amin >= 9.094947e-13f) {
+    if (b_ok && amax <= 1.0995116e12f && tmin >= 0x56fffffeu) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const float q0 = __fmul_rn(v[i], y);
             const float r = __fmaf_rn(-b, q0, v[i]);
-            xs[i] = v[i] == 0.0f ? q0 : __fmaf_rn(r, y, q0);  // r == 0 gives q0 as well
+            if constexpr (SIGNED_ZERO)
+                xs[i] = v[i] == 0.0f ? q0 : __fmaf_rn(r, y, q0);  // r == 0 gives q0 as well
+            else
+                xs[i] = __fmaf_rn(r, y, q0);
         }
     } else {
 #pragma unroll
@@ -209,6 +265,11 @@ __device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsig
     asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
     return r;
 }
+__device__ __forceinline__ unsigned long long f2_sub(unsigned long long a, unsigned long long b) {
+    unsigned long long r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
 __device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsigned long long b) {
     unsigned long long r;
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
@@ -222,17 +283,7 @@ __device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsig
 // levels of outcomes select the flipped coordinate.  The flip adds
 // sign(res) with sign(0) = +1, i.e. copysign(1, res) (res is never -0:
 // x - rint(x) of equal values is +0).
-__device__ __forceinline__ void d8_nearest(const float x[8], float r[8], float res[8]) {
-    float c[8];
-    float s = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        r[i] = rintf(x[i]);
-        s = __fadd_rn(s, r[i]);
-        res[i] = __fsub_rn(x[i], r[i]);
-        c[i] = __fmaf_rn(-2.0f, fabsf(res[i]), 1.0f);
-        if (i) c[i] = __fadd_rn(c[i], e8_tie(i));
-    }
+__device__ __forceinline__ void d8_flip(float s, const float c[8], const float res[8], float r[8]) {
     // parity = s % 2 != 0; s is integer valued, and even once |s| >= 2^24
     const bool odd = (fabsf(s) < 16777216.0f) && (((int)s) & 1);
     const bool w01 = c[1] < c[0], w23 = c[3] < c[2], w45 = c[5] < c[4], w67 = c[7] < c[6];
@@ -250,14 +301,56 @@ __device__ __forceinline__ void d8_nearest(const float x[8], float r[8], float r
     }
 }
 
+__device__ __forceinline__ void d8_nearest(const float x[8], float r[8], float res[8]) {
+    float c[8];
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        r[i] = rintf(x[i]);
+        s = __fadd_rn(s, r[i]);
+        res[i] = __fsub_rn(x[i], r[i]);
+        c[i] = __fmaf_rn(-2.0f, fabsf(res[i]), 1.0f);
+        if (i) c[i] = __fadd_rn(c[i], e8_tie(i));
+    }
+    d8_flip(s, c, res, r);
+}
+
+// The two D8 searches of the E8 decoder, of x and of y = x - 1/2, in one
+// pass: the coordinate sums and the residuals of both run as the two halves
+// of packed fp32x2 adds, each half rounded as its scalar op.  The sum starts
+// at r[0] instead of 0 + r[0], which differs only in the sign of a zero sum
+// and leaves the parity unchanged.
+__device__ __forceinline__ void d8_nearest_pair(const float x[8], const float y[8], float r1[8], float r2[8],
+                                                float res1[8], float res2[8]) {
+    float c1[8], c2[8];
+    unsigned long long s = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        r1[i] = rintf(x[i]);
+        r2[i] = rintf(y[i]);
+        const unsigned long long rr = f2_pack(r1[i], r2[i]);
+        s = i ? f2_add(s, rr) : rr;
+        f2_unpack(f2_sub(f2_pack(x[i], y[i]), rr), res1[i], res2[i]);
+        c1[i] = __fmaf_rn(-2.0f, fabsf(res1[i]), 1.0f);
+        c2[i] = __fmaf_rn(-2.0f, fabsf(res2[i]), 1.0f);
+        if (i) {
+            c1[i] = __fadd_rn(c1[i], e8_tie(i));
+            c2[i] = __fadd_rn(c2[i], e8_tie(i));
+        }
+    }
+    float s1, s2;
+    f2_unpack(s, s1, s2);
+    d8_flip(s1, c1, res1, r1);
+    d8_flip(s2, c2, res2, r2);
+}
+
 // E8 nearest point (core/e8_quantizer.py:61-83).  The two squared-distance
 // sums run left to right as the two halves of packed fp32x2 operations.
 __device__ __forceinline__ void e8_nearest(const float x[8], float q[8]) {
-    float c1[8], y[8], c2[8], res[8];
-    d8_nearest(x, c1, res);
+    float c1[8], y[8], c2[8], res1[8], res2[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) y[i] = __fsub_rn(x[i], 0.5f);
-    d8_nearest(y, c2, res);
+    d8_nearest_pair(x, y, c1, c2, res1, res2);
     unsigned long long d = 0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -281,11 +374,10 @@ __device__ __forceinline__ void e8_nearest(const float x[8], float q[8]) {
 // non-finite input).  q is written only when WANT_Q.
 template <bool WANT_Q>
 __device__ __forceinline__ int e8_nearest_symbols(const float x[8], float q[8], int sym[8], bool *finite) {
-    float c1[8], y[8], c2[8], res[8];
-    d8_nearest(x, c1, res);
+    float c1[8], y[8], c2[8], res1[8], res2[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) y[i] = __fsub_rn(x[i], 0.5f);
-    d8_nearest(y, c2, res);
+    d8_nearest_pair(x, y, c1, c2, res1, res2);
     unsigned long long d = 0;
     float h[8];
 #pragma unroll

@@ -43,8 +43,10 @@ struct OutlierArgs {
     uint32_t cap;
 };
 
-template <int DT, int DQ, bool QO>
-__global__ void __launch_bounds__(32 * kQWarps, 4) quantize_kernel(
+// TBC: the tile size as a compile-time constant (0 = take TB), so that the
+// eight column stores of a block address with immediate offsets.
+template <int DT, int DQ, bool QO, uint32_t TBC>
+__global__ void __launch_bounds__(32 * kQWarps, 3) quantize_kernel(
     const void *__restrict__ x, uint32_t n_heads, uint32_t bph, FastDiv bph_div, const float *__restrict__ scale_f32,
     uint32_t TB, uint32_t n_tiles, int16_t *__restrict__ sym_rows, uint32_t *__restrict__ coset_words,
     uint32_t *__restrict__ tile_n0, uint32_t *__restrict__ hist, void *__restrict__ deq, float *__restrict__ q_out,
@@ -60,6 +62,7 @@ __global__ void __launch_bounds__(32 * kQWarps, 4) quantize_kernel(
     __syncthreads();
     const uint32_t hist_base = static_cast<uint32_t>(__cvta_generic_to_shared(sh_hist));
 
+    if constexpr (TBC != 0) TB = TBC;
     const uint32_t tile = blockIdx.x * kQWarps + warp;
     uint32_t flags = 0;
     if (tile < n_tiles) {
@@ -76,8 +79,13 @@ __global__ void __launch_bounds__(32 * kQWarps, 4) quantize_kernel(
         float sc = 1.0f, rcp = 1.0f;
         bool fast = false;
         uint32_t n0 = 0, n1 = 0;  // running coset counts
+        // one block in flight ahead of the one being searched
+        RawBlock8 cur = {};
+        if (lane < tb) cur = load_raw8<DT>(x, cblk0 + b0 + lane);
         for (uint32_t off = 0; off < tb; off += 32) {
             const bool active = (off + lane) < tb;
+            RawBlock8 nxt = {};
+            if (off + 32 + lane < tb) nxt = load_raw8<DT>(x, cblk0 + b0 + off + 32 + lane);
             int sym[8] = {0, 0, 0, 0, 0, 0, 0, 0};
             int coset = 0;
             if (active) {
@@ -89,8 +97,8 @@ __global__ void __launch_bounds__(32 * kQWarps, 4) quantize_kernel(
                 }
                 const int64_t blk = cblk0 + b0 + off + lane;
                 float v[8], xs[8], q[8];
-                load_block8<DT>(x, blk, v);
-                div_block_by_scale(v, sc, rcp, fast, xs);
+                raw8_to_float<DT>(cur, v);
+                div_block_by_scale<(DQ >= 0) || QO>(v, sc, rcp, fast, xs);
                 bool finite;
                 coset = e8_nearest_symbols<(DQ >= 0) || QO>(xs, q, sym, &finite);
                 if (!finite) flags |= LQ_EF_NONFINITE;
@@ -144,23 +152,33 @@ __global__ void __launch_bounds__(32 * kQWarps, 4) quantize_kernel(
 #pragma unroll
                 for (int i = 0; i < 8; ++i) cols[i * TB + row] = (int16_t)sym[i];
                 const uint32_t sh = hist_base + (uint32_t)coset * (8 * kSmemBins * 4);
+                // one test for the whole block: every (sym + half) below kSmemBins as unsigned
+                uint32_t wide = 0;
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int v = sym[i];
-                    if ((uint32_t)(v + kSmemHalf) < (uint32_t)kSmemBins) {
-                        red_shared_add1(sh + (uint32_t)(i * kSmemBins + v + kSmemHalf) * 4u);
-                    } else if ((uint32_t)(v + LQ_SYM_LIMIT) < (uint32_t)(2 * LQ_SYM_LIMIT)) {
-                        uint32_t *gh = hist + ((int64_t)chunk * LQ_NSTREAMS + coset * 8 + i) * LQ_HIST_BINS;
-                        atomicAdd(&gh[v + LQ_SYM_LIMIT], 1u);
-                    } else {
-                        // outside the histogram window (float->int saturates, so huge values land here)
-                        flags |= LQ_EF_SYMRANGE;
+                for (int i = 0; i < 8; ++i) wide |= (uint32_t)(sym[i] + kSmemHalf);
+                if (wide < (uint32_t)kSmemBins) {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) red_shared_add1(sh + (uint32_t)(i * kSmemBins + sym[i] + kSmemHalf) * 4u);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int v = sym[i];
+                        if ((uint32_t)(v + kSmemHalf) < (uint32_t)kSmemBins) {
+                            red_shared_add1(sh + (uint32_t)(i * kSmemBins + v + kSmemHalf) * 4u);
+                        } else if ((uint32_t)(v + LQ_SYM_LIMIT) < (uint32_t)(2 * LQ_SYM_LIMIT)) {
+                            uint32_t *gh = hist + ((int64_t)chunk * LQ_NSTREAMS + coset * 8 + i) * LQ_HIST_BINS;
+                            atomicAdd(&gh[v + LQ_SYM_LIMIT], 1u);
+                        } else {
+                            // outside the histogram window (float->int saturates, so huge values land here)
+                            flags |= LQ_EF_SYMRANGE;
+                        }
                     }
                 }
             }
             const uint32_t c1 = __popc(ball);
             n1 += c1;
             n0 += __popc(act) - c1;
+            cur = nxt;
             rem += 32;
             while (rem >= bph) {
                 rem -= bph;
@@ -188,9 +206,17 @@ int launch_quantize(const void *x, int64_t n_chunks, int64_t n_heads, int64_t bp
     const int64_t N = n_heads * bph;
     const int64_t n_tiles = ceil_div(N, TB);
     dim3 grid((unsigned)ceil_div(n_tiles, kQWarps), (unsigned)n_chunks);
-    quantize_kernel<DT, DQ, QO><<<grid, 32 * kQWarps, 0, st>>>(x, (uint32_t)n_heads, (uint32_t)bph, FastDiv((uint32_t)bph),
-                                                            scale_f32, (uint32_t)TB, (uint32_t)n_tiles, sym_rows,
-                                                            coset_words, tile_n0, hist, deq, q_out, oa, err);
+    if constexpr (DQ < 0 && !QO) {
+        if (TB == 1024) {
+            quantize_kernel<DT, DQ, QO, 1024><<<grid, 32 * kQWarps, 0, st>>>(
+                x, (uint32_t)n_heads, (uint32_t)bph, FastDiv((uint32_t)bph), scale_f32, (uint32_t)TB,
+                (uint32_t)n_tiles, sym_rows, coset_words, tile_n0, hist, deq, q_out, oa, err);
+            return check_launch();
+        }
+    }
+    quantize_kernel<DT, DQ, QO, 0><<<grid, 32 * kQWarps, 0, st>>>(x, (uint32_t)n_heads, (uint32_t)bph, FastDiv((uint32_t)bph),
+                                                               scale_f32, (uint32_t)TB, (uint32_t)n_tiles, sym_rows,
+                                                               coset_words, tile_n0, hist, deq, q_out, oa, err);
     return check_launch();
 }
 
