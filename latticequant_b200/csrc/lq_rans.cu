@@ -83,11 +83,11 @@ __global__ void __launch_bounds__(16 * kEncTiles, 2) encode_lanes_kernel(
         }
         const uint32_t tab = smem_addr(etab) + s * (LQ_L * 4);
         const int16_t *col = sym_lanes + ((size_t)chunk * n_tiles + tile) * TB * 8 + (size_t)idx * TB;
-        uint32_t acc = 0, cnt = 0, bad = 0;
+        uint32_t acc = 0, cnt = 0, simax = 0;  // simax: largest alphabet index seen (unsigned)
         uint32_t *const out_end = out;
         auto code = [&](int v) {
             const uint32_t si = (uint32_t)(v - lo);
-            bad |= si >= (uint32_t)nsym ? 1u : 0u;
+            simax = max(simax, si);
             const uint32_t e = lds_u32(tab + ((si & (LQ_L - 1)) << 2));
             const uint32_t twof = e & 0xfffu, k0 = (e >> 12) & 0xfu;
             const uint32_t k = k0 + ((x >> k0) >= twof ? 1u : 0u);
@@ -126,7 +126,7 @@ __global__ void __launch_bounds__(16 * kEncTiles, 2) encode_lanes_kernel(
             }
         }
         for (; j < n; ++j) code(sym_at(j));
-        if (bad) raise_flag(err, LQ_EF_SYMRANGE);
+        if (simax >= (uint32_t)nsym) raise_flag(err, LQ_EF_SYMRANGE);
         nbits = 32u * (uint32_t)(out_end - out) + cnt;
         if (cnt) *--out = acc;
     }
