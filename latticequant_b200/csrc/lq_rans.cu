@@ -211,23 +211,61 @@ __global__ void __launch_bounds__(kScanT) scan_write_kernel(const uint32_t *__re
 }
 
 // ---------------------------------------------------------------- compaction
+// Output word i of a lane is the bit-reversed funnel of slot words i (high)
+// and i + 1 (low) by the lane's pad.  A warp takes kCompactLanes
+// consecutive lanes and covers 64 words of each per round: every thread
+// loads words i and i + 32 of every lane (thread 31 also word i + 64), all
+// before the first store, so that a warp keeps several lanes' loads in
+// flight; the low neighbours come by shuffle.  The word count follows from
+// the bit count (the encoder stores both); threads 0..kCompactLanes-1 load
+// the lanes' metadata at once.
+constexpr int kCompactLanes = 4;
+
 __global__ void __launch_bounds__(256) compact_lanes_kernel(const uint32_t *__restrict__ scratch, int64_t slot_words,
                                                              int64_t n_lanes, const uint32_t *__restrict__ lane_off,
                                                              const uint32_t *__restrict__ lane_nbits,
-                                                             const uint32_t *__restrict__ lane_nwords,
                                                              uint32_t *__restrict__ words, int64_t cap) {
     const int lane = threadIdx.x & 31;
-    const int64_t lg = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (lg >= n_lanes) return;
-    const int64_t nw = lane_nwords[lg];
-    const int64_t dst0 = lane_off[lg];
-    if (dst0 + nw > cap) return;  // capacity error already flagged by the scan
-    const uint32_t pad = (32u - (lane_nbits[lg] & 31u)) & 31u;
-    const uint32_t *src = scratch + lg * slot_words + (slot_words - nw);
-    for (int64_t i = lane; i < nw; i += 32) {
-        const uint32_t hi = src[i];
-        const uint32_t lo = (i + 1 < nw) ? src[i + 1] : 0u;
-        words[dst0 + i] = __brev(__funnelshift_l(lo, hi, pad));
+    const int64_t lg0 = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * kCompactLanes;
+    if (lg0 >= n_lanes) return;  // warp-uniform
+    uint32_t my_nb = 0, my_off = 0;
+    if (lane < kCompactLanes && lg0 + lane < n_lanes) {
+        my_nb = __ldg(lane_nbits + lg0 + lane);
+        my_off = __ldg(lane_off + lg0 + lane);
+    }
+    int64_t nw[kCompactLanes], dst0[kCompactLanes];
+    uint32_t pad[kCompactLanes];
+    int64_t nw_max = 0;
+#pragma unroll
+    for (int k = 0; k < kCompactLanes; ++k) {
+        const uint32_t nb = __shfl_sync(0xffffffffu, my_nb, k);
+        dst0[k] = __shfl_sync(0xffffffffu, my_off, k);
+        nw[k] = (int64_t)((nb + 31u) >> 5);
+        if (dst0[k] + nw[k] > cap) nw[k] = 0;  // capacity error already flagged by the scan
+        pad[k] = (32u - (nb & 31u)) & 31u;
+        nw_max = max(nw_max, nw[k]);
+    }
+    for (int64_t i0 = 0; i0 < nw_max; i0 += 64) {
+        const int64_t i = i0 + lane, i2 = i + 32;
+        uint32_t a[kCompactLanes], b[kCompactLanes], t[kCompactLanes];
+#pragma unroll
+        for (int k = 0; k < kCompactLanes; ++k) {
+            const uint32_t *src = scratch + (lg0 + k) * slot_words + (slot_words - nw[k]);
+            a[k] = i < nw[k] ? __ldg(src + i) : 0u;
+            b[k] = i2 < nw[k] ? __ldg(src + i2) : 0u;
+            t[k] = (lane == 31 && i0 + 64 < nw[k]) ? __ldg(src + i0 + 64) : 0u;
+        }
+#pragma unroll
+        for (int k = 0; k < kCompactLanes; ++k) {
+            const uint32_t a_next = __shfl_down_sync(0xffffffffu, a[k], 1);
+            const uint32_t b_first = __shfl_sync(0xffffffffu, b[k], 0);
+            const uint32_t b_next = __shfl_down_sync(0xffffffffu, b[k], 1);
+            const uint32_t lo_a = lane == 31 ? b_first : a_next;  // word i + 1 (0 past the end)
+            const uint32_t lo_b = lane == 31 ? t[k] : b_next;     // word i + 33
+            uint32_t *dst = words + dst0[k];
+            if (i < nw[k]) dst[i] = __brev(__funnelshift_l(lo_a, a[k], pad[k]));
+            if (i2 < nw[k]) dst[i2] = __brev(__funnelshift_l(lo_b, b[k], pad[k]));
+        }
     }
 }
 
@@ -557,8 +595,8 @@ extern "C" int lq_rans_encode(const int16_t *sym_rows, const uint32_t *tile_n0, 
     scan_reduce_kernel<<<(unsigned)nblk, kScanT, 0, st>>>(nwords, n_lanes, bsum);
     scan_blocks_kernel<<<1, kScanT, 0, st>>>(bsum, nblk);
     scan_write_kernel<<<(unsigned)nblk, kScanT, 0, st>>>(nwords, n_lanes, bsum, lane_off, words_cap, err);
-    compact_lanes_kernel<<<(unsigned)ceil_div(n_lanes, 8), 256, 0, st>>>(scratch, sw, n_lanes, lane_off, lane_nbits,
-                                                                          nwords, words, words_cap);
+    compact_lanes_kernel<<<(unsigned)ceil_div(n_lanes, 8 * kCompactLanes), 256, 0, st>>>(
+        scratch, sw, n_lanes, lane_off, lane_nbits, words, words_cap);
     return check_launch();
 }
 
