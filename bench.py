@@ -29,6 +29,18 @@ sharded by (layer, KV head) units over the ranks with no collective.  The
 line reports how many tokens went to the outlier side channel (chunks whose
 alphabet would exceed L = 1024 symbols).
 
+"config1" carries BASELINE config 1: 262,144 vectors of dim 128, fp32
+N(0,1) with a log-normal(0, 0.5) magnitude per vector, one fp16 scale per
+vector (the reference's _compress_tensor of the (1, 262144, 1, 128) view,
+llm/compressed_kv_cache.py:176-196), 4 bits/dim: encode + decode Gvec/s,
+reconstructed MSE and bitstream bytes, beside the C oracle's values for the
+same seeded input (rank 0 at N = 1).
+
+"config5" carries BASELINE config 5: a random-init Llama-3.1-8B-architecture
+model decoding through CompressedAttentionKVCache (batch 32, prefill 16,384
+random ids, 256 generated tokens, 4 bits/dim, KV-head-sharded at N > 1):
+decode tokens/s, the fused attention's share of a step and its roofline.
+
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 """
 import argparse
@@ -132,8 +144,10 @@ def measured_peaks():
         return 6650.0, "fallback"
 
 
-def cpu_baseline(n_threads, sample_chunks=2, reps=1):
-    """The C oracle port (oracle/lq_oracle_codec.c) on a bounded sample of the workload."""
+def cpu_baseline(n_threads, sample_chunks=2, reps=1, min_seconds=0.0):
+    """The C oracle port (oracle/lq_oracle_codec.c) on a bounded sample of the
+    workload: `sample_chunks` config-2 chunks coded and decoded `reps` times,
+    or more often until `min_seconds` have passed."""
     import numpy as np
 
     import oracle.lq_oracle as O
@@ -152,10 +166,12 @@ def cpu_baseline(n_threads, sample_chunks=2, reps=1):
     u = x.view(np.uint32)
     xb = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
     t0 = time.perf_counter()
-    for _ in range(reps):
+    done = 0
+    while done < reps or (time.perf_counter() - t0 < min_seconds and done < 64):
         O.codec_roundtrip_batch(xb, O.DT_BF16, sample_chunks, N_KV, BPH, BITS, TILE, O.DT_BF16, n_threads)
+        done += 1
     dt = time.perf_counter() - t0
-    blocks = reps * sample_chunks * N_KV * BPH
+    blocks = done * sample_chunks * N_KV * BPH
     return blocks / dt / 1e9, blocks, dt
 
 
@@ -222,19 +238,21 @@ def bench_attention(dev, rank, world, steps, warmup, barrier):
     del k, v
     op = A.DecodeAttention(kc, vc, A_G)
     rows = A_B * A_HKV * A_G
-    o_loc = torch.empty(rows, A_D, dtype=torch.float32 if world > 1 else torch.bfloat16, device=dev)
-    l_loc = torch.empty(rows, dtype=torch.float32, device=dev)
+    # at N > 1 the kernel writes (o, lse) straight into one packed fp32 buffer,
+    # all-gathered in one collective and merged from the packed layout
+    packed = torch.empty(rows * A_D + rows, dtype=torch.float32, device=dev)
+    o_loc = packed[:rows * A_D].view(rows, A_D) if world > 1 else \
+        torch.empty(rows, A_D, dtype=torch.bfloat16, device=dev)
+    l_loc = packed[rows * A_D:]
     out = torch.empty(rows, A_D, dtype=torch.bfloat16, device=dev)
     l_out = torch.empty(rows, dtype=torch.float32, device=dev)
-    o_all = torch.empty(world, rows, A_D, dtype=torch.float32, device=dev)
-    l_all = torch.empty(world, rows, dtype=torch.float32, device=dev)
+    gathered = torch.empty(world, rows * A_D + rows, dtype=torch.float32, device=dev)
 
     def step():
         op(q, o_loc, l_loc if world > 1 else None)
         if world > 1:
-            dist.all_gather_into_tensor(o_all, o_loc)
-            dist.all_gather_into_tensor(l_all, l_loc)
-            A.merge_attention(o_all, l_all, out=out, lse=l_out)
+            dist.all_gather_into_tensor(gathered, packed)
+            A.merge_attention_packed(gathered, rows, A_D, out=out, lse=l_out)
 
     for _ in range(max(warmup, 3)):
         step()
@@ -311,7 +329,8 @@ def bench_attention(dev, rank, world, steps, warmup, barrier):
             "compressed_GBps": tot_comp / (ms * 1e-3) / 1e9,
             "decode_steps_per_s": 1e3 / ms, "tokens_per_s": A_B * 1e3 / ms,
             "config": {"workload": "config3: B16 x 32 q-heads / 8 kv-heads x D128, ctx 32768, 4 b/dim, one decode "
-                                   "step", "parallelism": f"sequence-sharded over {world} (all-gather + LSE merge)"
+                                   "step", "parallelism": f"sequence-sharded over {world} (one all-gather of the "
+                                                          "packed (o, lse) + LSE merge)"
                                    if world > 1 else "single GPU", "tile_blocks": TILE,
                        "bits_per_dim": tot_comp * 8 / (2 * A_B * A_HKV * A_S * A_D),
                        "l2": "compressed K+V larger than L2"},
@@ -344,6 +363,16 @@ def c4_tensor(dev, seed, heads, student):
         chi = sum(torch.randn(shape, generator=g, device=dev) ** 2 for _ in range(3))
         z = z / torch.sqrt(chi / 3)
     return z.to(torch.bfloat16)
+
+
+def compact_chunk_bytes(chunk):
+    """Bytes the compact-layout attention kernel must read for one chunk:
+    codes, fp16 fallback rows, mask words, word ranks and head scales."""
+    from latticequant_b200 import attention as A
+
+    words, rank_t = A.compact_index(chunk)
+    return (chunk.packed.numel() + 2 * chunk.fallback.numel() + 4 * (words.numel() + rank_t.numel()) +
+            4 * chunk.scales.numel())
 
 
 def bench_attention_compact(dev, rank, world, steps, warmup, barrier):
@@ -429,8 +458,10 @@ def bench_attention_compact(dev, rank, world, steps, warmup, barrier):
 
 
 def bench_config4(dev, rank, world, steps, barrier):
-    """Config 4 on `world` ranks: (layer, KV head) units round-robin, encode of
-    every owned unit, then decode-attention steps over every owned layer."""
+    """Config 4 on `world` ranks: (layer, KV head) units round-robin; the
+    rank's K (and V) chunks of each bit rate are coded as ONE batch by one
+    Codec, with no host synchronisation inside the timed encode; then decode-
+    attention steps over every owned layer."""
     import torch
     import torch.distributed as dist
 
@@ -443,27 +474,64 @@ def bench_config4(dev, rank, world, steps, barrier):
     layers = {}
     for l, h in units:
         layers.setdefault(l, []).append(h)
+    heads_per_layer = {len(hs) for hs in layers.values()}
+    if len(heads_per_layer) != 1:
+        raise RuntimeError("config 4: ranks must own the same number of heads in every owned layer")
+    hr = heads_per_layer.pop()
+    shape = (C4_B, hr, C4_S, C4_D)
+    bph = C4_S * C4_D // 8
     st = torch.cuda.current_stream(dev)
-    chunks, blocks, comp, meta, n_out = [], 0, 0, 0, 0
-    enc_ms = 0.0
-    for l, heads in sorted(layers.items()):
-        # the owned heads of this layer, generated per (layer, head) so shards do not depend on N
-        k = torch.cat([c4_tensor(dev, 5000 + 16 * l + h, 1, True) for h in heads], 1)
-        v = torch.cat([c4_tensor(dev, 9000 + 16 * l + h, 1, False) for h in heads], 1)
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(st)
-        kc, _ = C.compress(k, bits[l], tile_blocks=TILE)
-        vc, _ = C.compress(v, bits[l], tile_blocks=TILE)
-        e1.record(st)
-        torch.cuda.synchronize()
-        enc_ms += e0.elapsed_time(e1)
-        blocks += 2 * k.numel() // 8
-        comp += kc.compressed_bytes() + vc.compressed_bytes()
-        meta += kc.metadata_bytes() + vc.metadata_bytes()
-        n_out += kc.n_outliers + vc.n_outliers
-        chunks.append((l, len(heads), A.DecodeAttention(kc, vc, C4_G)))
-        del k, v
+    bpt = C.blocks_per_token(C4_D, TILE, bph)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    enc_ms, blocks, comp, meta, n_out = 0.0, 0, 0, 0, 0
+    per_layer = {}
+    # groups of equal bit rate and kind (K: Student-t, V: Gaussian), one after
+    # another so only one group's input and buffers are resident; each group's
+    # encode is timed on its own (no host synchronisation inside) and the
+    # times are summed
+    for b in sorted(set(bits[l] for l in layers)):
+        ls = [l for l in sorted(layers) if bits[l] == b]
+        for kind, student, base in (("K", True, 5000), ("V", False, 9000)):
+            x = torch.empty((len(ls),) + shape, dtype=torch.bfloat16, device=dev)
+            for i, l in enumerate(ls):
+                x[i] = torch.cat([c4_tensor(dev, base + 16 * l + h, 1, student) for h in layers[l]], 1)
+            cd = C.Codec(C.Geometry(len(ls), C4_B * hr, bph, TILE), dev)
+            # does the group need the outlier side channel (alphabet over L)?
+            # decided by an untimed pass, as codec.compress decides it per chunk
+            cd.scales(x, b)
+            cd.quantize(x)
+            cd.build_tables()
+            outliers = bool(cd.read_err() & (C._lib.EF_ALPHABET | C._lib.EF_SYMRANGE | C._lib.EF_NOCONVERGE))
+
+            def encode():
+                cd.scales(x, b)
+                if outliers:
+                    cd.quantize_outliers(x, None, bpt)
+                else:
+                    cd.quantize(x)
+                cd.build_tables()
+                cd.expand_tables(enc=True, dec=False)
+                cd.entropy_encode()
+
+            encode()  # warm-up
+            torch.cuda.synchronize()
+            cd.err.zero_()
+            barrier()
+            e0.record(st)
+            encode()
+            e1.record(st)
+            torch.cuda.synchronize()
+            enc_ms += e0.elapsed_time(e1)
+            C._lib.raise_flags(cd.read_err(), f"config 4 encode ({kind}, {b} bits)")
+            for l, ch in zip(ls, cd.chunks(b, shape, torch.bfloat16, outliers)):
+                per_layer.setdefault(l, {})[kind] = ch
+                blocks += ch.geom.n_vectors
+                comp += ch.compressed_bytes()
+                meta += ch.metadata_bytes()
+                n_out += ch.n_outliers
+            del x, cd
+            torch.cuda.empty_cache()
+    chunks = [(l, hr, A.DecodeAttention(per_layer[l]["K"], per_layer[l]["V"], C4_G)) for l in sorted(per_layer)]
     g = torch.Generator(device=dev)
     g.manual_seed(6006)
     qs = {l: (torch.randn(C4_B, nh * C4_G, C4_D, generator=g, device=dev) / C4_D ** 0.5).to(torch.bfloat16)
@@ -481,7 +549,6 @@ def bench_config4(dev, rank, world, steps, barrier):
         if op.flags():
             raise RuntimeError(f"config-4 attention error flags {op.flags():#x}")
     barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(st)
     for _ in range(steps):
         step()
@@ -500,11 +567,17 @@ def bench_config4(dev, rank, world, steps, barrier):
         return None
     peak, peak_kind = measured_peaks()
     att_bytes = comp + meta + 2 * 2 * C4_B * C4_LAYERS * C4_KV * C4_G * C4_D
+    enc_alg = blocks * 16.0 + comp
     return {"workload": "config4: Qwen2.5-7B KV 28L x 4 kv-heads x D128, B4, ctx 131072, bits per layer "
                         f"{bits} (K Student-t(3), V N(0,1))",
             "parallelism": f"(layer, kv-head) units round-robin over {world} ranks, no collective",
             "encode": {"metric": "E8+rANS encode Gvec/s", "value": blocks / (enc_ms * 1e-3) / 1e9, "unit": "Gvec/s",
-                       "ms": enc_ms, "note": "whole model, through codec.compress (includes its host syncs)"},
+                       "ms": enc_ms, "note": "whole model: per rank one Codec batch per (bit rate, K/V), each "
+                                             "timed without host synchronisation inside, times summed",
+                       "roofline": {"bound": "hbm", "achieved": enc_alg / (enc_ms * 1e-3) / 1e9 / world,
+                                    "peak": peak, "unit": "GB/s per GPU",
+                                    "frac": enc_alg / (enc_ms * 1e-3) / 1e9 / world / peak, "peak_kind": peak_kind,
+                                    "algorithmic": "bf16 in + compressed out"}},
             "attention": {"metric": A_METRIC, "value": att_bytes / (att_ms * 1e-3) / 1e9, "unit": "GB/s",
                           "ms_per_step": att_ms, "tokens_per_s": C4_B * 1e3 / att_ms,
                           "roofline": {"bound": "hbm", "achieved": att_bytes / (att_ms * 1e-3) / 1e9 / world,
@@ -513,6 +586,153 @@ def bench_config4(dev, rank, world, steps, barrier):
                                        "peak_kind": peak_kind}},
             "bits_per_dim": comp * 8 / (blocks * 8), "outlier_records": int(n_out),
             "gpu_launches": steps * 3 * len(chunks) * world}
+
+
+C1_VEC, C1_D = 262144, 128
+
+
+def c1_input(dev, seed):
+    """Config 1: (262144, 128) fp32, N(0,1) times a log-normal(0, 0.5) magnitude per vector."""
+    import torch
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    return (torch.randn(C1_VEC, C1_D, generator=g, device=dev) *
+            torch.exp(0.5 * torch.randn(C1_VEC, 1, generator=g, device=dev))).contiguous()
+
+
+def bench_config1(dev, rank, world, steps, warmup, barrier, with_oracle):
+    """Config 1 per rank (weak scaling): one chunk of 262,144 heads x 16 blocks
+    (a per-vector fp16 scale), encode + decode to fp32 per step, CUDA-graphed;
+    reconstructed MSE and bitstream bytes, checked against the C oracle's for
+    the same input when `with_oracle` (rank 0 only)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from latticequant_b200 import codec as C
+
+    x = c1_input(dev, 7100 + rank)
+    bph = C1_D // 8
+    n_blocks = C1_VEC * bph
+    cd = C.Codec(C.Geometry(1, C1_VEC, bph, TILE), dev)
+    out = torch.empty(n_blocks * 8, dtype=torch.float32, device=dev)
+
+    def step():
+        cd.encode(x, BITS)
+        cd.expand_tables(enc=False, dec=True)
+        cd.decode(out)
+
+    step()
+    torch.cuda.synchronize()
+    if cd.read_err():
+        raise RuntimeError(f"config 1: device error flags {cd.read_err():#x}")
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        step()
+    torch.cuda.current_stream(dev).wait_stream(s)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(max(warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream(dev)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(steps):
+        graph.replay()
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    del graph
+    n_words = cd.n_words()
+    comp = 4 * n_words + (n_blocks + 7) // 8 + 2 * C1_VEC
+    lanes = C.Geometry(1, C1_VEC, bph, TILE).n_lanes
+    meta = 8 * lanes
+    diff = out.view(C1_VEC, C1_D).double() - x.double()
+    mse = float((diff * diff).mean())
+    nmse = mse / float((x.double() ** 2).mean())
+
+    # e2e through the same calls with host buffers: x in, decoded vectors out
+    host_x = x.cpu().pin_memory()
+    host_out = torch.empty(n_blocks * 8, dtype=torch.float32).pin_memory()
+    dx = torch.empty_like(x)
+
+    def e2e_step():
+        dx.copy_(host_x, non_blocking=True)
+        cd.encode(dx, BITS)
+        cd.expand_tables(enc=False, dec=True)
+        cd.decode(out)
+        host_out.copy_(out, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    k2 = max(2, min(steps, 5))
+    e0.record(st)
+    for _ in range(k2):
+        e2e_step()
+    e1.record(st)
+    torch.cuda.synchronize()
+    ems = e0.elapsed_time(e1) / k2
+    vals = torch.tensor([ms, ems], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    ms, ems = vals.tolist()
+    if rank != 0:
+        return None
+    peak, peak_kind = measured_peaks()
+    alg = n_blocks * (32.0 + 2 * comp / n_blocks + 32.0)  # fp32 in, compressed out, compressed in, fp32 out
+    res = {"metric": "E8+rANS encode/decode Gvec/s", "value": world * n_blocks / (ms * 1e-3) / 1e9,
+           "unit": "Gvec/s", "ms_per_step": ms,
+           "workload": "config1: 262,144 x 128 fp32 (N(0,1) x lognormal(0,0.5) per vector), per-vector fp16 "
+                       "scale (one chunk of 262,144 heads x 16 blocks), 4 b/dim, encode + decode to fp32",
+           "mse": mse, "nmse": nmse, "bitstream_bytes": comp, "bits_per_dim": comp * 8 / (n_blocks * 8),
+           "bytes_rule": "4 x words + coset bits + 2 B per scale (llm/compressed_kv_cache.py:113-119)",
+           "lane_metadata_bytes": meta,
+           "step_roofline": {"bound": "hbm", "achieved": alg / (ms * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
+                             "frac": alg / (ms * 1e-3) / 1e9 / peak, "peak_kind": peak_kind,
+                             "algorithmic_GB": alg / 1e9},
+           "e2e": {"value": world * n_blocks / (ems * 1e-3) / 1e9, "unit": "Gvec/s", "ms_per_step": ems,
+                   "h2d_bytes_per_step": x.numel() * 4, "d2h_bytes_per_step": out.numel() * 4},
+           "gpu_launches": steps * 10}
+    if with_oracle:
+        try:
+            import oracle.lq_oracle as O
+
+            O.build()
+            xn = x.cpu().numpy()
+            t0 = time.perf_counter()
+            ref = O.compress_chunk(xn, O.DT_F32, C1_VEC, bph, BITS, tile_blocks=TILE, ties="stable")
+            rec = O.decompress_chunk(ref, O.DT_F32).reshape(C1_VEC, C1_D)
+            dt = time.perf_counter() - t0
+            r_bytes = 4 * int(ref.words.size) + (n_blocks + 7) // 8 + 2 * C1_VEC
+            d = rec.astype(np.float64) - xn.astype(np.float64)
+            r_mse = float((d * d).mean())
+            same = (int(ref.words.size) == n_words and
+                    np.array_equal(ref.words, cd.words[:n_words].cpu().numpy().view(np.uint32)) and
+                    np.array_equal(rec.reshape(-1).view(np.uint32), out.cpu().numpy().view(np.uint32)))
+            # the reference's own layout: one 16-stream chunk, numpy table ties,
+            # plus the one spare word per stream the reference stores
+            refl = O.compress_chunk(xn, O.DT_F32, C1_VEC, bph, BITS, tile_blocks=None, ties="numpy")
+            n0 = int(refl.tile_n0.sum())
+            n_streams = 8 * (n0 > 0) + 8 * (n_blocks - n0 > 0)  # an empty coset has no streams
+            rl_bytes = 4 * (int(refl.words.size) + n_streams) + (n_blocks + 7) // 8 + 2 * C1_VEC
+            res["oracle"] = {"mse": r_mse, "bitstream_bytes": r_bytes, "identical_words_and_decode": bool(same),
+                             "mse_equal": r_mse == mse, "bytes_equal": r_bytes == comp,
+                             "reference_layout_bytes": rl_bytes,
+                             "reference_layout_bits_per_dim": rl_bytes * 8 / (n_blocks * 8),
+                             "note": "C oracle (oracle/lq_oracle_codec.c) on the same input: same lane layout "
+                                     "(1024-block tiles) and stable table ties; reference_layout_* = one "
+                                     "16-stream chunk as the reference codes it (numpy ties, spare word per "
+                                     f"stream); oracle time {dt:.1f} s"}
+        except Exception as e:  # the comparison is reported, not required
+            res["oracle"] = {"unavailable": str(e)[:200]}
+    return res
 
 
 C5_METRIC = "decode tok/s"
@@ -559,6 +779,7 @@ def bench_config5(dev, rank, world, args, barrier):
     cache = CompressedAttentionKVCache(4, tail_tokens=64, head_range=hr, layout=args.c5_layout).bind(model)
     host = torch.empty(T, B, dtype=torch.int64, pin_memory=True)
     st = torch.cuda.current_stream(dev)
+    e_dec0, e_dec1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.no_grad():
         barrier()
@@ -574,7 +795,7 @@ def bench_config5(dev, rank, world, args, barrier):
             if i == W:
                 barrier()
                 torch.cuda.synchronize()
-                e0.record(st)
+                e_dec0.record(st)
             if stepper is not None:
                 nxt = stepper.step(nxt)
             else:
@@ -582,15 +803,55 @@ def bench_config5(dev, rank, world, args, barrier):
                 nxt = out.logits[:, -1].argmax(-1, keepdim=True)
                 del out
             host[i].copy_(nxt.view(-1), non_blocking=True)
-        e1.record(st)
+        e_dec1.record(st)
         torch.cuda.synchronize()
         captures = stepper.captures if stepper is not None else 0
         if stepper is not None:
             stepper.release()  # the graph holds collectives when sharded: gone before the process group
-    ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+        # the attention of one layer (every compressed part, the exact tail and
+        # the LSE merge), timed eagerly after the run, and the fused kernel over
+        # the layer's prefill chunk alone (its roofline)
+        Hq = cfg.num_attention_heads // world
+        G = cfg.num_attention_heads // cfg.num_key_value_heads
+        D = cfg.hidden_size // cfg.num_attention_heads
+        gq = torch.Generator(device=dev)
+        gq.manual_seed(5007)
+        q4 = (torch.randn(B, Hq, 1, D, generator=gq, device=dev) / D ** 0.5).to(torch.bfloat16)
+        reps = 10
+        for _ in range(2):
+            cache.decode_attention(0, q4)
+        torch.cuda.synchronize()
+        e0.record(st)
+        for _ in range(reps):
+            cache.decode_attention(0, q4)
+        e1.record(st)
+        torch.cuda.synchronize()
+        layer_attn_ms = e0.elapsed_time(e1) / reps
+        part = cache._state[0].parts[0]
+        op = part.op(G)
+        q3 = q4.view(B, Hq, D)
+        o3 = torch.empty(B, Hq, D, dtype=torch.float32, device=dev)
+        l3 = torch.empty(B, Hq, dtype=torch.float32, device=dev)
+        for _ in range(2):
+            op(q3, o3, l3)
+        torch.cuda.synchronize()
+        e0.record(st)
+        for _ in range(reps):
+            op(q3, o3, l3)
+        e1.record(st)
+        torch.cuda.synchronize()
+        kern_ms = e0.elapsed_time(e1) / reps
+        if part.layout == "compact":
+            kern_bytes = compact_chunk_bytes(part.k) + compact_chunk_bytes(part.v)
+        else:
+            kern_bytes = (part.k.compressed_bytes() + part.v.compressed_bytes() + part.k.metadata_bytes() +
+                          part.v.metadata_bytes())
+        kern_bytes += q3.numel() * 2 + o3.numel() * 4
+    vals = torch.tensor([e_dec0.elapsed_time(e_dec1), layer_attn_ms, kern_ms],
+                        dtype=torch.float64, device=dev)
     if world > 1:
-        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    ms = float(ms.item())
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    ms, layer_attn_ms, kern_ms = vals.tolist()
     flags = cache.flags()
     if flags:
         raise RuntimeError(f"config-5 attention error flags {flags:#x}")
@@ -599,6 +860,7 @@ def bench_config5(dev, rank, world, args, barrier):
     mem = torch.cuda.max_memory_allocated(dev)
     if rank != 0:
         return None
+    peak, peak_kind = measured_peaks()
     return {"metric": C5_METRIC, "value": B * steps * 1e3 / ms, "unit": "tok/s", "n_gpus": world, "steps": steps,
             "warmup": W, "ms_per_step": ms / steps, "higher_is_better": True, "scaling": "strong",
             "dtype": "bf16", "data": "synthetic (random-init weights N(0,0.02), seeded random token ids)",
@@ -612,6 +874,15 @@ def bench_config5(dev, rank, world, args, barrier):
                                                      "after each tail flush, inside the timed region)",
             "prefill_s": prefill_s, "compressed_cache_GB_rank0": comp / 1e9,
             "max_memory_GB_rank0": mem / 1e9,
+            "attention": {"layer_ms": layer_attn_ms, "share_of_step": L * layer_attn_ms / (ms / steps),
+                          "note": "one layer's attention (compressed parts + exact tail + merge) timed eagerly "
+                                  "after the run, x layers / step time",
+                          "roofline": {"bound": "hbm", "kernel": "fused attention over a layer's prefill chunk "
+                                                                 f"({part.layout} layout)",
+                                       "kernel_ms": kern_ms, "achieved": kern_bytes / (kern_ms * 1e-3) / 1e9,
+                                       "peak": peak, "unit": "GB/s", "peak_kind": peak_kind,
+                                       "frac": kern_bytes / (kern_ms * 1e-3) / 1e9 / peak,
+                                       "algorithmic_GB": kern_bytes / 1e9}},
             "e2e": {"value": B * steps * 1e3 / ms, "unit": "tok/s", "h2d_bytes_per_step": B * 8,
                     "d2h_bytes_per_step": B * 8,
                     "note": "decode steps with the token ids copied to pinned host memory each step"}}
@@ -662,6 +933,10 @@ def main():
     ap.add_argument("--no-attn", action="store_true", help="skip the config-3 attention measurement")
     ap.add_argument("--e2e-group", type=int, default=E2E_GROUP, help="chunks per pipelined e2e transfer group")
     ap.add_argument("--no-c4", action="store_true", help="skip the config-4 mixed-rate measurement")
+    ap.add_argument("--no-c1", action="store_true", help="skip the config-1 measurement")
+    ap.add_argument("--no-c5", action="store_true", help="skip the config-5 decode measurement")
+    ap.add_argument("--no-c5-compact", action="store_true",
+                    help="skip the second config-5 run with the compact-layout cache")
     ap.add_argument("--only-c5", action="store_true",
                     help="run only config 5 (Llama-3.1-8B-shaped decode through the compressed cache) and print its line")
     ap.add_argument("--c5-layers", type=int, default=32)
@@ -851,23 +1126,31 @@ def main():
                "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": out.numel() * 2,
                "ms_per_step": ems, "pipeline": f"{n_grp} groups of {grp} chunks, 3 streams"}
 
-    # roofline of the dominant kernel phase, on algorithmic bytes (config-2 per-block figures)
+    # roofline of each phase on its OWN algorithmic bytes (what that phase must
+    # move at the least): scales read the bf16 input; quantize reads it and
+    # writes the coset bits; the lane encoder writes the words; decode reads
+    # words + coset bits + scales and writes bf16.  The symbol columns between
+    # quantize and the encoder are an intermediate and count nowhere.
     peak, peak_kind = measured_peaks()
     comp_per_block = comp_bytes / BLOCKS
-    enc_alg = BLOCKS * (16.0 + comp_per_block)     # bf16 in + compressed out
-    dec_alg = BLOCKS * (comp_per_block + 16.0)     # compressed in + bf16 out
-    alg = {"scales": BLOCKS * 16.0, "quantize": enc_alg, "tables": 0.0, "encode": enc_alg, "expand_dec": 0.0,
-           "decode": dec_alg}
+    words_per_block = 4.0 * n_words / BLOCKS
+    alg = {"scales": BLOCKS * 16.0, "quantize": BLOCKS * (16.0 + 1.0 / 8), "tables": 0.0,
+           "encode": BLOCKS * words_per_block, "expand_dec": 0.0, "decode": BLOCKS * (comp_per_block + 16.0)}
     dom = max(names, key=lambda n: acc[n])
     achieved = alg[dom] / (acc[dom] * 1e-3) / 1e9
+    phases = {n: {"ms": round(acc[n], 4), "algorithmic_GB": alg[n] / 1e9,
+                  "frac": (alg[n] / (acc[n] * 1e-3) / 1e9 / peak) if alg[n] and acc[n] else None}
+              for n in names}
+    step_alg = BLOCKS * (16.0 + comp_per_block) + BLOCKS * (comp_per_block + 16.0)
 
     cpu = None
-    if rank == 0 and not args.no_cpu:
+    if rank == 0 and world == 1 and not args.no_cpu:
         n_thr = os.cpu_count() or 1
-        v, blocks, dt = cpu_baseline(n_thr, sample_chunks=max(2, min(8, n_thr)))
+        v, blocks, dt = cpu_baseline(n_thr, sample_chunks=max(2, min(8, n_thr)), min_seconds=10.0)
         cpu = {"value": v, "unit": UNIT, "cores": n_thr, "kind": "port",
-               "sample": f"{blocks} blocks ({blocks // (N_KV * BPH)} chunks of config 2), "
-                         f"oracle/lq_oracle_codec.c on {n_thr} threads, {dt:.1f} s"}
+               "sample": f"{blocks} blocks ({max(2, min(8, n_thr))} config-2 chunks coded and decoded "
+                         f"{blocks // (max(2, min(8, n_thr)) * N_KV * BPH)} times), oracle/lq_oracle_codec.c on "
+                         f"{n_thr} threads, {dt:.1f} s"}
 
     attn = None
     if not args.no_attn:
@@ -883,6 +1166,21 @@ def main():
     if not args.no_c4:
         torch.cuda.empty_cache()
         c4 = bench_config4(dev, rank, world, max(2, min(args.steps, 5)), barrier)
+    c1 = None
+    if not args.no_c1:
+        torch.cuda.empty_cache()
+        c1 = bench_config1(dev, rank, world, args.steps, args.warmup, barrier, with_oracle=world == 1 and rank == 0)
+    c5 = None
+    if not args.no_c5:
+        torch.cuda.empty_cache()
+        c5 = bench_config5(dev, rank, world, args, barrier)
+        if not args.no_c5_compact and args.c5_layout == "rans":
+            torch.cuda.empty_cache()
+            args.c5_layout = "compact"
+            c5c = bench_config5(dev, rank, world, args, barrier)
+            args.c5_layout = "rans"
+            if rank == 0:
+                c5["compact_layout"] = c5c
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -895,12 +1193,18 @@ def main():
                            "cuda_graph": graph is not None},
                 "bits_per_dim": comp_bytes * 8 / (BLOCKS * 8),
                 "phase_ms": {n: round(acc[n], 4) for n in names},
+                "phases": phases,
                 "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
                              "frac": achieved / peak, "peak_kind": peak_kind,
                              "traffic": (TRAFFIC_PER_BLOCK[dom] * BLOCKS / 1e9) if dom in TRAFFIC_PER_BLOCK else None,
                              "traffic_unit": "GB per launch", "algorithmic_GB": alg[dom] / 1e9},
+                "step_roofline": {"bound": "hbm", "achieved": step_alg / (ms * 1e-3) / 1e9, "peak": peak,
+                                  "unit": "GB/s per GPU", "frac": step_alg / (ms * 1e-3) / 1e9 / peak,
+                                  "peak_kind": peak_kind, "algorithmic_GB": step_alg / 1e9,
+                                  "algorithmic": "bf16 in + compressed out (encode), compressed in + bf16 out "
+                                                 "(decode)"},
                 "clocks": clocks, "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
-                "cpu_baseline": cpu, "attention": attn, "config4": c4}
+                "cpu_baseline": cpu, "attention": attn, "config4": c4, "config1": c1, "config5": c5}
         print(json.dumps(line), flush=True)
     if graph is not None:
         del graph

@@ -98,7 +98,10 @@ int lq_head_scales(const void *x, int dtype, int64_t n_heads_total, int64_t elem
  *             most 254 heads per call)
  *   set-up    the first call on a device (with that device current) looks up
  *             the array's device address; make that first call before any
- *             CUDA stream capture
+ *             CUDA stream capture.  The address is cached per device and
+ *             context: after cudaDeviceReset (or in a context created by the
+ *             caller) the next call looks it up again, so that call, too,
+ *             belongs outside a capture
  *   sharing   all calls use the same array, which keeps the last call's
  *             contents (nothing needs to start at zero); calls that can
  *             overlap on the GPU -- different streams without ordering, or
@@ -290,6 +293,15 @@ int lq_attn_decode_compact(const lq_compact_view *k, const lq_compact_view *v, c
  *   out     [rows][head_dim] in out_dtype; lse optional [rows] */
 int lq_attn_merge(const float *o_parts, const float *lse_parts, int64_t n_parts, int64_t rows, int head_dim,
                   void *out, int out_dtype, float *lse, void *stream);
+
+/* lq_attn_merge over parts packed one after another, each [rows][head_dim]
+ * o values followed by its [rows] lse values -- the layout one all-gather of
+ * every rank's (o, lse) buffer produces, so a sequence-sharded decode step
+ * needs one collective.  No reference counterpart (the reference attends on
+ * one GPU).
+ *   parts   [n_parts][rows * head_dim + rows] fp32 */
+int lq_attn_merge_packed(const float *parts, int64_t n_parts, int64_t rows, int head_dim, void *out, int out_dtype,
+                         float *lse, void *stream);
 
 /* Fused merge of the compact layout with an fp16 fallback
  * (llm/fused_triton_merge.py:33-177): for each of n_heads*bph blocks,

@@ -88,6 +88,7 @@ def _declare(lib):
         "lq_attn_decode": ([ctypes.POINTER(ChunkView), ctypes.POINTER(ChunkView), vp, i32, i64, i64, i64, i32, i32,
                             i32, f32, vp, i32, vp, vp, vp, sz, vp, vp], i32),
         "lq_attn_merge": ([vp, vp, i64, i64, i32, vp, i32, vp, vp], i32),
+        "lq_attn_merge_packed": ([vp, i64, i64, i32, vp, i32, vp, vp], i32),
         "lq_attn_compact_workspace": ([i64, i64, i32, i32], sz),
         "lq_attn_decode_compact": ([ctypes.POINTER(CompactView), ctypes.POINTER(CompactView), vp, i32, i64, i64, i64,
                                     i32, i32, f32, vp, i32, vp, vp, sz, vp, vp], i32),

@@ -319,3 +319,22 @@ def merge_attention(o_parts: Sequence[torch.Tensor] | torch.Tensor, lse_parts: S
     check(lib().lq_attn_merge(ptr(of), ptr(lf), n, rows, D, ptr(out), _lib.dtype_code(out.dtype), ptr(lse),
                               stream_handle(o.device)), "lq_attn_merge")
     return out.view(o.shape[1:]), lse.view(ls.shape[1:])
+
+
+def merge_attention_packed(parts: torch.Tensor, rows: int, head_dim: int, out_dtype: torch.dtype = torch.float32,
+                           out: Optional[torch.Tensor] = None,
+                           lse: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """merge_attention over parts packed as one fp32 tensor (n_parts, rows *
+    head_dim + rows): each part's o rows, then its lse values -- what one
+    all-gather of every rank's packed (o, lse) gives.  Returns (o (rows, D), lse (rows,))."""
+    _lib.require_cuda(parts)
+    if parts.dtype != torch.float32 or not parts.is_contiguous() or parts.dim() != 2 or \
+            parts.shape[1] != rows * (head_dim + 1):
+        raise ValueError("parts must be a contiguous fp32 (n_parts, rows * (head_dim + 1)) tensor")
+    if out is None:
+        out = torch.empty((rows, head_dim), dtype=out_dtype, device=parts.device)
+    if lse is None:
+        lse = torch.empty(rows, dtype=torch.float32, device=parts.device)
+    check(lib().lq_attn_merge_packed(ptr(parts), parts.shape[0], rows, head_dim, ptr(out), _lib.dtype_code(out.dtype),
+                                     ptr(lse), stream_handle(parts.device)), "lq_attn_merge_packed")
+    return out, lse

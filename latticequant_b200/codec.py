@@ -269,6 +269,38 @@ class Codec:
     def n_words(self) -> int:
         return int(self.lane_off[-1].item()) & 0xFFFFFFFF
 
+    def chunks(self, bits: float, shape: tuple, dtype: torch.dtype, outliers: bool = False) -> list:
+        """The batch now in the buffers as one LaneChunk per chunk (reads the
+        lane offsets, so it synchronises).  Words, tables, scales and coset
+        words are copied out, so the Codec can code the next batch.  shape /
+        dtype: the (B, H, S, D) tensor and dtype of one chunk; outliers: the
+        batch went through quantize_outliers (records are split per chunk)."""
+        g = self.geom
+        lpc, nh, wpc, nt = g.n_tiles * NSTREAMS, g.n_heads, g.coset_words_per_chunk, g.n_tiles
+        off = self.lane_off.to(torch.int64) & 0xFFFFFFFF
+        bounds = off[::lpc].tolist()  # first word of every chunk, then the total
+        counts = self.out_count.tolist() if outliers else [0] * g.n_chunks
+        geom1 = Geometry(1, g.n_heads, g.bph, g.tile_blocks)
+        out = []
+        for c in range(g.n_chunks):
+            w0, w1 = int(bounds[c]), int(bounds[c + 1])
+            lo = (off[c * lpc:(c + 1) * lpc + 1] - w0).to(torch.int32)
+            n_out = int(counts[c])
+            rec = None
+            if n_out:
+                base = c * self.out_cap * 10
+                rec = self.out_rec[base:base + n_out * 10].view(n_out, 10).clone()
+            sl = lambda t, n: t[c * n:(c + 1) * n].clone()  # noqa: E731
+            out.append(LaneChunk(geom=geom1, bits=bits, orig_shape=tuple(shape), orig_dtype=dtype,
+                                 scale_f32=sl(self.scale_f32, nh), scale_f16=sl(self.scale_f16, nh),
+                                 coset_words=sl(self.coset_words, wpc), tile_n0=sl(self.tile_n0, nt),
+                                 tab_lo=sl(self.tab_lo, NSTREAMS), tab_nsym=sl(self.tab_nsym, NSTREAMS),
+                                 tab_freq=sl(self.tab_freq, NSTREAMS), words=self.words[w0:max(w1, w0 + 1)].clone(),
+                                 lane_off=lo, lane_nbits=sl(self.lane_nbits, lpc),
+                                 lane_state=sl(self.lane_state, lpc), n_words=w1 - w0, outlier_rec=rec,
+                                 n_outliers=n_out))
+        return out
+
 
 # --------------------------------------------------------------------------
 # allocating wrappers

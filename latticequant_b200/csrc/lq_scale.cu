@@ -315,16 +315,40 @@ namespace {
 constexpr int kMaxDevices = 64;
 std::mutex g_static_mu;
 float *g_static_scratch[kMaxDevices] = {};
+void *g_static_ctx[kMaxDevices] = {};  // the context the cached address belongs to
 
+// The current driver context (CUcontext), fetched through the runtime so the
+// library needs no link-time dependency on libcuda; nullptr if unavailable.
+void *current_context() {
+    using CtxGetCurrent = int (*)(void **);
+    static CtxGetCurrent fn = [] {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return (CtxGetCurrent) nullptr;
+        return reinterpret_cast<CtxGetCurrent>(f);
+    }();
+    void *ctx = nullptr;
+    if (fn == nullptr || fn(&ctx) != 0) return nullptr;
+    return ctx;
+}
+
+// The scratch array's device address on the current device.  The address is
+// looked up once per (device, context) and cached; a new context on the same
+// device (after cudaDeviceReset, or a context the caller created) makes the
+// next call look it up again.
 int static_scratch_for_current_device(float **out) {
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess) return LQ_ERR_CUDA;
     if (dev < 0 || dev >= kMaxDevices) return LQ_ERR_INVALID;
+    void *ctx = current_context();
     std::lock_guard<std::mutex> lock(g_static_mu);
-    if (g_static_scratch[dev] == nullptr) {
+    if (g_static_scratch[dev] == nullptr || ctx == nullptr || ctx != g_static_ctx[dev]) {
         void *p = nullptr;
         if (cudaGetSymbolAddress(&p, lq_scales_static_scratch) != cudaSuccess || p == nullptr) return LQ_ERR_CUDA;
         g_static_scratch[dev] = static_cast<float *>(p);
+        g_static_ctx[dev] = ctx;
     }
     *out = g_static_scratch[dev];
     return LQ_OK;
@@ -339,6 +363,11 @@ extern "C" int lq_head_scales_static(const void *x, int dtype, int64_t n_heads_t
     if (x == nullptr || elems_per_head == 0) return LQ_ERR_INVALID;
     if (dtype != LQ_F32 && dtype != LQ_F16 && dtype != LQ_BF16) return LQ_ERR_INVALID;
     const size_t cap = sizeof(float) * (size_t)LQ_HEAD_SCALES_STATIC_FLOATS;
+    // a head takes 32 * (n_l1 + 1) scratch floats when its sum needs a second
+    // pass (none otherwise); compared by division so no product can overflow
+    const lq::Cascade c(elems_per_head);
+    if (c.n_l1 > 1 && n_heads_total > (int64_t)(LQ_HEAD_SCALES_STATIC_FLOATS / 32) / (c.n_l1 + 1))
+        return LQ_ERR_CAPACITY;
     if (lq_head_scales_workspace(n_heads_total, elems_per_head) > cap) return LQ_ERR_CAPACITY;
     float *ws = nullptr;
     const int rc = static_scratch_for_current_device(&ws);

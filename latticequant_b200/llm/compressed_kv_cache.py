@@ -138,19 +138,41 @@ class OptimizedChunk:
         return self._offsets
 
 
+def _tensor_bytes(t) -> int:
+    return t.nelement() * t.element_size()
+
+
+def _chunk_stored_bytes(c) -> int:
+    """What one chunk costs under the reference's counting rule
+    (llm/compressed_kv_cache.py:113-119): merged bitstream words, packed coset
+    bits and fp16 scales -- tables, states and bit counts are not counted.
+    Outlier records (no reference counterpart) are counted at 40 B each; chunk
+    layouts without a merged bitstream report their own size."""
+    if not hasattr(c, "gpu_bitstream"):
+        return c.total_bytes
+    n = _tensor_bytes(c.gpu_bitstream) + _tensor_bytes(c.coset_packed) + _tensor_bytes(c.scales)
+    if c.lanes is not None and c.lanes.n_outliers:
+        n += codec.OUTLIER_REC_BYTES * c.lanes.n_outliers
+    return n
+
+
 class CompressedKVLayer:
-    """llm/compressed_kv_cache.py:96-126."""
+    """The chunks of one layer's K (or V), in append order; the attribute
+    surface of the reference's class (llm/compressed_kv_cache.py:96-126)."""
 
     def __init__(self):
         self.chunks: List[OptimizedChunk] = []
 
+    def append_chunk(self, chunk):
+        self.chunks.append(chunk)
+
     @property
     def is_empty(self):
-        return len(self.chunks) == 0
+        return not self.chunks
 
     @property
     def total_seq(self):
-        return sum(c.orig_shape[2] for c in self.chunks) if self.chunks else 0
+        return sum(c.orig_shape[2] for c in self.chunks)
 
     @property
     def num_vectors(self):
@@ -158,59 +180,37 @@ class CompressedKVLayer:
 
     @property
     def total_bytes(self):
-        total = 0
-        for c in self.chunks:
-            if not hasattr(c, "gpu_bitstream"):  # other chunk layouts count themselves
-                total += c.total_bytes
-                continue
-            total += c.gpu_bitstream.nelement() * c.gpu_bitstream.element_size()
-            total += c.coset_packed.nelement() * c.coset_packed.element_size()
-            total += c.scales.nelement() * c.scales.element_size()
-            if c.lanes is not None and c.lanes.n_outliers:
-                total += codec.OUTLIER_REC_BYTES * c.lanes.n_outliers
-        return total
+        return sum(_chunk_stored_bytes(c) for c in self.chunks)
 
     @property
     def fp16_equivalent_bytes(self):
-        return self.num_vectors * 8 * 2
-
-    def append_chunk(self, chunk):
-        self.chunks.append(chunk)
+        return 16 * self.num_vectors  # 8 fp16 values per E8 block
 
 
 class UncompressibleKVLayer:
-    """llm/compressed_kv_cache.py:129-143."""
+    """A layer kept raw because head_dim is not a multiple of 8
+    (llm/compressed_kv_cache.py:129-143): it costs what it holds."""
 
     def __init__(self, tensor):
         self.data = tensor
 
-    @property
-    def is_empty(self):
-        return False
-
-    @property
-    def total_bytes(self):
-        return self.data.nelement() * self.data.element_size()
-
-    @property
-    def fp16_equivalent_bytes(self):
-        return self.total_bytes
-
-    @property
-    def total_seq(self):
-        return self.data.shape[2]
+    is_empty = property(lambda self: False)
+    total_bytes = property(lambda self: _tensor_bytes(self.data))
+    fp16_equivalent_bytes = total_bytes
+    total_seq = property(lambda self: self.data.shape[2])
 
 
-_PLACEHOLDER = None
-_PLACEHOLDER_DTYPE = None
+# One empty (1, 1, 0, 1) tensor per (device, dtype) stands in for a freed or
+# not yet filled layer slot, as the reference keeps a shared placeholder.
+_PLACEHOLDERS = {}
 
 
 def _get_placeholder(device, dtype=torch.bfloat16):
-    global _PLACEHOLDER, _PLACEHOLDER_DTYPE
-    if _PLACEHOLDER is None or _PLACEHOLDER.device != torch.device(device) or _PLACEHOLDER_DTYPE != dtype:
-        _PLACEHOLDER = torch.zeros(1, 1, 0, 1, dtype=dtype, device=device)
-        _PLACEHOLDER_DTYPE = dtype
-    return _PLACEHOLDER
+    key = (torch.device(device), dtype)
+    t = _PLACEHOLDERS.get(key)
+    if t is None:
+        t = _PLACEHOLDERS[key] = torch.zeros(1, 1, 0, 1, dtype=dtype, device=device)
+    return t
 
 
 def _host_numpy_tables(chunk_lanes: codec.LaneChunk, hist: torch.Tensor):
@@ -355,83 +355,73 @@ class CompressedKVCache(DynamicCache):
         return self._store(layer_idx, device, key_states, value_states, comp_k, k_dec_new, comp_v, v_dec_new)
 
     def _store(self, layer_idx, device, key_states, value_states, comp_k, k_dec_new, comp_v, v_dec_new):
-        while len(self._comp_keys) <= layer_idx:
-            self._comp_keys.append(None)
-            self._comp_values.append(None)
-        while len(self.key_cache) <= layer_idx:
-            self.key_cache.append(_get_placeholder(device, self._model_dtype))
-            self.value_cache.append(_get_placeholder(device, self._model_dtype))
+        """Bookkeeping of update() (llm/compressed_kv_cache.py:363-395): grow the
+        per-layer lists to layer_idx, append the chunks, and extend the
+        resident dequantised K/V along the sequence (what attention reads)."""
+        missing = layer_idx + 1 - len(self._comp_keys)
+        if missing > 0:
+            self._comp_keys.extend([None] * missing)
+            self._comp_values.extend([None] * missing)
+        missing = layer_idx + 1 - len(self.key_cache)
+        if missing > 0:
+            ph = _get_placeholder(device, self._model_dtype)
+            self.key_cache.extend([ph] * missing)
+            self.value_cache.extend([ph] * missing)
         if comp_k == 'uncompressible':
+            # stored raw; the returned tensors are this update's alone
             self._comp_keys[layer_idx] = UncompressibleKVLayer(key_states)
             self._comp_values[layer_idx] = UncompressibleKVLayer(value_states)
-            self.key_cache[layer_idx] = k_dec_new
-            self.value_cache[layer_idx] = v_dec_new
+            self.key_cache[layer_idx], self.value_cache[layer_idx] = k_dec_new, v_dec_new
             return k_dec_new, v_dec_new
-        if self._comp_keys[layer_idx] is None:
-            self._comp_keys[layer_idx] = CompressedKVLayer()
-            self._comp_values[layer_idx] = CompressedKVLayer()
-        self._comp_keys[layer_idx].append_chunk(comp_k)
-        self._comp_values[layer_idx].append_chunk(comp_v)
-        prev_k = self.key_cache[layer_idx]
-        if prev_k.shape[2] > 0:
-            k_full = torch.cat([prev_k, k_dec_new], dim=2)
-            v_full = torch.cat([self.value_cache[layer_idx], v_dec_new], dim=2)
-        else:
-            k_full = k_dec_new
-            v_full = v_dec_new
-        self.key_cache[layer_idx] = k_full
-        self.value_cache[layer_idx] = v_full
-        return k_full, v_full
+        for layers, chunk in ((self._comp_keys, comp_k), (self._comp_values, comp_v)):
+            if layers[layer_idx] is None:
+                layers[layer_idx] = CompressedKVLayer()
+            layers[layer_idx].append_chunk(chunk)
+
+        def grow(resident, new):
+            return new if resident.shape[2] == 0 else torch.cat([resident, new], dim=2)
+
+        self.key_cache[layer_idx] = grow(self.key_cache[layer_idx], k_dec_new)
+        self.value_cache[layer_idx] = grow(self.value_cache[layer_idx], v_dec_new)
+        return self.key_cache[layer_idx], self.value_cache[layer_idx]
 
     # ---- reporting (llm/compressed_kv_cache.py:399-453) ----
+    def _layers(self):
+        return [l for l in self._comp_keys + self._comp_values if l is not None]
+
     def compressed_bytes(self):
-        total = 0
-        for layer in self._comp_keys + self._comp_values:
-            if layer is None:
-                continue
-            total += layer.total_bytes
-        return total
+        return sum(l.total_bytes for l in self._layers())
 
     def fp16_equivalent_bytes(self):
-        return sum(l.fp16_equivalent_bytes for l in self._comp_keys + self._comp_values if l is not None)
+        return sum(l.fp16_equivalent_bytes for l in self._layers())
 
     def decompressed_resident_bytes(self):
-        total = 0
-        for i in range(len(self.key_cache)):
-            for t in [self.key_cache[i], self.value_cache[i]]:
-                if t is not None:
-                    total += t.nelement() * t.element_size()
-        return total
+        return sum(_tensor_bytes(t) for t in self.key_cache + self.value_cache if t is not None)
 
     def actual_vram_bytes(self):
         return self.compressed_bytes() + self.decompressed_resident_bytes()
 
     def memory_report(self):
-        comp = self.compressed_bytes()
-        fp16 = self.fp16_equivalent_bytes()
-        decomp = self.decompressed_resident_bytes()
-        actual = self.actual_vram_bytes()
-        ratio_th = fp16 / max(comp, 1)
-        ratio_act = fp16 / max(actual, 1)
-        n_layers = sum(1 for x in self._comp_keys if x is not None)
-        total_dims = self.total_vectors * 8
-        eff_bits = (comp * 8) / max(total_dims, 1)
-        lines = [
+        """The reference's report text (same lines and number formats)."""
+        comp, fp16 = self.compressed_bytes(), self.fp16_equivalent_bytes()
+        decomp, actual = self.decompressed_resident_bytes(), self.actual_vram_bytes()
+        eff_bits = 8 * comp / max(8 * self.total_vectors, 1)
+        mb = lambda n: f"{n:,} B ({n / 1024 / 1024:.2f} MB)"  # noqa: E731
+        return "\n".join([
             "CompressedKVCache Report (optimized side info)",
             f"  Bits/dim:     {self.bits} (target), {eff_bits:.3f} (effective)",
-            f"  Layers:       {n_layers}",
+            f"  Layers:       {sum(x is not None for x in self._comp_keys)}",
             f"  Vectors:      {self.total_vectors:,}",
             "  OOR rate:     0.00%",
             "  ---",
-            f"  Total compressed:  {comp:,} B ({comp/1024/1024:.2f} MB)",
-            f"  Decompressed now:  {decomp:,} B ({decomp/1024/1024:.2f} MB)",
-            f"  Actual VRAM (KV):  {actual:,} B ({actual/1024/1024:.2f} MB)",
-            f"  FP16 baseline:     {fp16:,} B ({fp16/1024/1024:.2f} MB)",
+            f"  Total compressed:  {mb(comp)}",
+            f"  Decompressed now:  {mb(decomp)}",
+            f"  Actual VRAM (KV):  {mb(actual)}",
+            f"  FP16 baseline:     {mb(fp16)}",
             "  ---",
-            f"  Theoretical ratio: {ratio_th:.2f}x",
-            f"  Actual ratio:      {ratio_act:.2f}x",
-        ]
-        return "\n".join(lines)
+            f"  Theoretical ratio: {fp16 / max(comp, 1):.2f}x",
+            f"  Actual ratio:      {fp16 / max(actual, 1):.2f}x",
+        ])
 
     def get_seq_length(self, layer_idx=0):
         if layer_idx < len(self._comp_keys) and self._comp_keys[layer_idx] is not None:

@@ -58,20 +58,33 @@ def gather_heads(o_local: torch.Tensor, group: Optional[dist.ProcessGroup] = Non
     return buf.permute(1, 2, 0, 3, 4).reshape(B, Q, world * H, D)
 
 
+def _pack_partials(o_local: torch.Tensor, lse_local: torch.Tensor) -> torch.Tensor:
+    """One flat buffer: the o rows (..., D) followed by the lse values (...)."""
+    o = o_local.reshape(-1)
+    ls = lse_local.reshape(-1).to(o.dtype)
+    return torch.cat([o, ls])
+
+
+def _all_gather_flat(buf: torch.Tensor, group: Optional[dist.ProcessGroup]) -> torch.Tensor:
+    world = dist.get_world_size(group)
+    out = torch.empty((world, buf.numel()), dtype=buf.dtype, device=buf.device)
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(out, buf, group=group)
+    else:
+        dist.all_gather(list(out.unbind(0)), buf, group=group)
+    return out
+
+
 def gather_partials(o_local: torch.Tensor, lse_local: torch.Tensor,
                     group: Optional[dist.ProcessGroup] = None) -> Tuple[torch.Tensor, torch.Tensor]:
-    """All-gather the per-rank attention partials: (world, *o.shape), (world, *lse.shape)."""
-    world = dist.get_world_size(group)
-    o = o_local.contiguous()
-    ls = lse_local.contiguous()
-    o_all = torch.empty((world,) + tuple(o.shape), dtype=o.dtype, device=o.device)
-    l_all = torch.empty((world,) + tuple(ls.shape), dtype=ls.dtype, device=ls.device)
-    if dist.get_backend(group) == "nccl":
-        dist.all_gather_into_tensor(o_all, o, group=group)
-        dist.all_gather_into_tensor(l_all, ls, group=group)
-    else:
-        dist.all_gather(list(o_all.unbind(0)), o, group=group)
-        dist.all_gather(list(l_all.unbind(0)), ls, group=group)
+    """All-gather the per-rank attention partials with ONE collective (o and
+    lse packed in one buffer): returns (world, *o.shape), (world, *lse.shape)
+    views of the gathered buffer."""
+    n_o = o_local.numel()
+    packed = _all_gather_flat(_pack_partials(o_local, lse_local), group)
+    world = packed.shape[0]
+    o_all = packed[:, :n_o].reshape((world,) + tuple(o_local.shape))
+    l_all = packed[:, n_o:].reshape((world,) + tuple(lse_local.shape))
     return o_all, l_all
 
 
@@ -82,11 +95,17 @@ def sequence_sharded_merge(o_local: torch.Tensor, lse_local: torch.Tensor,
     """Attention over the whole context from each rank's slice result.
 
     o_local: (..., D) fp32 attention over this rank's keys; lse_local: (...)
-    their log-sum-exp.  Every rank returns the merged (o, lse).  `merge`
-    defaults to the CUDA merge (attention.merge_attention)."""
-    o_all, l_all = gather_partials(o_local, lse_local, group)
-    if merge is None:
-        from .attention import merge_attention
+    their log-sum-exp.  Every rank returns the merged (o, lse).  One
+    all-gather moves every rank's (o, lse) as one packed buffer; `merge`
+    defaults to the CUDA merge of that packed layout
+    (attention.merge_attention_packed, no copies)."""
+    if merge is not None:
+        o_all, l_all = gather_partials(o_local, lse_local, group)
+        return merge(o_all, l_all, out_dtype=out_dtype)
+    from .attention import merge_attention_packed
 
-        merge = merge_attention
-    return merge(o_all, l_all, out_dtype=out_dtype)
+    D = o_local.shape[-1]
+    rows = o_local.numel() // D
+    packed = _all_gather_flat(_pack_partials(o_local.float(), lse_local.float()), group)
+    o, lse = merge_attention_packed(packed, rows, D, out_dtype=out_dtype or o_local.dtype)
+    return o.view(o_local.shape), lse.view(lse_local.shape)

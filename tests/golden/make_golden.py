@@ -1,10 +1,10 @@
 """Generate golden fixtures by running the reference implementation itself.
 
-Runs ONLY in a container where the reference checkout is mounted (default
-``/root/reference``, override with LQ_REFERENCE).  The GPU box never runs
-this script; it only reads the committed ``*.npz`` files.
+Runs ONLY where a checkout of the reference is available; its path comes
+from the LQ_REFERENCE environment variable (required).  The GPU box never
+runs this script; it only reads the committed ``*.npz`` files.
 
-    python tests/golden/make_golden.py
+    LQ_REFERENCE=<path to the reference checkout> python tests/golden/make_golden.py
 
 Each fixture is produced by calling the reference's own functions on seeded
 inputs (torch.manual_seed / np.random.seed as the reference's tests use):
@@ -34,7 +34,9 @@ import sys
 import numpy as np
 import torch
 
-REF = os.environ.get("LQ_REFERENCE", "/root/reference")
+REF = os.environ.get("LQ_REFERENCE")
+if not REF or not os.path.isdir(REF):
+    sys.exit("make_golden.py: set LQ_REFERENCE to the reference checkout (the directory holding core/ and llm/)")
 OUT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(REF, "core"))
 sys.path.insert(0, os.path.join(REF, "llm"))

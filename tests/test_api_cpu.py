@@ -54,6 +54,19 @@ def test_host_only_entry_points(cabi):
     assert cabi.lq_head_scales_workspace(16, 1 << 20) > 0
 
 
+def test_static_scales_refuse_oversized_counts_before_any_device_call(cabi):
+    """lq_head_scales_static checks its scratch capacity on the host, before it
+    asks for a device: head counts whose scratch size would overflow a 64-bit
+    product are refused with LQ_ERR_CAPACITY (x is never dereferenced)."""
+    f = cabi.lq_head_scales_static
+    f.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_int64, ctypes.c_float] + \
+        [ctypes.c_void_p] * 4
+    f.restype = ctypes.c_int
+    dummy = ctypes.c_void_p(256)
+    for n_heads in (255, 1 << 40, 1 << 57, (1 << 63) - 1):
+        assert f(dummy, 2, n_heads, 1 << 20, ctypes.c_float(1.0), None, None, None, None) == -3, n_heads
+
+
 def test_build_rans_table_matches_reference_fixtures():
     from latticequant_b200.core.gpu_ans import L, build_rans_table
 

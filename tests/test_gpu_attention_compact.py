@@ -48,12 +48,16 @@ def _kv(shape, seed):
 
 
 CASES = [
-    # B, Hkv, G, S, D, bits, q dtype
+    # B, Hkv, G, S, D, bits, q dtype  (head_dim 128 with G <= 4 runs the tensor-core kernel)
     (2, 2, 4, 256, 128, 4, torch.bfloat16),
     (1, 3, 2, 128, 64, 4, torch.float16),
     (2, 1, 1, 64, 128, 3, torch.float32),
     (1, 2, 8, 96, 128, 5, torch.bfloat16),
     (1, 4, 7, 1030, 128, 4, torch.bfloat16),   # tokens past the last full warp slab
+    (1, 2, 4, 1030, 128, 4, torch.bfloat16),   # tensor cores: partial stage and CTA
+    (2, 2, 3, 2050, 128, 4, torch.float16),    # three of four padded query heads
+    (1, 3, 2, 300, 128, 5, torch.float32),
+    (1, 1, 4, 4096, 128, 3, torch.bfloat16),   # four CTAs per head
 ]
 
 
@@ -125,3 +129,52 @@ def test_compact_attention_flags_inconsistent_index(how):
 
     with pytest.raises(LatticeQuantError, match="decode_attention_compact"):
         attention.decode_attention_compact(q, kc, vc)
+
+
+def _force_fallback(chunk, force):
+    """The same chunk with the blocks in `force` (bool, per block) stored as
+    fp16 fallback rows (their merged values) instead of codes."""
+    from latticequant_b200.llm.fused_triton_merge import CompressedChunk, fused_decompress_chunk
+
+    vals = fused_decompress_chunk(chunk).reshape(-1, 8)
+    mask = chunk.repr_mask.bool()
+    keep = mask & ~force
+    rank = torch.cumsum(mask.int(), 0) - mask.int()
+    fb_rank = torch.cumsum((~mask).int(), 0) - (~mask).int()
+    was_fb = (~mask)[~keep]
+    old_rows = chunk.fallback[fb_rank[~keep].clamp(max=max(chunk.fallback.shape[0] - 1, 0)).long()] \
+        if chunk.fallback.shape[0] else torch.zeros_like(vals[~keep])
+    fb = torch.where(was_fb[:, None], old_rows, vals[~keep]).contiguous()
+    return CompressedChunk(packed=chunk.packed[rank[keep].long()].contiguous(), fallback=fb, repr_mask=keep,
+                           scales=chunk.scales, orig_shape=chunk.orig_shape, blocks_per_head=chunk.blocks_per_head,
+                           bits_per_dim=chunk.bits_per_dim, orig_dtype=chunk.orig_dtype)
+
+
+@pytest.mark.parametrize("bits", [4, 3])
+def test_compact_attention_stage_beyond_staged_fallback_rows(bits):
+    """A 128-token stage whose blocks are all fallback rows (more than the 768
+    a tensor-core stage buffer holds): the rows past the staged ones are read
+    from HBM; the result matches the reference as everywhere else."""
+    from oracle import lq_oracle as O
+
+    from latticequant_b200 import attention
+    from latticequant_b200.llm.fused_triton_merge import compress_compact
+
+    B, Hkv, G, S, D = 1, 2, 4, 512, 128
+    k = _kv((B, Hkv, S, D), 61).cuda()
+    v = _kv((B, Hkv, S, D), 62).cuda()
+    kc, _ = compress_compact(k, bits)
+    vc, _ = compress_compact(v, bits)
+    bph = S * D // 8
+    force = torch.zeros(B * Hkv * bph, dtype=torch.bool, device="cuda")
+    force[128 * 16:256 * 16] = True             # head 0, tokens 128..255: one whole stage
+    force[bph + 300 * 16:bph + 400 * 16] = True  # head 1: 100 tokens across two stages
+    kc2, vc2 = _force_fallback(kc, force), _force_fallback(vc, force)
+    assert kc2.fallback.shape[0] > kc.fallback.shape[0] + 1000
+    q = (torch.randn(B, Hkv * G, D, generator=torch.Generator().manual_seed(63)) / math.sqrt(D)).to(torch.bfloat16)
+    o = attention.decode_attention_compact(q.cuda(), kc2, vc2, out_dtype=torch.float32)
+    ref = O.decode_attention_f64(q.float().numpy(), _exact_values(kc2), _exact_values(vc2), 1 / math.sqrt(D))
+    assert _row_err(o.cpu().numpy().reshape(ref.shape), ref) <= RTOL
+    # and the same numbers as the unforced chunks (the forced rows hold the merged values)
+    o1 = attention.decode_attention_compact(q.cuda(), kc, vc, out_dtype=torch.float32)
+    assert _row_err(o.cpu().numpy(), o1.cpu().numpy()) <= RTOL
