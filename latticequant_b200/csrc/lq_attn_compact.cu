@@ -1,6 +1,7 @@
 // lq_attn_compact.cu -- decode attention over the compact fixed-rate layout.
 #include <algorithm>
 #include <cstdlib>
+#include <type_traits>
 
 #include "lq_attn_common.cuh"
 
@@ -501,10 +502,6 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
     asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
     return d;
 }
-__device__ __forceinline__ uint32_t scale_half2(uint32_t h, float m) {
-    const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&h));
-    return pack_half2(f.x * m, f.y * m);
-}
 __device__ __forceinline__ void mma_16816(float d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                           uint32_t b1) {
     asm volatile(
@@ -554,20 +551,51 @@ __device__ __forceinline__ void mstage_issue(const CompactDev &c, const CStageSp
     cp_async_commit();
 }
 
-// All threads: the staged fallback rows in units of u.
+// A block's eight values travel as four fp16x2 registers whose (low, high)
+// halves are the channels (6, 2), (5, 1), (4, 0), (7, 3): the order in which
+// two-nibble groups of a 4-bit code reach the fp16 mantissas with one mask
+// each (mblock).  The MMA fragments are laid out to match (q's channels in
+// phase K, the output rows in phase V), so the order costs nothing.
+__device__ __forceinline__ constexpr int blk_ch(int r, int hi) {
+    return (r == 0 ? (hi ? 2 : 6) : r == 1 ? (hi ? 1 : 5) : r == 2 ? (hi ? 0 : 4) : (hi ? 3 : 7));
+}
+
+// An fp16 row of 8 values (natural order), times m, in the register order above.
+__device__ __forceinline__ uint4 row_to_regs(uint4 v, float m) {
+    float f[8];
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 t = __half22float2(*reinterpret_cast<const __half2 *>(&w[i]));
+        f[2 * i] = t.x * m;
+        f[2 * i + 1] = t.y * m;
+    }
+    return make_uint4(pack_half2(f[blk_ch(0, 0)], f[blk_ch(0, 1)]), pack_half2(f[blk_ch(1, 0)], f[blk_ch(1, 1)]),
+                      pack_half2(f[blk_ch(2, 0)], f[blk_ch(2, 1)]), pack_half2(f[blk_ch(3, 0)], f[blk_ch(3, 1)]));
+}
+
+// All threads: the staged fallback rows in units of u, in register order.
 template <bool B4>
 __device__ __forceinline__ void mstage_rescale(const CStageSpan &s, uint32_t buf, float inv_u) {
     using S = MStage<B4>;
     if (s.bad) return;
     const uint32_t nf = min(32u * s.nw - (s.r1 - s.r0), (uint32_t)kMFbCap);
-    for (uint32_t r = threadIdx.x; r < nf; r += blockDim.x) {
-        uint4 v = lds_v4(buf + S::kFbOff + 16u * r);
-        v.x = scale_half2(v.x, inv_u);
-        v.y = scale_half2(v.y, inv_u);
-        v.z = scale_half2(v.z, inv_u);
-        v.w = scale_half2(v.w, inv_u);
-        sts_v4(buf + S::kFbOff + 16u * r, v);
-    }
+    for (uint32_t r = threadIdx.x; r < nf; r += blockDim.x)
+        sts_v4(buf + S::kFbOff + 16u * r, row_to_regs(lds_v4(buf + S::kFbOff + 16u * r), inv_u));
+}
+
+// A 4-bit code as the four registers: v = the big-endian code word,
+// w = (v << 1) | parity holds u0..u6 and 2*c7u + parity in nibbles 7..0
+// (channel i in nibble 7 - i); each mask leaves two nibbles times 16 in the
+// mantissas of the fp16 pair (1024, 1024).
+__device__ __forceinline__ void decode4(uint32_t v, const MUnit &m, uint32_t h[4]) {
+    const uint32_t par = __popc(v & 0x08888888u) & 1u;
+    const uint32_t w = (v << 1) | par;
+    const uint32_t add = (v >> 31) ? m.hadd1 : m.hadd0;
+    h[0] = hfma2_u32((w & 0x00F000F0u) | 0x64006400u, m.hmul, add);          // nibbles 1, 5: channels 6, 2
+    h[1] = hfma2_u32(((w >> 4) & 0x00F000F0u) | 0x64006400u, m.hmul, add);   // nibbles 2, 6: channels 5, 1
+    h[2] = hfma2_u32(((w >> 8) & 0x00F000F0u) | 0x64006400u, m.hmul, add);   // nibbles 3, 7: channels 4, 0
+    h[3] = hfma2_u32(((w << 4) & 0x00F000F0u) | 0x64006400u, m.hmul, add);   // nibbles 0, 4: channels 7, 3
 }
 
 // One block of a stage as four fp16x2 registers (channels 0-1, 2-3, 4-5, 6-7)
@@ -590,25 +618,18 @@ __device__ __forceinline__ void mblock(const CompactDev &c, const CStageSpan &s,
     const bool fb = good && !rep && f < nf;
     uint4 fv;
     if (fb && f >= (uint32_t)kMFbCap) {  // past the staged rows (a stage more than 3/8 fallback): from HBM
-        fv = __ldg(c.fallback + (b0 - s.r0) + f);
-        fv.x = scale_half2(fv.x, m.inv_u);
-        fv.y = scale_half2(fv.y, m.inv_u);
-        fv.z = scale_half2(fv.z, m.inv_u);
-        fv.w = scale_half2(fv.w, m.inv_u);
+        fv = row_to_regs(__ldg(c.fallback + (b0 - s.r0) + f), m.inv_u);
     } else {
         fv = lds_v4(buf + (fb ? S::kFbOff + 16u * f : S::kZeroOff));
     }
     if constexpr (B4) {
         const uint32_t raw = lds_u32(buf + S::kPackedOff + (s.r0 * 4u - s.a0) + 4u * pr);
         // a block that is not representable decodes the code of zeros: nibbles 8, coset 0
-        const uint32_t v = rep ? __byte_perm(raw, 0u, 0x0123u) : 0x44444444u;
-        const uint32_t par = __popc(v & 0x08888888u) & 1u;
-        const uint32_t w1 = (v << 1) | par, w4 = w1 << 4;
-        const uint32_t add = (v >> 31) ? m.hadd1 : m.hadd0;
-        h[0] = hfma2_u32((__byte_perm(w1, w4, 0x0703u) & 0x00F000F0u) | 0x64006400u, m.hmul, add) | fv.x;
-        h[1] = hfma2_u32((__byte_perm(w1, w4, 0x0602u) & 0x00F000F0u) | 0x64006400u, m.hmul, add) | fv.y;
-        h[2] = hfma2_u32((__byte_perm(w1, w4, 0x0501u) & 0x00F000F0u) | 0x64006400u, m.hmul, add) | fv.z;
-        h[3] = hfma2_u32((__byte_perm(w1, w4, 0x0400u) & 0x00F000F0u) | 0x64006400u, m.hmul, add) | fv.w;
+        decode4(rep ? __byte_perm(raw, 0u, 0x0123u) : 0x44444444u, m, h);
+        h[0] |= fv.x;
+        h[1] |= fv.y;
+        h[2] |= fv.z;
+        h[3] |= fv.w;
     } else {
         float x[8];
         if (rep) {
@@ -636,11 +657,59 @@ __device__ __forceinline__ void mblock(const CompactDev &c, const CStageSpan &s,
 #pragma unroll
             for (int i = 0; i < 8; ++i) x[i] = 0.f;
         }
-        h[0] = pack_half2(x[0], x[1]) | fv.x;
-        h[1] = pack_half2(x[2], x[3]) | fv.y;
-        h[2] = pack_half2(x[4], x[5]) | fv.z;
-        h[3] = pack_half2(x[6], x[7]) | fv.w;
+        h[0] = pack_half2(x[blk_ch(0, 0)], x[blk_ch(0, 1)]) | fv.x;
+        h[1] = pack_half2(x[blk_ch(1, 0)], x[blk_ch(1, 1)]) | fv.y;
+        h[2] = pack_half2(x[blk_ch(2, 0)], x[blk_ch(2, 1)]) | fv.z;
+        h[3] = pack_half2(x[blk_ch(3, 0)], x[blk_ch(3, 1)]) | fv.w;
     }
+}
+
+// mblock for a stage that is full (every token in range), whose index
+// chained on arrival and whose fallback rows are all staged: no range
+// checks.  code0: shared address of the word's first code; fb0: of the
+// fallback row the block would have if no block before it in its word were
+// representable; lowmask: the word's bits below the block's.
+template <bool B4>
+__device__ __forceinline__ void mblock_fast(int bits, uint32_t code0, uint32_t fb0, uint32_t zero, uint32_t wd,
+                                            uint32_t lowmask, const MUnit &m, uint32_t h[4]) {
+    const uint32_t below = __popc(wd & lowmask);
+    const bool rep = (wd & (lowmask + 1u)) != 0u;
+    const uint4 fv = lds_v4(rep ? zero : fb0 - 16u * below);
+    if constexpr (B4) {
+        const uint32_t raw = lds_u32(code0 + 4u * below);
+        decode4(rep ? __byte_perm(raw, 0u, 0x0123u) : 0x44444444u, m, h);
+    } else {
+        float x[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] = 0.f;
+        if (rep) {
+            const int b = bits, R = 1 << (b - 1);
+            const uint32_t o = code0 + (uint32_t)b * below;
+            uint64_t acc = 0;
+            for (int i = 0; i < b; ++i)
+                acc = (acc << 8) | (lds_u32((o + i) & ~3u) >> (8 * ((o + i) & 3u)) & 0xffu);
+            const uint32_t c7u = (uint32_t)(acc & ((1ull << (b - 1)) - 1));
+            acc >>= (b - 1);
+            uint32_t u[7], par = 0;
+#pragma unroll
+            for (int i = 6; i >= 0; --i) {
+                u[i] = (uint32_t)(acc & ((1ull << b) - 1));
+                par ^= u[i];
+                acc >>= b;
+            }
+            const uint32_t base = 0x4A800000u | (uint32_t)(acc & 1u);
+            const float bias = 4194304.0f + (float)R;
+#pragma unroll
+            for (int i = 0; i < 7; ++i) x[i] = (__int_as_float((u[i] << 1) | base) - bias) * m.fk;
+            x[7] = (__int_as_float(((2u * c7u + (par & 1u)) << 1) | base) - bias) * m.fk;
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r) h[r] = pack_half2(x[blk_ch(r, 0)], x[blk_ch(r, 1)]);
+    }
+    h[0] |= fv.x;
+    h[1] |= fv.y;
+    h[2] |= fv.z;
+    h[3] |= fv.w;
 }
 
 template <int G, int QDT, bool B4>
@@ -660,21 +729,22 @@ __global__ void __launch_bounds__(kMThreads, 2) attn_compact_mma_kernel(CompactA
     const uint32_t hb0 = head * a.bph;
     const MUnit mk = make_unit(a.k.scales[head]), mv = make_unit(a.v.scales[head]);
 
-    // q as the B operand of phase K: lane (g, t) holds q[h] at channels
-    // 32 ks + 8 t + 4 j + {0, 1} and {2, 3}, h = g % 4, j = g / 4
+    // q as the B operand of phase K.  A k-step's A registers (a0..a3) are the
+    // four registers of block 4 ks + t, so A column pair (2t, 2t+1) of row
+    // half j holds register j's channels, pair (2t+8, 2t+9) register 2 + j's;
+    // lane (g, t) of B (column g = head h + 4 j) holds q[h] at those channels.
     uint32_t qb[4][2];
     {
         const uint32_t h = g & 3u, j = g >> 2;
         const int64_t row = ((int64_t)b * a.n_kv_heads + kvh) * G + h;
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks) {
-            float qv[4] = {0.f, 0.f, 0.f, 0.f};
-            if (h < (uint32_t)G) {
+            float qv[8];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) qv[i] = Elem<QDT>::load(a.q, row * D + 32 * ks + 8 * t + 4 * j + i);
-            }
-            qb[ks][0] = pack_half2(qv[0], qv[1]);
-            qb[ks][1] = pack_half2(qv[2], qv[3]);
+            for (int i = 0; i < 8; ++i)
+                qv[i] = h < (uint32_t)G ? Elem<QDT>::load(a.q, row * D + 8 * (4 * ks + t) + i) : 0.f;
+            qb[ks][0] = j ? pack_half2(qv[blk_ch(1, 0)], qv[blk_ch(1, 1)]) : pack_half2(qv[blk_ch(0, 0)], qv[blk_ch(0, 1)]);
+            qb[ks][1] = j ? pack_half2(qv[blk_ch(3, 0)], qv[blk_ch(3, 1)]) : pack_half2(qv[blk_ch(2, 0)], qv[blk_ch(2, 1)]);
         }
     }
 
@@ -689,6 +759,7 @@ __global__ void __launch_bounds__(kMThreads, 2) attn_compact_mma_kernel(CompactA
         }
     }
     if (threadIdx.x < kMRing) sts_v4(bufs + threadIdx.x * S::kBytes + S::kZeroOff, make_uint4(0, 0, 0, 0));
+    __shared__ uint32_t s_dirty[kMRing];  // per ring slot: the stage's index did not chain
     __syncthreads();
 
     // the stages of both phases stream through a ring of kMRing buffers: K
@@ -697,6 +768,7 @@ __global__ void __launch_bounds__(kMThreads, 2) attn_compact_mma_kernel(CompactA
     auto issue = [&](uint32_t q) {
         if (q < n_seq) {
             const uint32_t ph = q >= nst, st = q - ph * nst;
+            if (threadIdx.x == 0) s_dirty[q % kMRing] = 0u;
             mstage_issue<B4>(ph ? a.v : a.k, spans[ph][st], stage_b0(st), bufs + (q % kMRing) * S::kBytes);
         } else {
             cp_async_commit();
@@ -731,8 +803,10 @@ __global__ void __launch_bounds__(kMThreads, 2) attn_compact_mma_kernel(CompactA
         for (uint32_t i = threadIdx.x; i < s.nw && !s.bad; i += blockDim.x) {
             const uint32_t ri = lds_u32(buf + S::kRanksOff + 4 * i);
             const uint32_t rn = i + 1 < s.nw ? lds_u32(buf + S::kRanksOff + 4 * (i + 1)) : s.r1;
-            if (rn - ri != (uint32_t)__popc(lds_u32(buf + S::kWordsOff + 4 * i)) || (i == 0 && ri != s.r0))
+            if (rn - ri != (uint32_t)__popc(lds_u32(buf + S::kWordsOff + 4 * i)) || (i == 0 && ri != s.r0)) {
                 raise_flag(a.err, LQ_EF_BITSTREAM);
+                s_dirty[q % kMRing] = 1u;
+            }
         }
         mstage_rescale<B4>(s, buf, ph ? mv.inv_u : mk.inv_u);
         if (ph == 1 && st == 0) {
@@ -774,21 +848,42 @@ __global__ void __launch_bounds__(kMThreads, 2) attn_compact_mma_kernel(CompactA
 
         const uint32_t tw = st * kMStageTok + (uint32_t)warp * 16;  // the warp's first token, CTA-relative
         const uint32_t b0 = stage_b0(st);
-        if (ph == 0) {
-            // ---- phase K: two groups of 8 tokens, four k-steps of 4 blocks each
+        const uint32_t nrep = s.r1 - s.r0;
+        // a full stage whose index chained and whose fallback rows all fit the
+        // buffer takes the unchecked block decode
+        const bool fast = !s.bad && s_dirty[q % kMRing] == 0u && s.nw == (uint32_t)MStage<B4>::kWords &&
+                          32u * s.nw - nrep <= (uint32_t)kMFbCap;
+        const int bits = c.bits;
+        const uint32_t code_base = buf + S::kPackedOff + (s.r0 * (uint32_t)bits - s.a0);
+        const uint32_t zero = buf + S::kZeroOff;
+        // word wi of the stage: its mask word and its representable blocks before it
+        auto word = [&](uint32_t wi, bool live, uint32_t &wd, uint32_t &rk) {
+            wd = live ? lds_u32(buf + S::kWordsOff + 4 * wi) : 0u;
+            rk = live ? lds_u32(buf + S::kRanksOff + 4 * wi) - s.r0 : 0u;
+        };
+        auto blockv = [&](auto fast_tag, uint32_t wd, uint32_t rk, uint32_t wi, uint32_t bit, bool live,
+                          const MUnit &m, uint32_t h[4]) {
+            if constexpr (decltype(fast_tag)::value)
+                mblock_fast<B4>(bits, code_base + (uint32_t)bits * rk,
+                                buf + S::kFbOff + 16u * (32u * wi + bit - rk), zero, wd, (1u << bit) - 1u, m, h);
+            else
+                mblock<B4>(c, s, buf, b0, wd, rk, wi, bit, live, m, h);
+        };
+        auto phase_k = [&](auto fast_tag) {
+            // two groups of 8 tokens, four k-steps of 4 blocks each
 #pragma unroll
             for (int grp = 0; grp < 2; ++grp) {
                 const uint32_t tok = tw + 8u * grp + g;  // this lane's token
                 const bool live = T0 + tok < T1;
                 const uint32_t wi = (tok - st * kMStageTok) >> 1;  // its word in the stage
-                const uint32_t wd = live ? lds_u32(buf + S::kWordsOff + 4 * wi) : 0u;
-                const uint32_t rk = live ? lds_u32(buf + S::kRanksOff + 4 * wi) - s.r0 : 0u;
+                uint32_t wd, rk;
+                word(wi, live, wd, rk);
                 float d[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                 for (int ks = 0; ks < 4; ++ks) {
                     uint32_t h[4];
-                    mblock<B4>(c, s, buf, b0, wd, rk, wi, 16u * (g & 1u) + 4u * ks + t, live, mk, h);
-                    mma_16816(d, h[0], h[2], h[1], h[3], qb[ks][0], qb[ks][1]);
+                    blockv(fast_tag, wd, rk, wi, 16u * (g & 1u) + 4u * ks + t, live, mk, h);
+                    mma_16816(d, h[0], h[1], h[2], h[3], qb[ks][0], qb[ks][1]);
                 }
                 float v0 = t < 2 ? d[0] : d[2], v1 = t < 2 ? d[1] : d[3];
                 v0 += __shfl_xor_sync(0xffffffffu, v0, 2);
@@ -799,21 +894,22 @@ __global__ void __launch_bounds__(kMThreads, 2) attn_compact_mma_kernel(CompactA
                     row[1] = v1 * fk_score;
                 }
             }
-        } else {
-            // ---- phase V: one group of 16 tokens; lane (g, t) holds blocks 2g, 2g+1
-            // of tokens 2t, 2t+1 (word t of the group) and 2t+8, 2t+9 (word 4 + t)
+        };
+        auto phase_v = [&](auto fast_tag) {
+            // one group of 16 tokens; lane (g, t) holds blocks 2g, 2g+1 of tokens
+            // 2t, 2t+1 (word t of the group) and 2t+8, 2t+9 (word 4 + t)
             uint32_t R[8][4];
 #pragma unroll
             for (int hw = 0; hw < 2; ++hw) {
                 const uint32_t tok = tw + 8u * hw + 2u * t;  // first of the word's two tokens
                 const bool live = T0 + tok < T1;
                 const uint32_t wi = (tok - st * kMStageTok) >> 1;
-                const uint32_t wd = live ? lds_u32(buf + S::kWordsOff + 4 * wi) : 0u;
-                const uint32_t rk = live ? lds_u32(buf + S::kRanksOff + 4 * wi) - s.r0 : 0u;
-                mblock<B4>(c, s, buf, b0, wd, rk, wi, 2u * g, live, mv, R[4 * hw + 0]);
-                mblock<B4>(c, s, buf, b0, wd, rk, wi, 2u * g + 1u, live, mv, R[4 * hw + 1]);
-                mblock<B4>(c, s, buf, b0, wd, rk, wi, 16u + 2u * g, live, mv, R[4 * hw + 2]);
-                mblock<B4>(c, s, buf, b0, wd, rk, wi, 17u + 2u * g, live, mv, R[4 * hw + 3]);
+                uint32_t wd, rk;
+                word(wi, live, wd, rk);
+                blockv(fast_tag, wd, rk, wi, 2u * g, live, mv, R[4 * hw + 0]);
+                blockv(fast_tag, wd, rk, wi, 2u * g + 1u, live, mv, R[4 * hw + 1]);
+                blockv(fast_tag, wd, rk, wi, 16u + 2u * g, live, mv, R[4 * hw + 2]);
+                blockv(fast_tag, wd, rk, wi, 17u + 2u * g, live, mv, R[4 * hw + 3]);
             }
             // p^T as the B operand: (p[g][2t], p[g][2t+1]) and (p[g][2t+8], p[g][2t+9])
             uint32_t pb0 = 0u, pb1 = 0u;
@@ -826,12 +922,20 @@ __global__ void __launch_bounds__(kMThreads, 2) attn_compact_mma_kernel(CompactA
                 pb0 = pack_half2(pa, pbv);
                 pb1 = pack_half2(pc, pd);
             }
+            // m-tile j: output rows 16g + ch and 16g + 8 + ch, ch = blk_ch(j / 2, j % 2)
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
                 const uint32_t sel = (j & 1) ? 0x7632u : 0x5410u, i = j >> 1;
                 mma_16816(acc[j], __byte_perm(R[0][i], R[2][i], sel), __byte_perm(R[1][i], R[3][i], sel),
                           __byte_perm(R[4][i], R[6][i], sel), __byte_perm(R[5][i], R[7][i], sel), pb0, pb1);
             }
+        };
+        if (ph == 0) {
+            if (fast) phase_k(std::true_type{});
+            else phase_k(std::false_type{});
+        } else {
+            if (fast) phase_v(std::true_type{});
+            else phase_v(std::false_type{});
         }
     }
     cp_async_wait<0>();
@@ -848,8 +952,9 @@ __global__ void __launch_bounds__(kMThreads, 2) attn_compact_mma_kernel(CompactA
                 float *o = mrg + (warp * G + hh) * rs;
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
-                    o[16 * g + j] = acc[j][e] * mv.u;
-                    o[16 * g + 8 + j] = acc[j][2 + e] * mv.u;
+                    const int ch = blk_ch(j >> 1, j & 1);
+                    o[16 * g + ch] = acc[j][e] * mv.u;
+                    o[16 * g + 8 + ch] = acc[j][2 + e] * mv.u;
                 }
             }
         }

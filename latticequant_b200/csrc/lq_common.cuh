@@ -344,23 +344,30 @@ __device__ __forceinline__ void d8_nearest_pair(const float x[8], const float y[
     d8_flip(s2, c2, res2, r2);
 }
 
-// E8 nearest point (core/e8_quantizer.py:61-83).  The two squared-distance
-// sums run left to right as the two halves of packed fp32x2 operations.
+// The squared distance sum((x - c) ** 2) left to right, each product and
+// each sum rounded on its own.  __fmul_rn / __fadd_rn are never contracted
+// into an FMA; a fused square-and-add rounds once instead of twice and
+// decides exact ties of dist1 and dist2 the other way (seen at full chunk
+// size: a few blocks per million).
+__device__ __forceinline__ float e8_dist(const float x[8], const float c[8]) {
+    float d = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float e = __fsub_rn(x[i], c[i]);
+        d = i ? __fadd_rn(d, __fmul_rn(e, e)) : __fmul_rn(e, e);  // 0 + v == v exactly
+    }
+    return d;
+}
+
+// E8 nearest point (core/e8_quantizer.py:61-83).
 __device__ __forceinline__ void e8_nearest(const float x[8], float q[8]) {
     float c1[8], y[8], c2[8], res1[8], res2[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) y[i] = __fsub_rn(x[i], 0.5f);
     d8_nearest_pair(x, y, c1, c2, res1, res2);
-    unsigned long long d = 0;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        c2[i] = __fadd_rn(c2[i], 0.5f);
-        const unsigned long long e = f2_pack(__fsub_rn(x[i], c1[i]), __fsub_rn(x[i], c2[i]));
-        const unsigned long long e2 = f2_mul(e, e);
-        d = i ? f2_add(d, e2) : e2;  // 0 + v == v exactly
-    }
-    float d1, d2;
-    f2_unpack(d, d1, d2);
+    for (int i = 0; i < 8; ++i) c2[i] = __fadd_rn(c2[i], 0.5f);
+    const float d1 = e8_dist(x, c1), d2 = e8_dist(x, c2);
     const bool use1 = d1 <= d2;
 #pragma unroll
     for (int i = 0; i < 8; ++i) q[i] = use1 ? c1[i] : c2[i];
@@ -378,17 +385,10 @@ __device__ __forceinline__ int e8_nearest_symbols(const float x[8], float q[8], 
 #pragma unroll
     for (int i = 0; i < 8; ++i) y[i] = __fsub_rn(x[i], 0.5f);
     d8_nearest_pair(x, y, c1, c2, res1, res2);
-    unsigned long long d = 0;
     float h[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        h[i] = __fadd_rn(c2[i], 0.5f);  // the half-coset point, as the reference forms it
-        const unsigned long long e = f2_pack(__fsub_rn(x[i], c1[i]), __fsub_rn(x[i], h[i]));
-        const unsigned long long e2 = f2_mul(e, e);
-        d = i ? f2_add(d, e2) : e2;
-    }
-    float d1, d2;
-    f2_unpack(d, d1, d2);
+    for (int i = 0; i < 8; ++i) h[i] = __fadd_rn(c2[i], 0.5f);  // the half-coset point, as the reference forms it
+    const float d1 = e8_dist(x, c1), d2 = e8_dist(x, h);
     *finite = isfinite(d1) && isfinite(d2);
     const bool use1 = d1 <= d2;
 #pragma unroll

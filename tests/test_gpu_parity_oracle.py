@@ -209,12 +209,12 @@ def test_compressed_attention_tails_match_oracle():
     vv = [oracle_fp16_values(v0)] + [oracle_fp16_values(torch.cat(toks_v[i * T:(i + 1) * T], 2)
                                                         .reshape(B, H * T, 1, D)).reshape(B, H, T, D)
                                      for i in range(2)]
-    open_k = torch.cat(toks_k[2 * T:], 2)
-    open_v = torch.cat(toks_v[2 * T:], 2)
-    kk.append(_oracle_update_values(open_k, 4)[0].view(np.int16))
-    vv.append(_oracle_update_values(open_v, 4)[0].view(np.int16))
-    kk[-1] = torch.from_numpy(kk[-1]).view(torch.bfloat16).double().numpy()
-    vv[-1] = torch.from_numpy(vv[-1]).view(torch.bfloat16).double().numpy()
+    # the open tail: each token as its own update() quantised it (a scale per token, fp32)
+    n_open = steps - 2 * T
+    for toks, dst in ((toks_k, kk), (toks_v, vv)):
+        per_tok = torch.cat(toks[2 * T:], 2).reshape(B, H * n_open, 1, D)
+        bits = _oracle_update_values(per_tok, 4)[0].reshape(B, H, n_open, D)
+        dst.append(torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16).double().numpy())
     K = np.concatenate(kk, 2)
     V = np.concatenate(vv, 2)
     gq = torch.Generator().manual_seed(10)
@@ -245,7 +245,10 @@ def test_outlier_chunk_matches_oracle_lattice():
     assert np.array_equal(_u32(ch.scale_f32), s32.view(np.uint32))
     q, cos, osym, _ = O.quantize_chunk(xn, O.DT_BF16, n_heads, bph, s32)
     sc = s16.view(np.float16).astype(np.float32)
-    want = (q.reshape(n_heads, bph, 8) * sc[:, None, None]).reshape(-1)
+    # decoded values come from the symbols (symbols_to_e8, so zeros are +0)
+    qs = O.symbols_to_e8(cos, osym)
+    assert np.array_equal(qs, q)  # equal as numbers (q may hold -0)
+    want = (qs.reshape(n_heads, bph, 8) * sc[:, None, None]).reshape(-1)
     assert np.array_equal(_u32(out).reshape(-1), want.view(np.uint32))
     assert np.array_equal(sym.cpu().numpy(), osym)
     rec = ch.outlier_rec.cpu().numpy()
