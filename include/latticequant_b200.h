@@ -48,6 +48,7 @@ extern "C" {
 #define LQ_EF_BITSTREAM 0x8u  /* lane metadata points outside the word buffer */
 #define LQ_EF_NONFINITE 0x10u /* non-finite input or scaled input */
 #define LQ_EF_NOCONVERGE 0x20u /* table normalisation did not converge */
+#define LQ_EF_TIMEOUT 0x40u    /* a bulk copy into shared memory did not complete within a second */
 
 /* ---- dtypes ---- */
 #define LQ_F32 0
@@ -243,7 +244,18 @@ typedef struct lq_chunk_view {
     const uint32_t *dec_tab;
     const uint16_t *scale_f16;
     int64_t n_heads, bph, tile_blocks;
+    /* optional (may be NULL): the chunk's 16 decode tables in the kernels'
+     * shared-memory form, from lq_stage_tables, 16-byte aligned; with it each
+     * CTA fills its table region with one bulk copy (cp.async.bulk) instead of
+     * loading and converting the tables thread by thread */
+    const uint32_t *staged_tab;
 } lq_chunk_view;
+
+/* The decode tables of n_tables streams (lq_expand_tables' dec_tab, with the
+ * streams' tab_lo) in the shared-memory form lq_attn_decode copies in bulk:
+ *   staged [n_tables][LQ_L] u32 (a chunk's 16 tables are 64 KB)
+ * No reference counterpart (the reference keeps numpy tables on the host). */
+int lq_stage_tables(const uint32_t *dec_tab, const int32_t *tab_lo, int64_t n_tables, uint32_t *staged, void *stream);
 
 size_t lq_attn_decode_workspace(int64_t n_heads, int64_t bph, int64_t tile_blocks, int group, int head_dim);
 int lq_attn_decode(const lq_chunk_view *k, const lq_chunk_view *v, const void *q, int q_dtype, int64_t batch,

@@ -19,6 +19,7 @@ LIB_PATH = os.path.join(HERE, "liblq_b200.so")
 LQ_OK = 0
 LQ_ERR_INVALID, LQ_ERR_ALPHABET, LQ_ERR_CAPACITY, LQ_ERR_CUDA, LQ_ERR_STREAM = -1, -2, -3, -4, -5
 EF_ALPHABET, EF_SYMRANGE, EF_CAPACITY, EF_BITSTREAM, EF_NONFINITE, EF_NOCONVERGE = 0x1, 0x2, 0x4, 0x8, 0x10, 0x20
+EF_TIMEOUT = 0x40
 LQ_F32, LQ_F16, LQ_BF16 = 0, 1, 2
 L = 1024
 SYM_LIMIT = 512
@@ -32,6 +33,7 @@ _FLAG_TEXT = {
     EF_BITSTREAM: "corrupt bitstream or lane metadata",
     EF_NONFINITE: "non-finite value in the input or in input/scale",
     EF_NOCONVERGE: "rANS frequency normalisation did not converge",
+    EF_TIMEOUT: "a bulk copy into shared memory did not complete within a second",
 }
 
 _lib = None
@@ -50,7 +52,8 @@ class ChunkView(ctypes.Structure):
                 ("coset_words", ctypes.c_void_p), ("tile_n0", ctypes.c_void_p),
                 ("tab_lo", ctypes.c_void_p), ("tab_nsym", ctypes.c_void_p), ("tab_freq", ctypes.c_void_p),
                 ("dec_tab", ctypes.c_void_p), ("scale_f16", ctypes.c_void_p),
-                ("n_heads", ctypes.c_int64), ("bph", ctypes.c_int64), ("tile_blocks", ctypes.c_int64)]
+                ("n_heads", ctypes.c_int64), ("bph", ctypes.c_int64), ("tile_blocks", ctypes.c_int64),
+                ("staged_tab", ctypes.c_void_p)]
 
 
 class CompactView(ctypes.Structure):
@@ -89,6 +92,7 @@ def _declare(lib):
                             i32, f32, vp, i32, vp, vp, vp, sz, vp, vp], i32),
         "lq_attn_merge": ([vp, vp, i64, i64, i32, vp, i32, vp, vp], i32),
         "lq_attn_merge_packed": ([vp, i64, i64, i32, vp, i32, vp, vp], i32),
+        "lq_stage_tables": ([vp, vp, i64, vp, vp], i32),
         "lq_attn_compact_workspace": ([i64, i64, i32, i32], sz),
         "lq_attn_decode_compact": ([ctypes.POINTER(CompactView), ctypes.POINTER(CompactView), vp, i32, i64, i64, i64,
                                     i32, i32, f32, vp, i32, vp, vp, sz, vp, vp], i32),

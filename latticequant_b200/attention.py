@@ -20,7 +20,7 @@ import torch
 
 from . import _lib
 from ._lib import ChunkView, check, lib, ptr, raise_flags, stream_handle
-from .codec import LaneChunk, decompress, expand_dec_tables
+from .codec import LaneChunk, decompress, expand_dec_tables, staged_tables
 
 
 def chunk_view(chunk: LaneChunk) -> ChunkView:
@@ -45,6 +45,7 @@ def chunk_view(chunk: LaneChunk) -> ChunkView:
     v.n_heads = g.n_heads
     v.bph = g.bph
     v.tile_blocks = g.tile_blocks
+    v.staged_tab = staged_tables(chunk).data_ptr()
     return v
 
 

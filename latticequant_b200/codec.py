@@ -371,6 +371,21 @@ def expand_dec_tables(chunk: LaneChunk) -> torch.Tensor:
     return chunk.dec_tab
 
 
+def staged_tables(chunk: LaneChunk) -> torch.Tensor:
+    """The chunk's decode tables in the attention kernel's shared-memory form
+    (lq_stage_tables, 64 KB per chunk), so each CTA fills its table region with
+    one bulk copy.  Cached on the chunk."""
+    st = getattr(chunk, "_staged_tab", None)
+    if st is None:
+        dec = expand_dec_tables(chunk)
+        n_tab = chunk.tab_nsym.numel()
+        st = torch.empty(n_tab * L, dtype=torch.int32, device=dec.device)
+        check(lib().lq_stage_tables(ptr(dec), ptr(chunk.tab_lo), n_tab, ptr(st), stream_handle(dec.device)),
+              "lq_stage_tables")
+        chunk._staged_tab = st
+    return st
+
+
 def decompress(chunk: LaneChunk, out_dtype: Optional[torch.dtype] = None, want_symbols: bool = False):
     """Decode a LaneChunk to a tensor of its original shape (dtype out_dtype or the original)."""
     g = chunk.geom

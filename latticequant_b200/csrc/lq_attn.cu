@@ -62,6 +62,18 @@ __host__ __device__ constexpr int attn_threads() {
 // does); attn_redo_kernel then recomputes those CTAs with CHECKED = true.
 // Keeping the exact decode out of the main kernel keeps that kernel to one
 // copy of the decoder and within its registers.
+// The 16 tables of a chunk in their shared-memory form (smem_entry), so a
+// CTA can fill its table region with one bulk copy.
+__global__ void staged_tables_kernel(const uint32_t *__restrict__ dec_tab, const int32_t *__restrict__ tab_lo,
+                                     uint32_t n_tables, uint32_t *__restrict__ out) {
+    const uint32_t t = blockIdx.x;  // table
+    if (t >= n_tables) return;
+    const int s = (int)(t % LQ_NSTREAMS);
+    const int lo = tab_lo[t], c = s >> 3, mul = (s & 7) == 7 ? 4 : 2;
+    for (uint32_t i = threadIdx.x; i < LQ_L; i += blockDim.x)
+        out[(size_t)t * LQ_L + i] = smem_entry(dec_tab[(size_t)t * LQ_L + i], lo, c, mul);
+}
+
 template <int G, int BPT, int QDT, bool CHECKED>
 __device__ __forceinline__ void attn_partial_cta(const AttnArgs &a, uint32_t cx, uint32_t head) {
     static_assert(BPT == 8 || BPT == 16, "head_dim 64 or 128");
@@ -107,9 +119,21 @@ __device__ __forceinline__ void attn_partial_cta(const AttnArgs &a, uint32_t cx,
     // ---- phase K: scores
     // set when a lane of the CTA read past its bits (optimistic decode only)
     __shared__ uint32_t s_overrun;
-    if (threadIdx.x == 0) s_overrun = 0u;
-    stage_tables(a.k, 0, dtab);
+    __shared__ __align__(8) uint64_t s_tab_bar;  // completion of the bulk table copies (K: phase 0, V: phase 1)
+    const uint32_t tbar = smem_addr(&s_tab_bar);
+    const bool bulk = a.k.staged_tab != nullptr && a.v.staged_tab != nullptr;
+    if (threadIdx.x == 0) {
+        s_overrun = 0u;
+        if (bulk) {
+            mbar_init(tbar, 1);
+            bulk_load(dta, a.k.staged_tab, (uint32_t)kTablesSmem, tbar);
+        }
+    }
+    if (!bulk) stage_tables(a.k, 0, dtab);
     __syncthreads();
+    // a copy that never completes leaves the flag raised and stale tables:
+    // every table index is masked, so stale entries give wrong values only
+    if (bulk) mbar_wait(tbar, 0, a.err);
     if (wact) {
         auto epi_k = [&](bool ok, int t, uint32_t grp, uint32_t j, uint32_t cc, const uint4 blk) {
             float kq[8];
@@ -231,8 +255,13 @@ __device__ __forceinline__ void attn_partial_cta(const AttnArgs &a, uint32_t cx,
 
     // ---- phase V: p * v accumulated per lane over its 8 channels
     __syncthreads();  // every warp is done with the K tables
-    stage_tables(a.v, 0, dtab);
-    __syncthreads();
+    if (bulk) {
+        if (threadIdx.x == 0) bulk_load(dta, a.v.staged_tab, (uint32_t)kTablesSmem, tbar);
+        mbar_wait(tbar, 1, a.err);
+    } else {
+        stage_tables(a.v, 0, dtab);
+        __syncthreads();
+    }
     // p * v accumulated as packed channel pairs (i, i+1) per head
     unsigned long long acc2[G][4];
 #pragma unroll
@@ -415,7 +444,8 @@ int launch_partial_g(const AttnArgs &a, const AttnPlan &p, uint32_t n_heads, int
 
 bool view_ok(const lq_chunk_view *c) {
     return c && c->lane_off && c->lane_nbits && c->lane_state && c->coset_words && c->tile_n0 && c->tab_lo &&
-           c->tab_nsym && c->tab_freq && c->dec_tab && c->scale_f16 && c->n_words >= 0 && (c->n_words == 0 || c->words);
+           c->tab_nsym && c->tab_freq && c->dec_tab && c->scale_f16 && c->n_words >= 0 &&
+           (c->n_words == 0 || c->words) && (reinterpret_cast<uintptr_t>(c->staged_tab) & 15) == 0;
 }
 
 ChunkDev to_dev(const lq_chunk_view *c) {
@@ -423,7 +453,8 @@ ChunkDev to_dev(const lq_chunk_view *c) {
     return ChunkDev{c->words,        (uint32_t)c->n_words, c->lane_off,          c->lane_nbits,
                     c->lane_state,   c->coset_words,       c->tile_n0,           (uint32_t)c->n_heads,
                     (uint32_t)c->bph, (uint32_t)c->tile_blocks, (uint32_t)ceil_div(N, c->tile_blocks), c->tab_lo,
-                    c->tab_nsym,     c->tab_freq,          c->dec_tab,           c->scale_f16};
+                    c->tab_nsym,     c->tab_freq,          c->dec_tab,           c->scale_f16,
+                    c->staged_tab};
 }
 
 }  // namespace
@@ -497,3 +528,12 @@ extern "C" int lq_attn_decode(const lq_chunk_view *k, const lq_chunk_view *v, co
     return launch_attn_combine(part, rows, hkv, G, D, p.nct, out, out_dtype, lse, st);
 }
 
+
+extern "C" int lq_stage_tables(const uint32_t *dec_tab, const int32_t *tab_lo, int64_t n_tables, uint32_t *staged,
+                               void *stream) {
+    if (n_tables < 0 || n_tables > 0x7fffffff) return LQ_ERR_INVALID;
+    if (n_tables == 0) return LQ_OK;
+    if (!dec_tab || !tab_lo || !staged || (reinterpret_cast<uintptr_t>(staged) & 15)) return LQ_ERR_INVALID;
+    staged_tables_kernel<<<(unsigned)n_tables, 256, 0, as_stream(stream)>>>(dec_tab, tab_lo, (uint32_t)n_tables, staged);
+    return check_launch();
+}

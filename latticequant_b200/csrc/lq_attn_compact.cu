@@ -532,21 +532,33 @@ __device__ __forceinline__ MUnit make_unit(float s) {
 }
 
 // All threads: copy one stage (mask words, ranks, codes, at most kMFbCap
-// fallback rows) into shared memory at `buf` and commit the group.
+// fallback rows) into shared memory at `buf` and commit the group.  Every
+// copy loop has a fixed trip count (predicated copies, no divergent loops).
 template <bool B4>
 __device__ __forceinline__ void mstage_issue(const CompactDev &c, const CStageSpan &s, uint32_t b0, uint32_t buf) {
     using S = MStage<B4>;
+    static_assert(S::kWords <= kMThreads, "one mask word per thread");
     if (!s.bad) {
-        for (uint32_t i = threadIdx.x; i < s.nw; i += blockDim.x) {
-            cp_async4(buf + S::kWordsOff + 4 * i, c.mask_words + s.w0 + i);
-            cp_async4(buf + S::kRanksOff + 4 * i, c.word_rank + s.w0 + i);
+        const uint32_t tid = threadIdx.x;
+        if (tid < s.nw) {
+            cp_async4(buf + S::kWordsOff + 4 * tid, c.mask_words + s.w0 + tid);
+            cp_async4(buf + S::kRanksOff + 4 * tid, c.word_rank + s.w0 + tid);
         }
-        const uint32_t total = c.n_repr * (uint32_t)c.bits, a1 = s.r1 * (uint32_t)c.bits;
-        for (uint32_t off = s.a0 + 16u * threadIdx.x; off < a1; off += 16u * blockDim.x)
-            cp_async16(buf + S::kPackedOff + (off - s.a0), c.packed + off, min(16u, total - off));
+        const uint32_t bits = B4 ? 4u : (uint32_t)c.bits;
+        const uint32_t total = c.n_repr * bits, a1 = s.r1 * bits;
+        constexpr int kCodeIters = (S::kPacked / 16 + kMThreads - 1) / kMThreads;
+#pragma unroll
+        for (int it = 0; it < kCodeIters; ++it) {
+            const uint32_t off = s.a0 + 16u * (tid + (uint32_t)it * kMThreads);
+            if (off < a1) cp_async16(buf + S::kPackedOff + (off - s.a0), c.packed + off, min(16u, total - off));
+        }
         const uint32_t f0 = b0 - s.r0, nf = min(32u * s.nw - (s.r1 - s.r0), (uint32_t)kMFbCap);
-        for (uint32_t r = threadIdx.x; r < nf; r += blockDim.x)
-            cp_async16(buf + S::kFbOff + 16u * r, c.fallback + f0 + r, 16u);
+        constexpr int kFbIters = (kMFbCap + kMThreads - 1) / kMThreads;
+#pragma unroll
+        for (int it = 0; it < kFbIters; ++it) {
+            const uint32_t r = tid + (uint32_t)it * kMThreads;
+            if (r < nf) cp_async16(buf + S::kFbOff + 16u * r, c.fallback + f0 + r, 16u);
+        }
     }
     cp_async_commit();
 }
@@ -580,8 +592,12 @@ __device__ __forceinline__ void mstage_rescale(const CStageSpan &s, uint32_t buf
     using S = MStage<B4>;
     if (s.bad) return;
     const uint32_t nf = min(32u * s.nw - (s.r1 - s.r0), (uint32_t)kMFbCap);
-    for (uint32_t r = threadIdx.x; r < nf; r += blockDim.x)
-        sts_v4(buf + S::kFbOff + 16u * r, row_to_regs(lds_v4(buf + S::kFbOff + 16u * r), inv_u));
+    constexpr int kIters = (kMFbCap + kMThreads - 1) / kMThreads;
+#pragma unroll
+    for (int it = 0; it < kIters; ++it) {
+        const uint32_t r = threadIdx.x + (uint32_t)it * kMThreads;
+        if (r < nf) sts_v4(buf + S::kFbOff + 16u * r, row_to_regs(lds_v4(buf + S::kFbOff + 16u * r), inv_u));
+    }
 }
 
 // A 4-bit code as the four registers: v = the big-endian code word,
@@ -666,17 +682,17 @@ __device__ __forceinline__ void mblock(const CompactDev &c, const CStageSpan &s,
 
 // mblock for a stage that is full (every token in range), whose index
 // chained on arrival and whose fallback rows are all staged: no range
-// checks.  code0: shared address of the word's first code; fb0: of the
-// fallback row the block would have if no block before it in its word were
-// representable; lowmask: the word's bits below the block's.
+// checks.  cw: shared address of the first code of the block's word; fw:
+// of the fallback row the block would have if no block before it in its
+// word were representable; lowmask: the word's bits below the block's.
 template <bool B4>
-__device__ __forceinline__ void mblock_fast(int bits, uint32_t code0, uint32_t fb0, uint32_t zero, uint32_t wd,
+__device__ __forceinline__ void mblock_fast(int bits, uint32_t cw, uint32_t fw, uint32_t zero, uint32_t wd,
                                             uint32_t lowmask, const MUnit &m, uint32_t h[4]) {
     const uint32_t below = __popc(wd & lowmask);
     const bool rep = (wd & (lowmask + 1u)) != 0u;
-    const uint4 fv = lds_v4(rep ? zero : fb0 - 16u * below);
+    const uint4 fv = lds_v4(rep ? zero : fw - 16u * below);
     if constexpr (B4) {
-        const uint32_t raw = lds_u32(code0 + 4u * below);
+        const uint32_t raw = lds_u32(cw + 4u * below);
         decode4(rep ? __byte_perm(raw, 0u, 0x0123u) : 0x44444444u, m, h);
     } else {
         float x[8];
@@ -684,7 +700,7 @@ __device__ __forceinline__ void mblock_fast(int bits, uint32_t code0, uint32_t f
         for (int i = 0; i < 8; ++i) x[i] = 0.f;
         if (rep) {
             const int b = bits, R = 1 << (b - 1);
-            const uint32_t o = code0 + (uint32_t)b * below;
+            const uint32_t o = cw + (uint32_t)b * below;
             uint64_t acc = 0;
             for (int i = 0; i < b; ++i)
                 acc = (acc << 8) | (lds_u32((o + i) & ~3u) >> (8 * ((o + i) & 3u)) & 0xffu);
@@ -854,27 +870,30 @@ __global__ void __launch_bounds__(kMThreads, 2) attn_compact_mma_kernel(CompactA
         const bool fast = !s.bad && s_dirty[q % kMRing] == 0u && s.nw == (uint32_t)MStage<B4>::kWords &&
                           32u * s.nw - nrep <= (uint32_t)kMFbCap;
         const int bits = c.bits;
-        const uint32_t code_base = buf + S::kPackedOff + (s.r0 * (uint32_t)bits - s.a0);
+        const uint32_t code_base = buf + S::kPackedOff + (s.r0 * (B4 ? 4u : (uint32_t)bits) - s.a0);
         const uint32_t zero = buf + S::kZeroOff;
         // word wi of the stage: its mask word and its representable blocks before it
         auto word = [&](uint32_t wi, bool live, uint32_t &wd, uint32_t &rk) {
             wd = live ? lds_u32(buf + S::kWordsOff + 4 * wi) : 0u;
             rk = live ? lds_u32(buf + S::kRanksOff + 4 * wi) - s.r0 : 0u;
         };
+        const uint32_t cbits = B4 ? 4u : (uint32_t)bits;
         auto blockv = [&](auto fast_tag, uint32_t wd, uint32_t rk, uint32_t wi, uint32_t bit, bool live,
                           const MUnit &m, uint32_t h[4]) {
             if constexpr (decltype(fast_tag)::value)
-                mblock_fast<B4>(bits, code_base + (uint32_t)bits * rk,
-                                buf + S::kFbOff + 16u * (32u * wi + bit - rk), zero, wd, (1u << bit) - 1u, m, h);
+                // the word's code and fallback bases (the same for its blocks, hoisted by the compiler)
+                mblock_fast<B4>(bits, code_base + cbits * rk, buf + S::kFbOff + 16u * (32u * wi - rk) + 16u * bit,
+                                zero, wd, (1u << bit) - 1u, m, h);
             else
                 mblock<B4>(c, s, buf, b0, wd, rk, wi, bit, live, m, h);
         };
         auto phase_k = [&](auto fast_tag) {
+            constexpr bool kFull = decltype(fast_tag)::value;  // every token of the stage in range
             // two groups of 8 tokens, four k-steps of 4 blocks each
 #pragma unroll
             for (int grp = 0; grp < 2; ++grp) {
                 const uint32_t tok = tw + 8u * grp + g;  // this lane's token
-                const bool live = T0 + tok < T1;
+                const bool live = kFull || T0 + tok < T1;
                 const uint32_t wi = (tok - st * kMStageTok) >> 1;  // its word in the stage
                 uint32_t wd, rk;
                 word(wi, live, wd, rk);
@@ -896,13 +915,14 @@ __global__ void __launch_bounds__(kMThreads, 2) attn_compact_mma_kernel(CompactA
             }
         };
         auto phase_v = [&](auto fast_tag) {
+            constexpr bool kFull = decltype(fast_tag)::value;
             // one group of 16 tokens; lane (g, t) holds blocks 2g, 2g+1 of tokens
             // 2t, 2t+1 (word t of the group) and 2t+8, 2t+9 (word 4 + t)
             uint32_t R[8][4];
 #pragma unroll
             for (int hw = 0; hw < 2; ++hw) {
                 const uint32_t tok = tw + 8u * hw + 2u * t;  // first of the word's two tokens
-                const bool live = T0 + tok < T1;
+                const bool live = kFull || T0 + tok < T1;
                 const uint32_t wi = (tok - st * kMStageTok) >> 1;
                 uint32_t wd, rk;
                 word(wi, live, wd, rk);
@@ -915,10 +935,11 @@ __global__ void __launch_bounds__(kMThreads, 2) attn_compact_mma_kernel(CompactA
             uint32_t pb0 = 0u, pb1 = 0u;
             if (g < (uint32_t)G) {
                 const uint32_t ta = tw + 2u * t, tc = ta + 8u;
-                const float pa = T0 + ta < T1 ? sc[ta * GP + g] : 0.f;
-                const float pbv = T0 + ta < T1 ? sc[(ta + 1) * GP + g] : 0.f;
-                const float pc = T0 + tc < T1 ? sc[tc * GP + g] : 0.f;
-                const float pd = T0 + tc < T1 ? sc[(tc + 1) * GP + g] : 0.f;
+                const bool la = kFull || T0 + ta < T1, lc = kFull || T0 + tc < T1;
+                const float pa = la ? sc[ta * GP + g] : 0.f;
+                const float pbv = la ? sc[(ta + 1) * GP + g] : 0.f;
+                const float pc = lc ? sc[tc * GP + g] : 0.f;
+                const float pd = lc ? sc[(tc + 1) * GP + g] : 0.f;
                 pb0 = pack_half2(pa, pbv);
                 pb1 = pack_half2(pc, pd);
             }

@@ -57,6 +57,7 @@ struct ChunkDev {
     const uint16_t *tab_freq;
     const uint32_t *dec_tab;
     const uint16_t *scale_f16;
+    const uint32_t *staged_tab;  // optional: the tables in shared-memory form (staged_tables_kernel)
 };
 
 constexpr size_t kTablesSmem = (size_t)LQ_NSTREAMS * LQ_L * 4;
@@ -73,6 +74,44 @@ __device__ __forceinline__ uint32_t smem_entry(uint32_t e, int lo, int c, int mu
     const uint32_t si = e & 0x3ffu, k = (e >> 10) & 0xfu, xs = (e >> 14) >> k;
     const uint32_t v = (uint32_t)(((int)si + lo) * mul + c + 32768) & 0xffffu;
     return v | (xs << 16) | (k << 27);
+}
+
+// ---- bulk (TMA engine) copies into shared memory, completed on an mbarrier
+__device__ __forceinline__ void mbar_init(uint32_t mbar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(mbar), "r"(count) : "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// one thread: expect `bytes` on the barrier and copy them global -> shared
+// (both addresses 16-byte aligned, bytes a multiple of 16); no multicast
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t mbar) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // earlier generic reads of dst before the async write
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(mbar), "r"(bytes) : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(mbar)
+                 : "memory");
+}
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+// Wait for phase `parity` of the barrier, at most about a second; false
+// (with LQ_EF_TIMEOUT raised) if it did not complete.
+__device__ __forceinline__ bool mbar_wait(uint32_t mbar, uint32_t parity, uint32_t *err) {
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(mbar), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if (global_ns() - t0 > 1000000000ull) {
+            raise_flag(err, LQ_EF_TIMEOUT);
+            return false;
+        }
+    }
 }
 
 // all threads of the CTA: the chunk's 16 decode tables into shared memory

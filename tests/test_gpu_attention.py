@@ -166,3 +166,26 @@ def test_attention_rejects_bad_geometry():
         attention.decode_attention(torch.randn(1, 6, 64, device="cuda"), kc2, kc2)   # head_dim mismatch
     with pytest.raises(ValueError):
         attention.decode_attention(torch.randn(1, 7, 128, device="cuda"), kc2, kc2)  # 7 not a multiple of 2
+
+
+def test_bulk_staged_tables_match_per_thread_staging():
+    """The decode tables filled by one bulk copy (lq_stage_tables +
+    cp.async.bulk) give bit-identical attention to the per-thread staging."""
+    from latticequant_b200 import attention, codec
+
+    B, Hkv, G, S, D = 2, 2, 4, 512, 128
+    k = _kv((B, Hkv, S, D), 71, torch.bfloat16).cuda()
+    v = _kv((B, Hkv, S, D), 72, torch.bfloat16).cuda()
+    q = (torch.randn(B, Hkv * G, D, generator=torch.Generator().manual_seed(73)) / math.sqrt(D)).to(torch.bfloat16)
+    kc, _ = codec.compress(k, 4, tile_blocks=1024)
+    vc, _ = codec.compress(v, 4, tile_blocks=1024)
+    op = attention.DecodeAttention(kc, vc, G)
+    assert op.kv.staged_tab and op.vv.staged_tab
+    o1 = torch.empty(B, Hkv * G, D, dtype=torch.float32, device="cuda")
+    o2 = torch.empty_like(o1)
+    op(q.cuda(), o1)
+    op.kv.staged_tab = None
+    op.vv.staged_tab = None
+    op(q.cuda(), o2)
+    assert op.flags() == 0
+    assert torch.equal(o1, o2)
