@@ -1146,10 +1146,11 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         n_thr = os.cpu_count() or 1
-        v, blocks, dt = cpu_baseline(n_thr, sample_chunks=max(2, min(8, n_thr)), min_seconds=10.0)
+        n_smp = max(2, min(N_CHUNKS, n_thr))  # one chunk per host thread (the port threads over chunks)
+        v, blocks, dt = cpu_baseline(n_thr, sample_chunks=n_smp, min_seconds=10.0)
         cpu = {"value": v, "unit": UNIT, "cores": n_thr, "kind": "port",
-               "sample": f"{blocks} blocks ({max(2, min(8, n_thr))} config-2 chunks coded and decoded "
-                         f"{blocks // (max(2, min(8, n_thr)) * N_KV * BPH)} times), oracle/lq_oracle_codec.c on "
+               "sample": f"{blocks} blocks ({n_smp} config-2 chunks coded and decoded "
+                         f"{blocks // (n_smp * N_KV * BPH)} times), oracle/lq_oracle_codec.c on "
                          f"{n_thr} threads, {dt:.1f} s"}
 
     attn = None

@@ -563,6 +563,50 @@ __device__ __forceinline__ void mstage_issue(const CompactDev &c, const CStageSp
     cp_async_commit();
 }
 
+// Whether a stage can come in as bulk copies (the TMA engine moves each of
+// its four contiguous pieces -- mask words, ranks, codes, fallback rows --
+// in one request): every piece must start and end on a 16-byte boundary
+// inside its array.  Other stages (a chunk's last codes, heads whose word
+// index is not a multiple of 4) take the per-thread cp.async path.
+template <bool B4>
+__device__ __forceinline__ bool mstage_bulk_ok(const CompactDev &c, const CStageSpan &s) {
+    if (s.bad) return false;
+    const uint32_t bits = B4 ? 4u : (uint32_t)c.bits;
+    const uint32_t a1r = (s.r1 * bits + 15u) & ~15u, total16 = (c.n_repr * bits) & ~15u;
+    const uintptr_t al = reinterpret_cast<uintptr_t>(c.mask_words + s.w0) | reinterpret_cast<uintptr_t>(c.word_rank + s.w0);
+    return (s.nw & 3u) == 0 && (al & 15u) == 0 && a1r <= total16;
+}
+
+// One thread: a bulk-eligible stage as up to four bulk copies completed on
+// the slot's barrier.
+template <bool B4>
+__device__ __forceinline__ void mstage_bulk(const CompactDev &c, const CStageSpan &s, uint32_t b0, uint32_t buf,
+                                            uint32_t bar) {
+    using S = MStage<B4>;
+    const uint32_t bits = B4 ? 4u : (uint32_t)c.bits;
+    const uint32_t wbytes = 4u * s.nw;
+    const uint32_t cbytes = ((s.r1 * bits + 15u) & ~15u) - s.a0;
+    const uint32_t nf = min(32u * s.nw - (s.r1 - s.r0), (uint32_t)kMFbCap);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the slot's earlier generic reads first
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(2u * wbytes + cbytes + 16u * nf)
+                 : "memory");
+    auto copy = [&](uint32_t dst, const void *src, uint32_t bytes) {
+        if (bytes)
+            asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                             dst),
+                         "l"(src), "r"(bytes), "r"(bar)
+                         : "memory");
+    };
+    copy(buf + S::kWordsOff, c.mask_words + s.w0, wbytes);
+    copy(buf + S::kRanksOff, c.word_rank + s.w0, wbytes);
+    copy(buf + S::kPackedOff, c.packed + s.a0, cbytes);
+    copy(buf + S::kFbOff, c.fallback + (b0 - s.r0), 16u * nf);
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
 // A block's eight values travel as four fp16x2 registers whose (low, high)
 // halves are the channels (6, 2), (5, 1), (4, 0), (7, 3): the order in which
 // two-nibble groups of a 4-bit code reach the fp16 mantissas with one mask
@@ -776,6 +820,11 @@ __global__ void __launch_bounds__(kMThreads, 2) attn_compact_mma_kernel(CompactA
     }
     if (threadIdx.x < kMRing) sts_v4(bufs + threadIdx.x * S::kBytes + S::kZeroOff, make_uint4(0, 0, 0, 0));
     __shared__ uint32_t s_dirty[kMRing];  // per ring slot: the stage's index did not chain
+    // per ring slot: completion of the stage copied into it, one phase per
+    // stage (bulk copies, or a plain arrival for a cp.async stage)
+    __shared__ __align__(8) uint64_t s_bar[kMRing];
+    if (threadIdx.x == 0)
+        for (int i = 0; i < kMRing; ++i) mbar_init(smem_addr(&s_bar[i]), 1);
     __syncthreads();
 
     // the stages of both phases stream through a ring of kMRing buffers: K
@@ -784,8 +833,20 @@ __global__ void __launch_bounds__(kMThreads, 2) attn_compact_mma_kernel(CompactA
     auto issue = [&](uint32_t q) {
         if (q < n_seq) {
             const uint32_t ph = q >= nst, st = q - ph * nst;
-            if (threadIdx.x == 0) s_dirty[q % kMRing] = 0u;
-            mstage_issue<B4>(ph ? a.v : a.k, spans[ph][st], stage_b0(st), bufs + (q % kMRing) * S::kBytes);
+            const CompactDev &cq = ph ? a.v : a.k;
+            const CStageSpan &sq = spans[ph][st];
+            const uint32_t slot = q % kMRing, bar = smem_addr(&s_bar[slot]), dst = bufs + slot * S::kBytes;
+            if (mstage_bulk_ok<B4>(cq, sq)) {
+                if (threadIdx.x == 0) {
+                    s_dirty[slot] = 0u;
+                    mstage_bulk<B4>(cq, sq, stage_b0(st), dst, bar);
+                }
+                cp_async_commit();  // an empty group keeps the group count one per stage
+            } else {
+                if (threadIdx.x == 0) s_dirty[slot] = 0u;
+                mstage_issue<B4>(cq, sq, stage_b0(st), dst);
+                if (threadIdx.x == 0) mbar_arrive(bar);
+            }
         } else {
             cp_async_commit();
         }
@@ -813,6 +874,9 @@ __global__ void __launch_bounds__(kMThreads, 2) attn_compact_mma_kernel(CompactA
         const CompactDev &c = ph ? a.v : a.k;
         const uint32_t buf = bufs + (q % kMRing) * S::kBytes;
         cp_async_wait<2>();
+        // a copy that never completes leaves the flag raised and stale data,
+        // which every index below stays inside
+        mbar_wait(smem_addr(&s_bar[q % kMRing]), (q / kMRing) & 1u, a.err);
         __syncthreads();
         if (s.bad && threadIdx.x == 0) raise_flag(a.err, LQ_EF_BITSTREAM);
         // the stage's index must chain: rank(w+1) - rank(w) = popcount(word w)
