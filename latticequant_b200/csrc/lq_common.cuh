@@ -344,19 +344,25 @@ __device__ __forceinline__ void d8_nearest_pair(const float x[8], const float y[
     d8_flip(s2, c2, res2, r2);
 }
 
-// The squared distance sum((x - c) ** 2) left to right, each product and
-// each sum rounded on its own.  __fmul_rn / __fadd_rn are never contracted
-// into an FMA; a fused square-and-add rounds once instead of twice and
-// decides exact ties of dist1 and dist2 the other way (seen at full chunk
-// size: a few blocks per million).
-__device__ __forceinline__ float e8_dist(const float x[8], const float c[8]) {
-    float d = 0.0f;
+// The two squared distances sum((x - c1) ** 2), sum((x - c2) ** 2), each
+// left to right with every product and every sum rounded on its own.  The
+// squares are scalar __fmul_rn, which is never contracted into an FMA; the
+// differences and the running sums of both distances go as the halves of
+// packed fp32x2 subtracts and adds.  (A fused square-and-add rounds once
+// instead of twice and decides exact ties of dist1 and dist2 the other way:
+// seen at full chunk size, a few blocks per million, when the squares were
+// packed multiplies.)
+__device__ __forceinline__ void e8_dist2(const float x[8], const float c1[8], const float c2[8], float &d1,
+                                         float &d2) {
+    unsigned long long d = 0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        const float e = __fsub_rn(x[i], c[i]);
-        d = i ? __fadd_rn(d, __fmul_rn(e, e)) : __fmul_rn(e, e);  // 0 + v == v exactly
+        float e1, e2;
+        f2_unpack(f2_sub(f2_pack(x[i], x[i]), f2_pack(c1[i], c2[i])), e1, e2);
+        const unsigned long long sq = f2_pack(__fmul_rn(e1, e1), __fmul_rn(e2, e2));
+        d = i ? f2_add(d, sq) : sq;  // 0 + v == v exactly
     }
-    return d;
+    f2_unpack(d, d1, d2);
 }
 
 // E8 nearest point (core/e8_quantizer.py:61-83).
@@ -367,7 +373,8 @@ __device__ __forceinline__ void e8_nearest(const float x[8], float q[8]) {
     d8_nearest_pair(x, y, c1, c2, res1, res2);
 #pragma unroll
     for (int i = 0; i < 8; ++i) c2[i] = __fadd_rn(c2[i], 0.5f);
-    const float d1 = e8_dist(x, c1), d2 = e8_dist(x, c2);
+    float d1, d2;
+    e8_dist2(x, c1, c2, d1, d2);
     const bool use1 = d1 <= d2;
 #pragma unroll
     for (int i = 0; i < 8; ++i) q[i] = use1 ? c1[i] : c2[i];
@@ -388,7 +395,8 @@ __device__ __forceinline__ int e8_nearest_symbols(const float x[8], float q[8], 
     float h[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) h[i] = __fadd_rn(c2[i], 0.5f);  // the half-coset point, as the reference forms it
-    const float d1 = e8_dist(x, c1), d2 = e8_dist(x, h);
+    float d1, d2;
+    e8_dist2(x, c1, h, d1, d2);
     *finite = isfinite(d1) && isfinite(d2);
     const bool use1 = d1 <= d2;
 #pragma unroll
