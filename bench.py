@@ -776,7 +776,7 @@ def bench_config5(dev, rank, world, args, barrier):
     g.manual_seed(5006)
     ids = torch.randint(0, cfg.vocab_size, (B, P), generator=g, device=dev)
     hr = SH.head_slice(cfg.num_key_value_heads, world, rank) if world > 1 else None
-    cache = CompressedAttentionKVCache(4, tail_tokens=64, head_range=hr, layout=args.c5_layout).bind(model)
+    cache = CompressedAttentionKVCache(4, tail_tokens=args.c5_tail, head_range=hr, layout=args.c5_layout).bind(model)
     host = torch.empty(T, B, dtype=torch.int64, pin_memory=True)
     st = torch.cuda.current_stream(dev)
     e_dec0, e_dec1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -866,7 +866,8 @@ def bench_config5(dev, rank, world, args, barrier):
             "dtype": "bf16", "data": "synthetic (random-init weights N(0,0.02), seeded random token ids)",
             "config": {"workload": f"config5: Llama-3.1-8B architecture ({L} layers, 4096 hidden, 32 q / 8 kv heads), "
                                    f"batch {B}, prefill {P} random ids, {T} generated tokens, 4 b/dim KV "
-                                   f"({'rANS lanes' if args.c5_layout == 'rans' else 'compact fixed-rate layout'})",
+                                   f"({'rANS lanes' if args.c5_layout == 'rans' else 'compact fixed-rate layout'}; "
+                                   f"decode tokens encoded every {args.c5_tail})",
                        "parallelism": f"KV-head-sharded cache over {world} GPUs (weights replicated, per-layer "
                                       "all-gather of attention heads)" if world > 1 else "single GPU",
                        "global_batch": B, "seq_len": P + T},
@@ -944,6 +945,7 @@ def main():
     ap.add_argument("--c5-prefill", type=int, default=16384)
     ap.add_argument("--c5-gen", type=int, default=256)
     ap.add_argument("--c5-eager", action="store_true", help="config 5 decode steps run eagerly (no CUDA graph)")
+    ap.add_argument("--c5-tail", type=int, default=64, help="decode tokens encoded together (the cache's tail_tokens)")
     ap.add_argument("--c5-layout", default="rans", choices=["rans", "compact"],
                     help="cache layout of config 5: entropy-coded lanes or the compact fixed-rate layout")
     ap.add_argument("--layers", type=int, default=N_LAYERS,

@@ -413,6 +413,22 @@ def decompress(chunk: LaneChunk, out_dtype: Optional[torch.dtype] = None, want_s
     return out
 
 
+def lattice_points(chunk: LaneChunk) -> torch.Tensor:
+    """The chunk's E8 points (n_blocks, 8) fp32, exactly: the decoded symbols
+    (outlier records patched in) through symbols_to_e8 (core/entropy_coder.py:71-89)."""
+    g = chunk.geom
+    dev = chunk.words.device
+    n = g.n_chunks * g.n_vectors
+    _, sym = decompress(chunk, out_dtype=torch.float32, want_symbols=True)
+    cos = torch.empty(n, dtype=torch.uint8, device=dev)
+    s = stream_handle(dev)
+    check(lib().lq_unpack_bits(ptr(chunk.coset_words), n, ptr(cos), s), "lq_unpack_bits")
+    cos32 = cos.to(torch.int32)
+    q = torch.empty(n, 8, dtype=torch.float32, device=dev)
+    check(lib().lq_symbols_to_e8(ptr(cos32), ptr(sym.contiguous()), n, ptr(q), s), "lq_symbols_to_e8")
+    return q
+
+
 def patch_outliers(chunk: LaneChunk, out: Optional[torch.Tensor], sym: Optional[torch.Tensor],
                    err: torch.Tensor):
     """Write a chunk's outlier records back into its decoded output / symbols."""

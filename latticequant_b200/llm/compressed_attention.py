@@ -35,6 +35,7 @@ from ..codec import LaneChunk
 from .compressed_kv_cache import CompressedKVCache, CompressedKVLayer, OptimizedChunk
 
 ATTN_NAME = "lq_compressed"
+TAIL_MERGE_MAX = 1024  # tokens of one merged tail part
 
 
 def _attn_tile(bph: int, limit: int) -> Optional[int]:
@@ -49,10 +50,12 @@ def _attn_tile(bph: int, limit: int) -> Optional[int]:
 
 class _Part:
     """One compressed (K, V) chunk pair of a layer and its prepared attention:
-    LaneChunks (rANS lanes) or, for layout "compact", CompressedChunks."""
+    LaneChunks (rANS lanes) or, for layout "compact", CompressedChunks.
+    opt_k / opt_v: the layer's stored chunk objects the part reads (rANS)."""
 
-    def __init__(self, k, v, shape, per_token: bool, layout: str = "rans"):
+    def __init__(self, k, v, shape, per_token: bool, layout: str = "rans", opt_k=None, opt_v=None):
         self.k, self.v, self.shape, self.per_token, self.layout = k, v, tuple(shape), per_token, layout
+        self.opt_k, self.opt_v = opt_k, opt_v
         self.ops = {}
 
     def op(self, group: int):
@@ -124,11 +127,11 @@ class CompressedAttentionKVCache(CompressedKVCache):
             self._comp_values[i] = CompressedKVLayer()
         return self._state[i]
 
-    def _compress_with_tile(self, x: torch.Tensor, tile: int):
+    def _compress_with_tile(self, x: torch.Tensor, tile: int, scale_f32: Optional[torch.Tensor] = None):
         saved = self.tile_blocks
         self.tile_blocks = tile
         try:
-            return self._compress_tensor(x)
+            return self._compress_tensor(x, scale_f32=scale_f32)
         finally:
             self.tile_blocks = saved
 
@@ -261,11 +264,52 @@ class CompressedAttentionKVCache(CompressedKVCache):
         self._comp_keys[layer_idx].append_chunk(ck)
         self._comp_values[layer_idx].append_chunk(cv)
         if tile is not None and not force:
-            st.parts.append(_Part(ck.lanes, cv.lanes, (B, H, n, D), per_token=True))
+            prev = st.parts[-1] if st.parts and st.parts[-1].per_token and st.parts[-1].opt_k is not None else None
+            # merged tails grow up to TAIL_MERGE_MAX tokens, then a new part starts
+            # (a recode costs time in proportion to the part's tokens)
+            if prev is not None and prev.shape[2] + n <= TAIL_MERGE_MAX:
+                self._merge_tail_parts(st, layer_idx, prev, ck, cv, n)
+            else:
+                st.parts.append(_Part(ck.lanes, cv.lanes, (B, H, n, D), per_token=True, opt_k=ck, opt_v=cv))
         else:
             st.dense_k.append(st.tail_deq_k[:, :, :n].clone())
             st.dense_v.append(st.tail_deq_v[:, :, :n].clone())
         st.n_tail = 0
+
+    def _merge_tail_parts(self, st, layer_idx, prev: "_Part", ck, cv, n_new: int):
+        """Recode the layer's encoded tail part and the chunk just flushed as ONE
+        per-token-scale chunk, so a decode step attends over one tail part
+        however many tails have been flushed.  Each token keeps its lattice
+        points and its scale: the chunks' points times their fp32 scales are
+        coded again with those scales (x / s rounds back to the same points),
+        only the rANS tables and lanes change."""
+        B, H, n_old, D = prev.shape
+        n = n_old + n_new
+
+        def joined(old_lanes, new_lanes):
+            q = torch.cat([codec.lattice_points(old_lanes).view(B, H, n_old, D),
+                           codec.lattice_points(new_lanes).view(B, H, n_new, D)], 2)
+            s = torch.cat([old_lanes.scale_f32.view(B, H, n_old), new_lanes.scale_f32.view(B, H, n_new)], 2)
+            return (q * s.unsqueeze(-1)).reshape(B, H * n, 1, D), s.reshape(-1)
+
+        tile = _attn_tile(n * D // 8, self.tile_blocks or codec.DEFAULT_TILE_BLOCKS)
+        xk, sk = joined(prev.k, ck.lanes)
+        xv, sv = joined(prev.v, cv.lanes)
+        saved = self.total_vectors
+        mk, _ = self._compress_with_tile(xk, tile or 32, scale_f32=sk)
+        mv, _ = self._compress_with_tile(xv, tile or 32, scale_f32=sv)
+        self.total_vectors = saved  # counted when the tokens arrived
+        # the stored chunks: the two tails' entries become the merged one
+        for layers, gone, merged in ((self._comp_keys, (prev.opt_k, ck), mk), (self._comp_values, (prev.opt_v, cv), mv)):
+            chunks = layers[layer_idx].chunks
+            chunks[:] = [c for c in chunks if all(c is not g for g in gone)]
+            chunks.append(merged)
+        if tile is not None:
+            st.parts[-1] = _Part(mk.lanes, mv.lanes, (B, H, n, D), per_token=True, opt_k=mk, opt_v=mv)
+        else:  # no tile divides the merged tail: keep it dequantised (fp16 scale), as a chunk would be
+            st.parts.pop()
+            st.dense_k.append(self._decompress_chunk(mk))
+            st.dense_v.append(self._decompress_chunk(mv))
 
     def _materialise(self, st, dtype: Optional[torch.dtype] = None):
         """Every token of a layer, dequantised (fp16 scale for chunks, fp32 for the

@@ -266,8 +266,13 @@ class CompressedKVCache(DynamicCache):
         self.total_vectors = 0
         self._model_dtype = None
 
-    def _compress_tensor(self, tensor: torch.Tensor) -> Tuple[Any, torch.Tensor]:
-        """Quantise + entropy-code one (B, H, S, D) tensor (llm/compressed_kv_cache.py:176-287)."""
+    def _compress_tensor(self, tensor: torch.Tensor,
+                         scale_f32: Optional[torch.Tensor] = None) -> Tuple[Any, torch.Tensor]:
+        """Quantise + entropy-code one (B, H, S, D) tensor (llm/compressed_kv_cache.py:176-287).
+
+        scale_f32 (an addition, default off): fp32 per-head scales to use in
+        place of the computed ones -- re-coding values that are already lattice
+        points times these scales gives back exactly their lattice points."""
         device = tensor.device
         orig_dtype = tensor.dtype
         batch, heads, seq, hd = tensor.shape
@@ -283,7 +288,12 @@ class CompressedKVCache(DynamicCache):
             raise ValueError("cannot compress an empty tensor (the reference's scale would be NaN)")
         geom = codec.Geometry(1, n_heads, bph, codec.round_tile(self.tile_blocks, n_vectors))
         cd = codec.Codec(geom, x.device, keep_deq=True, deq_dtype=orig_dtype)
-        cd.scales(x, self.bits)
+        if scale_f32 is None:
+            cd.scales(x, self.bits)
+        else:
+            sf = scale_f32.to(device=x.device, dtype=torch.float32).reshape(-1)
+            cd.scale_f32.copy_(sf)
+            cd.scale_f16.copy_(sf.to(torch.float16))
         n_out = 0
         if self.eval_only_no_entropy or self.table_mode == "numpy":
             cd.quantize(x)

@@ -201,7 +201,8 @@ def load_cache(path: str, device="cuda"):
             st = _LayerState()
             lk, lv = cache._comp_keys[li], cache._comp_values[li]
             for (i, shape, per_token), j in zip(a["parts"], a["part_chunks"]):
-                st.parts.append(_Part(lk.chunks[j].lanes, lv.chunks[j].lanes, tuple(shape), bool(per_token)))
+                st.parts.append(_Part(lk.chunks[j].lanes, lv.chunks[j].lanes, tuple(shape), bool(per_token),
+                                      opt_k=lk.chunks[j], opt_v=lv.chunks[j]))
             st.dense_k = [t.to(device) for t in a["dense_k"]]
             st.dense_v = [t.to(device) for t in a["dense_v"]]
             tr = [None if t is None else t.to(device) for t in a["tail"]]

@@ -182,7 +182,8 @@ def test_compressed_attention_tails_match_oracle():
         toks_v.append(vt)
     st = cache._state[0]
     tails = [p for p in st.parts if p.per_token]
-    assert len(tails) == 2 and st.n_tail == steps - 2 * T
+    # the two flushed tails are recoded into one per-token-scale part of 2T tokens
+    assert len(tails) == 1 and tails[0].shape == (B, H, 2 * T, D) and st.n_tail == steps - 2 * T
 
     def oracle_fp16_values(x):  # (B, H, S, D) -> q * fp16 scale per head, float64
         xb, q, s32, s16 = _oracle_update_values(x, 4)
@@ -190,12 +191,12 @@ def test_compressed_attention_tails_match_oracle():
         sc = s16.view(np.float16).astype(np.float64).reshape(b * h, 1, 1)
         return (q.astype(np.float64).reshape(b * h, s * d // 8, 8) * sc).reshape(b, h, s, d)
 
-    for i, p in enumerate(tails):
-        kt = torch.cat(toks_k[i * T:(i + 1) * T], 2)  # (B, H, T, D)
-        vt = torch.cat(toks_v[i * T:(i + 1) * T], 2)
+    for p in tails:
+        kt = torch.cat(toks_k[:2 * T], 2)  # (B, H, 2T, D)
+        vt = torch.cat(toks_v[:2 * T], 2)
         for chunk, x in ((p.k, kt), (p.v, vt)):
-            # the tail chunk holds the (B, H*T, 1, D) view: one head per token
-            per_tok = x.reshape(B, H * T, 1, D)
+            # the tail chunk holds the (B, H*2T, 1, D) view: one head per token
+            per_tok = x.reshape(B, H * 2 * T, 1, D)
             _, _, s32, s16 = _oracle_update_values(per_tok, 4)
             assert np.array_equal(_u32(chunk.scale_f32), s32.view(np.uint32))
             assert np.array_equal(chunk.scale_f16.cpu().numpy().view(np.uint16), s16)
