@@ -315,6 +315,31 @@ int lq_attn_merge(const float *o_parts, const float *lse_parts, int64_t n_parts,
 int lq_attn_merge_packed(const float *parts, int64_t n_parts, int64_t rows, int head_dim, void *out, int out_dtype,
                          float *lse, void *stream);
 
+/* One decode step's attention over the dense end of a layer's cache, merged
+ * with the finished attention of its compressed parts, in one launch.
+ * Replaces, for a cache whose older tokens are compressed, the reference's
+ * SDPA over the whole dequantised buffer that update() returns
+ * (llm/compressed_kv_cache.py:342-395, read with repeat_kv): the parts come
+ * from lq_attn_decode / lq_attn_decode_compact, the dense tokens (the open
+ * tail, tails kept dequantised) are attended here.
+ *   q        [batch * n_kv_heads * group][head_dim] in q_dtype (query head
+ *            kvh * group + g reads kv head kvh); out the same shape and dtype
+ *   segment s < n_seg (host arrays): k_seg[s], v_seg[s] [batch * n_kv_heads]
+ *            [cap_seg[s]][head_dim] in kv_dtype, 16-byte aligned, of which
+ *            the first len_seg[s] tokens count -- or, where last_seg is not
+ *            NULL and last_seg[s] is, last_seg[s][0] + 1 tokens (a device slot
+ *            index, so a captured CUDA graph replays with a moving length)
+ *   o_parts  [n_parts][rows][head_dim] fp32 normalised, lse_parts
+ *            [n_parts][rows] natural log (rows = batch * n_kv_heads * group)
+ *   lse      optional [rows]: the merged log-sum-exp.  No keys at all gives
+ *            o = 0, lse = -inf.  head_dim 64 or 128, group 1..8. */
+#define LQ_DENSE_MAX_SEGMENTS 8
+int lq_attn_dense_merge(const void *q, int q_dtype, int n_seg, const void *const *k_seg, const void *const *v_seg,
+                        const int64_t *cap_seg, const int64_t *len_seg, const int64_t *const *last_seg, int kv_dtype,
+                        const float *o_parts, const float *lse_parts, int64_t n_parts, int64_t batch,
+                        int64_t n_kv_heads, int group, int head_dim, float sm_scale, void *out, float *lse,
+                        void *stream);
+
 /* Fused merge of the compact layout with an fp16 fallback
  * (llm/fused_triton_merge.py:33-177): for each of n_heads*bph blocks,
  * repr_mask[k] != 0 -> decode code repr_rank[k] of `packed` (bits bytes per

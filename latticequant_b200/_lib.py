@@ -25,6 +25,7 @@ L = 1024
 SYM_LIMIT = 512
 HIST_BINS = 1024
 NSTREAMS = 16
+DENSE_MAX_SEGMENTS = 8  # lq_attn_dense_merge segments per call
 
 _FLAG_TEXT = {
     EF_ALPHABET: "a stream alphabet exceeds L=1024 symbols (the reference's build_rans_table loops forever here)",
@@ -93,6 +94,8 @@ def _declare(lib):
         "lq_attn_merge": ([vp, vp, i64, i64, i32, vp, i32, vp, vp], i32),
         "lq_attn_merge_packed": ([vp, i64, i64, i32, vp, i32, vp, vp], i32),
         "lq_stage_tables": ([vp, vp, i64, vp, vp], i32),
+        "lq_attn_dense_merge": ([vp, i32, i32, vp, vp, vp, vp, vp, i32, vp, vp, i64, i64, i64, i32, i32, f32, vp, vp,
+                                 vp], i32),
         "lq_attn_compact_workspace": ([i64, i64, i32, i32], sz),
         "lq_attn_decode_compact": ([ctypes.POINTER(CompactView), ctypes.POINTER(CompactView), vp, i32, i64, i64, i64,
                                     i32, i32, f32, vp, i32, vp, vp, sz, vp, vp], i32),

@@ -339,3 +339,69 @@ def merge_attention_packed(parts: torch.Tensor, rows: int, head_dim: int, out_dt
     check(lib().lq_attn_merge_packed(ptr(parts), parts.shape[0], rows, head_dim, ptr(out), _lib.dtype_code(out.dtype),
                                      ptr(lse), stream_handle(parts.device)), "lq_attn_merge_packed")
     return out, lse
+
+
+def dense_merge_attention(q: torch.Tensor, segments: Sequence[tuple], o_parts: Optional[torch.Tensor],
+                          lse_parts: Optional[torch.Tensor], n_kv_heads: int, sm_scale: Optional[float] = None,
+                          out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Attention of one decode position over dense K/V segments, merged with the
+    finished attention of compressed parts, in one launch (lq_attn_dense_merge).
+
+    q: (B, Hq, D) or (B, Hq, 1, D); segments: (k, v, n) with k, v contiguous
+    (B, n_kv_heads, cap, D) buffers of which the first n tokens count -- n an
+    int, or a (1,) int64 device tensor holding the last valid slot (n = value +
+    1, read on the device: CUDA-graph replays); o_parts / lse_parts: stacked
+    (n_parts, B, Hq, D) fp32 and (n_parts, B, Hq) fp32 (natural log) or None.
+    Returns (B, Hq, D) in q's dtype (written to `out` if given); `lse`
+    (B, Hq) fp32 optional."""
+    _lib.require_cuda(q)
+    B, Hq, D = q.shape[0], q.shape[1], q.shape[-1]
+    if Hq % n_kv_heads != 0:
+        raise ValueError("query heads must be a multiple of the kv heads")
+    if len(segments) > _lib.DENSE_MAX_SEGMENTS:
+        raise ValueError(f"at most {_lib.DENSE_MAX_SEGMENTS} dense segments")
+    q3 = q.reshape(B, Hq, D)
+    q3 = q3 if q3.is_contiguous() else q3.contiguous()
+    scale = (1.0 / math.sqrt(D)) if sm_scale is None else float(sm_scale)
+    n = len(segments)
+    kp = (ctypes.c_void_p * max(n, 1))()
+    vp = (ctypes.c_void_p * max(n, 1))()
+    cap = (ctypes.c_int64 * max(n, 1))()
+    ln = (ctypes.c_int64 * max(n, 1))()
+    last = (ctypes.c_void_p * max(n, 1))()
+    kv_dtype = None
+    for i, (k, v, cnt) in enumerate(segments):
+        if k.shape != v.shape or k.dim() != 4 or k.shape[0] != B or k.shape[1] != n_kv_heads or k.shape[3] != D \
+                or not (k.is_contiguous() and v.is_contiguous()) or k.dtype != v.dtype:
+            raise ValueError("dense segments must be contiguous (B, n_kv_heads, cap, D) K/V pairs of one dtype")
+        if kv_dtype is not None and k.dtype != kv_dtype:
+            raise ValueError("dense segments must share one dtype")
+        kv_dtype = k.dtype
+        kp[i], vp[i], cap[i] = k.data_ptr(), v.data_ptr(), k.shape[2]
+        if torch.is_tensor(cnt):
+            if cnt.dtype != torch.int64 or cnt.device != q.device:
+                raise ValueError("a device segment length is a (1,) int64 tensor on the query's device")
+            ln[i], last[i] = 0, cnt.data_ptr()
+        else:
+            if not 0 <= int(cnt) <= k.shape[2]:
+                raise ValueError("a dense segment's length exceeds its buffer")
+            ln[i], last[i] = int(cnt), None
+    n_parts = 0
+    if o_parts is not None:
+        n_parts = o_parts.shape[0]
+        if o_parts.dtype != torch.float32 or lse_parts is None or lse_parts.dtype != torch.float32 or \
+                not (o_parts.is_contiguous() and lse_parts.is_contiguous()) or \
+                o_parts.numel() != n_parts * B * Hq * D or lse_parts.numel() != n_parts * B * Hq:
+            raise ValueError("parts must be contiguous fp32 (n_parts, B, Hq, D) and (n_parts, B, Hq) tensors")
+    if out is None:
+        out = torch.empty(B, Hq, D, dtype=q.dtype, device=q.device)
+    if out.dtype != q.dtype or out.numel() != B * Hq * D or not out.is_contiguous():
+        raise ValueError("out must be a contiguous (B, Hq, D) tensor of the query's dtype")
+    if lse is not None and (lse.dtype != torch.float32 or lse.numel() != B * Hq or not lse.is_contiguous()):
+        raise ValueError("lse must be a contiguous fp32 (B, Hq) tensor")
+    check(lib().lq_attn_dense_merge(
+        ptr(q3), _lib.dtype_code(q.dtype), n, *(ctypes.cast(a, ctypes.c_void_p) for a in (kp, vp, cap, ln, last)),
+        _lib.dtype_code(kv_dtype) if kv_dtype is not None else _lib.dtype_code(q.dtype),
+        ptr(o_parts) if n_parts else None, ptr(lse_parts) if n_parts else None, n_parts, B, n_kv_heads, Hq // n_kv_heads,
+        D, scale, ptr(out), ptr(lse), stream_handle(q.device)), "lq_attn_dense_merge")
+    return out

@@ -78,6 +78,21 @@ class _LayerState:
         self.n_tail = 0
         self.seq = 0
 
+    # dense segments a decode step attends besides the open tail: at most
+    # this many (consolidated into one tensor when the list reaches it)
+    MAX_DENSE = 4
+
+    def push_dense(self, k: torch.Tensor, v: torch.Tensor):
+        """Keep a (B, H, n, D) K/V pair dequantised (attended by lq_attn_dense_merge)."""
+        self.dense_k.append(k.contiguous())
+        self.dense_v.append(v.contiguous())
+        self.consolidate()
+
+    def consolidate(self):
+        if len(self.dense_k) >= self.MAX_DENSE:
+            self.dense_k = [torch.cat(self.dense_k, 2)]
+            self.dense_v = [torch.cat(self.dense_v, 2)]
+
 
 class CompressedAttentionKVCache(CompressedKVCache):
     """CompressedKVCache without the resident dequantised buffer; see the module text.
@@ -181,8 +196,7 @@ class CompressedAttentionKVCache(CompressedKVCache):
             if (S * D // 8) % 32 == 0:
                 st.parts.append(_Part(ck, cv, (B, H, S, D), per_token=False, layout="compact"))
             else:  # heads not 32-block aligned: keep this chunk merged (fp16 values)
-                st.dense_k.append(fused_decompress_chunk(ck))
-                st.dense_v.append(fused_decompress_chunk(cv))
+                st.push_dense(fused_decompress_chunk(ck), fused_decompress_chunk(cv))
             st.seq += S
             if history is not None:
                 return torch.cat([history[0], kd], 2), torch.cat([history[1], vd], 2)
@@ -195,8 +209,7 @@ class CompressedAttentionKVCache(CompressedKVCache):
         if tile is not None:
             st.parts.append(_Part(ck.lanes, cv.lanes, (B, H, S, D), per_token=False))
         else:  # no tile divides the blocks per head: keep this chunk dequantised (fp16 scale)
-            st.dense_k.append(self._decompress_chunk(ck))
-            st.dense_v.append(self._decompress_chunk(cv))
+            st.push_dense(self._decompress_chunk(ck), self._decompress_chunk(cv))
         st.seq += S
         if history is not None:
             return torch.cat([history[0], kd], 2), torch.cat([history[1], vd], 2)
@@ -272,8 +285,7 @@ class CompressedAttentionKVCache(CompressedKVCache):
             else:
                 st.parts.append(_Part(ck.lanes, cv.lanes, (B, H, n, D), per_token=True, opt_k=ck, opt_v=cv))
         else:
-            st.dense_k.append(st.tail_deq_k[:, :, :n].clone())
-            st.dense_v.append(st.tail_deq_v[:, :, :n].clone())
+            st.push_dense(st.tail_deq_k[:, :, :n].clone(), st.tail_deq_v[:, :, :n].clone())
         st.n_tail = 0
 
     def _merge_tail_parts(self, st, layer_idx, prev: "_Part", ck, cv, n_new: int):
@@ -308,8 +320,7 @@ class CompressedAttentionKVCache(CompressedKVCache):
             st.parts[-1] = _Part(mk.lanes, mv.lanes, (B, H, n, D), per_token=True, opt_k=mk, opt_v=mv)
         else:  # no tile divides the merged tail: keep it dequantised (fp16 scale), as a chunk would be
             st.parts.pop()
-            st.dense_k.append(self._decompress_chunk(mk))
-            st.dense_v.append(self._decompress_chunk(mv))
+            st.push_dense(self._decompress_chunk(mk).view(B, H, n, D), self._decompress_chunk(mv).view(B, H, n, D))
 
     def _materialise(self, st, dtype: Optional[torch.dtype] = None):
         """Every token of a layer, dequantised (fp16 scale for chunks, fp32 for the
@@ -343,40 +354,22 @@ class CompressedAttentionKVCache(CompressedKVCache):
             raise ValueError("decode_attention takes one query position")
         scaling = (1.0 / math.sqrt(D)) if scaling is None else float(scaling)
         q3 = query.reshape(B, Hq, D).contiguous()
-        o_parts, l_parts = [], []
-        for p in st.parts:
-            H = p.shape[1]
-            op = p.op(Hq // H)
-            o = torch.empty(B, Hq, D, dtype=torch.float32, device=query.device)
-            lse = torch.empty(B, Hq, dtype=torch.float32, device=query.device)
-            op(q3, o, lse, scaling)
-            o_parts.append(o)
-            l_parts.append(lse)
-        dense_k, dense_v = list(st.dense_k), list(st.dense_v)
-        graph = self._graph_idx is not None
-        if graph:  # the whole tail, its slots past the step's masked below
-            dense_k.append(st.tail_deq_k)
-            dense_v.append(st.tail_deq_v)
+        # the compressed parts (fused kernels) write their (o, lse) into one
+        # stacked buffer; one launch attends the dense tokens and merges all
+        P = len(st.parts)
+        po = pl = None
+        if P:
+            po = torch.empty(P, B, Hq, D, dtype=torch.float32, device=query.device)
+            pl = torch.empty(P, B, Hq, dtype=torch.float32, device=query.device)
+            for i, p in enumerate(st.parts):
+                p.op(Hq // p.shape[1])(q3, po[i], pl[i], scaling)
+        segs = [(k, v, k.shape[2]) for k, v in zip(st.dense_k, st.dense_v)]
+        if self._graph_idx is not None:  # the whole tail; slots past the step's are not counted
+            segs.append((st.tail_deq_k, st.tail_deq_v, self._graph_idx))
         elif st.n_tail:
-            dense_k.append(st.tail_deq_k[:, :, :st.n_tail])
-            dense_v.append(st.tail_deq_v[:, :, :st.n_tail])
-        if dense_k:
-            k = torch.cat(dense_k, 2).float()
-            v = torch.cat(dense_v, 2).float()
-            H = k.shape[1]
-            qg = q3.float().view(B, H, Hq // H, D)
-            s = torch.einsum("bhgd,bhsd->bhgs", qg, k) * scaling
-            if graph:
-                T = st.tail_deq_k.shape[2]
-                s[..., -T:] = s[..., -T:].masked_fill(self._tail_ar > self._graph_idx, float("-inf"))
-            lse = torch.logsumexp(s, -1)
-            o = torch.einsum("bhgs,bhsd->bhgd", torch.exp(s - lse[..., None]), v)
-            o_parts.append(o.reshape(B, Hq, D))
-            l_parts.append(lse.reshape(B, Hq))
-        if len(o_parts) == 1:
-            out = o_parts[0].to(query.dtype)
-        else:
-            out, _ = A.merge_attention(o_parts, l_parts, out_dtype=query.dtype)
+            segs.append((st.tail_deq_k, st.tail_deq_v, st.n_tail))
+        H = st.parts[0].shape[1] if P else segs[0][0].shape[1]
+        out = A.dense_merge_attention(q3, segs, po, pl, H, scaling)
         return out.view(B, Hq, 1, D)
 
     # ---- CUDA-graph decode steps (llm.graph_decode) --------------------------

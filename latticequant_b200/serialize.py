@@ -205,6 +205,7 @@ def load_cache(path: str, device="cuda"):
                                       opt_k=lk.chunks[j], opt_v=lv.chunks[j]))
             st.dense_k = [t.to(device) for t in a["dense_k"]]
             st.dense_v = [t.to(device) for t in a["dense_v"]]
+            st.consolidate()
             tr = [None if t is None else t.to(device) for t in a["tail"]]
             st.tail_raw_k, st.tail_raw_v, st.tail_deq_k, st.tail_deq_v = tr
             st.n_tail, st.seq = int(a["n_tail"]), int(a["seq"])
