@@ -120,9 +120,13 @@ int lq_head_scales_static(const void *x, int dtype, int64_t n_heads_total, int64
  * -> pack_coset_bits (llm/compressed_kv_cache.py:46-54), plus the per-stream
  * counts that feed build_rans_table (:236-253).
  *   scale_f32    [n_chunks][n_heads]
- *   sym_rows     [n_chunks][n_tiles][8][TB] int16: per tile and coordinate
- *                a column holding the coset-0 blocks' symbols in block order
- *                from the front and the coset-1 blocks' from the back
+ *   sym_cols     lq_sym_cols_bytes() bytes, 16-byte aligned: per tile and
+ *                coordinate an int8 column ([n_chunks][n_tiles][8][TB])
+ *                holding the coset-0 blocks' symbols in block order from the
+ *                front and the coset-1 blocks' from the back; a symbol
+ *                outside [-127, 127] is written as -128 there and in full to
+ *                the same index of the int16 plane that follows, and its
+ *                tile's u32 flag (after that plane) is set
  *   coset_words  [n_chunks][ceil(N/32)] u32, bit i of word w = block 32w+i
  *   tile_n0      [n_chunks][n_tiles] number of coset-0 blocks per tile
  *   hist         [n_chunks][16][LQ_HIST_BINS] u32, zeroed by this call
@@ -130,8 +134,9 @@ int lq_head_scales_static(const void *x, int dtype, int64_t n_heads_total, int64
  *                buffer update() returns, :204); NULL to skip
  *   q_out        optional [n_chunks][N][8] fp32 lattice points; NULL to skip
  * ---------------------------------------------------------------------- */
+size_t lq_sym_cols_bytes(int64_t n_chunks, int64_t n_vectors, int64_t tile_blocks);
 int lq_e8_quantize(const void *x, int dtype, int64_t n_chunks, int64_t n_heads, int64_t bph, const float *scale_f32,
-                   int64_t tile_blocks, int16_t *sym_rows, uint32_t *coset_words, uint32_t *tile_n0, uint32_t *hist,
+                   int64_t tile_blocks, void *sym_cols, uint32_t *coset_words, uint32_t *tile_n0, uint32_t *hist,
                    void *deq, int deq_dtype, float *q_out, uint32_t *err, void *stream);
 
 /* lq_e8_quantize with the outlier side channel (no counterpart in the
@@ -145,7 +150,7 @@ int lq_e8_quantize(const void *x, int dtype, int64_t n_chunks, int64_t n_heads, 
  *   outlier_rec    [n_chunks][outlier_cap][10]; outlier_count [n_chunks]
  *                  (zeroed by this call); a full list raises LQ_EF_CAPACITY */
 int lq_e8_quantize_outliers(const void *x, int dtype, int64_t n_chunks, int64_t n_heads, int64_t bph,
-                            const float *scale_f32, int64_t tile_blocks, int16_t *sym_rows, uint32_t *coset_words,
+                            const float *scale_f32, int64_t tile_blocks, void *sym_cols, uint32_t *coset_words,
                             uint32_t *tile_n0, uint32_t *hist, void *deq, int deq_dtype, float *q_out, int limit,
                             int blocks_per_token, uint32_t *outlier_words, int32_t *outlier_rec,
                             uint32_t *outlier_count, int64_t outlier_cap, uint32_t *err, void *stream);
@@ -187,7 +192,7 @@ int lq_expand_tables(const int32_t *tab_nsym, const uint16_t *tab_freq, int64_t 
  *   workspace    lq_rans_encode_workspace() bytes
  * ---------------------------------------------------------------------- */
 size_t lq_rans_encode_workspace(int64_t n_chunks, int64_t n_vectors, int64_t tile_blocks);
-int lq_rans_encode(const int16_t *sym_rows, const uint32_t *tile_n0, int64_t n_chunks, int64_t n_vectors,
+int lq_rans_encode(const void *sym_cols, const uint32_t *tile_n0, int64_t n_chunks, int64_t n_vectors,
                    int64_t tile_blocks, const int32_t *tab_lo, const int32_t *tab_nsym, const uint32_t *enc_tab,
                    uint32_t *words, int64_t words_cap, uint32_t *lane_off, uint32_t *lane_nbits,
                    uint32_t *lane_state, void *workspace, size_t workspace_bytes, uint32_t *err, void *stream);

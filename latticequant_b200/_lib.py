@@ -74,6 +74,7 @@ def _declare(lib):
         "lq_strerror": ([i32], ctypes.c_char_p),
         "lq_head_scales_workspace": ([i64, i64], sz),
         "lq_head_scales": ([vp, i32, i64, i64, f32, vp, vp, vp, vp, sz, vp], i32),
+        "lq_sym_cols_bytes": ([i64, i64, i64], sz),
         "lq_e8_quantize": ([vp, i32, i64, i64, i64, vp, i64, vp, vp, vp, vp, vp, i32, vp, vp, vp], i32),
         "lq_encode_e8": ([vp, i64, vp, i32, vp], i32),
         "lq_build_tables": ([vp, i64, vp, vp, vp, vp, vp], i32),

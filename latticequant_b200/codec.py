@@ -140,7 +140,9 @@ class Codec:
         self.sigma2 = torch.empty(nh, dtype=torch.float32, device=dev)
         self.scale_f32 = torch.empty(nh, dtype=torch.float32, device=dev)
         self.scale_f16 = torch.empty(nh, dtype=torch.float16, device=dev)
-        self.sym_rows = torch.empty(g.n_chunks * g.n_tiles * g.tile_blocks * 8, dtype=torch.int16, device=dev)
+        # int8 symbol columns + their int16 escape plane + per-tile flags (lq_sym_cols_bytes)
+        self.sym_rows = torch.empty(int(lib().lq_sym_cols_bytes(g.n_chunks, g.n_vectors, g.tile_blocks)),
+                                    dtype=torch.uint8, device=dev)
         self.coset_words = torch.empty(g.n_chunks * g.coset_words_per_chunk, **i32)
         self.tile_n0 = torch.empty(g.n_chunks * g.n_tiles, **i32)
         self.hist = torch.empty(g.n_chunks * NSTREAMS * HIST_BINS, **i32)

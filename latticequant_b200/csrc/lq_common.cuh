@@ -230,6 +230,30 @@ __device__ __forceinline__ void div_block_by_scale(const float v[8], float b, fl
     }
 }
 
+// ---- symbol columns between the quantiser and the lane encoder -----------
+// One buffer (lq_sym_cols_bytes): int8 columns [tiles][8][TB], then an int16
+// plane of the same shape holding the symbols the columns mark with -128
+// (those outside [-127, 127]), then one u32 flag per tile (any such symbol).
+struct SymCols {
+    int8_t *cols;
+    int16_t *wide;
+    uint32_t *esc;
+};
+
+__host__ __device__ inline size_t sym_cols_elems(int64_t n_tiles_total, int64_t tile_blocks) {
+    return (size_t)n_tiles_total * (size_t)tile_blocks * 8;
+}
+__host__ __device__ inline size_t sym_cols_bytes(int64_t n_tiles_total, int64_t tile_blocks) {
+    const size_t e = sym_cols_elems(n_tiles_total, tile_blocks);
+    return ((3 * e + 15) & ~(size_t)15) + (((size_t)n_tiles_total * 4 + 15) & ~(size_t)15);
+}
+__host__ __device__ inline SymCols sym_cols_view(void *buf, int64_t n_tiles_total, int64_t tile_blocks) {
+    const size_t e = sym_cols_elems(n_tiles_total, tile_blocks);
+    char *b = static_cast<char *>(buf);
+    return SymCols{reinterpret_cast<int8_t *>(b), reinterpret_cast<int16_t *>(b + e),
+                   reinterpret_cast<uint32_t *>(b + ((3 * e + 15) & ~(size_t)15))};
+}
+
 // ---- E8 nearest point ---------------------------------------------------
 // Bit-exact restatement of core/e8_quantizer.py:20-83 as torch evaluates it
 // on the CPU: every operation below is one rounded binary32 op (explicit

@@ -13,17 +13,22 @@
 // the packed coset bitmap.  The ballot also ranks each block inside its
 // coset, which places its 8 symbols in the tile's 8 coordinate columns:
 // coset-0 blocks from the front in block order, coset-1 blocks from the back
-// -- so each rANS lane later reads its symbols contiguously, 8 at a time.  Symbol counts go to a shared-memory histogram per CTA
-// (values in [-128, 128)), falling back to global atomics outside that
-// window, and are flushed once per CTA.
+// -- so each rANS lane later reads its symbols contiguously, 8 at a time.
+// The columns are int8: a block whose symbols all lie in [-127, 127] (one
+// test per block) stores them directly; a symbol outside is stored as -128
+// with its full value at the same index of an int16 plane, and the tile is
+// flagged so that the encoder looks there.  Symbol counts go to a
+// shared-memory histogram per CTA (values in [-127, 127], the same test),
+// falling back to global atomics outside that window, and are flushed once
+// per CTA.
 #include "lq_common.cuh"
 
 namespace lq {
 namespace {
 
 constexpr int kQWarps = 8;          // tiles per CTA
-constexpr int kSmemHalf = 128;      // shared histogram window [-128, 128)
-constexpr int kSmemBins = 2 * kSmemHalf;
+constexpr int kSmemHalf = 127;      // shared histogram window [-127, 127]: the int8 column range
+constexpr int kSmemBins = 2 * kSmemHalf + 1;
 
 __device__ __forceinline__ void red_shared_add1(uint32_t addr) {
     asm volatile("red.shared.add.u32 [%0], 1;" ::"r"(addr) : "memory");
@@ -48,7 +53,7 @@ struct OutlierArgs {
 template <int DT, int DQ, bool QO, uint32_t TBC>
 __global__ void __launch_bounds__(32 * kQWarps, 3) quantize_kernel(
     const void *__restrict__ x, uint32_t n_heads, uint32_t bph, FastDiv bph_div, const float *__restrict__ scale_f32,
-    uint32_t TB, uint32_t n_tiles, int16_t *__restrict__ sym_rows, uint32_t *__restrict__ coset_words,
+    uint32_t TB, uint32_t n_tiles, SymCols sc8, uint32_t *__restrict__ coset_words,
     uint32_t *__restrict__ tile_n0, uint32_t *__restrict__ hist, void *__restrict__ deq, float *__restrict__ q_out,
     OutlierArgs oa, uint32_t *__restrict__ err) {
     __shared__ uint32_t sh_hist[LQ_NSTREAMS * kSmemBins];
@@ -69,7 +74,10 @@ __global__ void __launch_bounds__(32 * kQWarps, 3) quantize_kernel(
         const uint32_t b0 = tile * TB;
         const uint32_t tb = (b0 + TB <= N) ? TB : N - b0;
         const int64_t cblk0 = (int64_t)chunk * N;  // first block of the chunk
-        int16_t *cols = sym_rows + ((int64_t)chunk * n_tiles + tile) * TB * 8;  // [8][TB] coordinate columns
+        const int64_t col0 = ((int64_t)chunk * n_tiles + tile) * TB * 8;  // [8][TB] coordinate columns
+        int8_t *cols = sc8.cols + col0;
+        int16_t *wide = sc8.wide + col0;
+        bool esc = false;
         const float *sc_chunk = scale_f32 + (int64_t)chunk * n_heads;
         uint32_t *cw = coset_words + (int64_t)chunk * words_per_chunk + b0 / 32;
         // per-thread position: block b = b0 + off + lane lives in head `head`, at `rem` within it
@@ -149,20 +157,27 @@ __global__ void __launch_bounds__(32 * kQWarps, 3) quantize_kernel(
             const uint32_t lt = (1u << lane) - 1u;
             if (active) {
                 const uint32_t row = coset ? tb - 1 - (n1 + __popc(ball & lt)) : n0 + __popc(act & ~ball & lt);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) cols[i * TB + row] = (int16_t)sym[i];
                 const uint32_t sh = hist_base + (uint32_t)coset * (8 * kSmemBins * 4);
-                // one test for the whole block: every (sym + half) below kSmemBins as unsigned
-                uint32_t wide = 0;
+                // one test for the whole block: every (sym + half) at most 2 * half as unsigned
+                uint32_t top = 0;
 #pragma unroll
-                for (int i = 0; i < 8; ++i) wide |= (uint32_t)(sym[i] + kSmemHalf);
-                if (wide < (uint32_t)kSmemBins) {
+                for (int i = 0; i < 8; ++i) top = max(top, (uint32_t)(sym[i] + kSmemHalf));
+                if (top < (uint32_t)kSmemBins) {
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) red_shared_add1(sh + (uint32_t)(i * kSmemBins + sym[i] + kSmemHalf) * 4u);
+                    for (int i = 0; i < 8; ++i) {
+                        cols[i * TB + row] = (int8_t)sym[i];
+                        red_shared_add1(sh + (uint32_t)(i * kSmemBins + sym[i] + kSmemHalf) * 4u);
+                    }
                 } else {
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
                         const int v = sym[i];
+                        const bool in8 = (uint32_t)(v + kSmemHalf) < (uint32_t)kSmemBins;
+                        cols[i * TB + row] = in8 ? (int8_t)v : (int8_t)-128;
+                        if (!in8) {
+                            wide[i * TB + row] = (int16_t)v;
+                            esc = true;
+                        }
                         if ((uint32_t)(v + kSmemHalf) < (uint32_t)kSmemBins) {
                             red_shared_add1(sh + (uint32_t)(i * kSmemBins + v + kSmemHalf) * 4u);
                         } else if ((uint32_t)(v + LQ_SYM_LIMIT) < (uint32_t)(2 * LQ_SYM_LIMIT)) {
@@ -185,7 +200,11 @@ __global__ void __launch_bounds__(32 * kQWarps, 3) quantize_kernel(
                 ++head;
             }
         }
-        if (lane == 0) tile_n0[(int64_t)chunk * n_tiles + tile] = n0;
+        const bool tesc = __any_sync(0xffffffffu, esc);
+        if (lane == 0) {
+            tile_n0[(int64_t)chunk * n_tiles + tile] = n0;
+            sc8.esc[(int64_t)chunk * n_tiles + tile] = tesc ? 1u : 0u;
+        }
     }
     if (flags) raise_flag(err, flags);
     __syncthreads();
@@ -201,7 +220,7 @@ __global__ void __launch_bounds__(32 * kQWarps, 3) quantize_kernel(
 
 template <int DT, int DQ, bool QO>
 int launch_quantize(const void *x, int64_t n_chunks, int64_t n_heads, int64_t bph, const float *scale_f32, int64_t TB,
-                    int16_t *sym_rows, uint32_t *coset_words, uint32_t *tile_n0, uint32_t *hist, void *deq,
+                    SymCols sym_rows, uint32_t *coset_words, uint32_t *tile_n0, uint32_t *hist, void *deq,
                     float *q_out, const OutlierArgs &oa, uint32_t *err, cudaStream_t st) {
     const int64_t N = n_heads * bph;
     const int64_t n_tiles = ceil_div(N, TB);
@@ -222,7 +241,7 @@ int launch_quantize(const void *x, int64_t n_chunks, int64_t n_heads, int64_t bp
 
 template <int DT, bool QO>
 int dispatch_deq(int deq_dtype, const void *x, int64_t n_chunks, int64_t n_heads, int64_t bph, const float *sc,
-                 int64_t TB, int16_t *sym_rows, uint32_t *cw, uint32_t *tn0, uint32_t *hist, void *deq, float *q_out,
+                 int64_t TB, SymCols sym_rows, uint32_t *cw, uint32_t *tn0, uint32_t *hist, void *deq, float *q_out,
                  const OutlierArgs &oa, uint32_t *err, cudaStream_t st) {
     if (deq == nullptr)
         return launch_quantize<DT, -1, QO>(x, n_chunks, n_heads, bph, sc, TB, sym_rows, cw, tn0, hist, deq, q_out,
@@ -244,7 +263,7 @@ int dispatch_deq(int deq_dtype, const void *x, int64_t n_chunks, int64_t n_heads
 
 template <int DT>
 int dispatch_q(int deq_dtype, const void *x, int64_t n_chunks, int64_t n_heads, int64_t bph, const float *sc,
-               int64_t TB, int16_t *sym_rows, uint32_t *cw, uint32_t *tn0, uint32_t *hist, void *deq, float *q_out,
+               int64_t TB, SymCols sym_rows, uint32_t *cw, uint32_t *tn0, uint32_t *hist, void *deq, float *q_out,
                const OutlierArgs &oa, uint32_t *err, cudaStream_t st) {
     return q_out ? dispatch_deq<DT, true>(deq_dtype, x, n_chunks, n_heads, bph, sc, TB, sym_rows, cw, tn0, hist, deq,
                                           q_out, oa, err, st)
@@ -270,15 +289,16 @@ __global__ void encode_e8_kernel(const float *__restrict__ x, int64_t n, float *
 namespace lq {
 namespace {
 int quantize_entry(const void *x, int dtype, int64_t n_chunks, int64_t n_heads, int64_t bph, const float *scale_f32,
-                   int64_t tile_blocks, int16_t *sym_rows, uint32_t *coset_words, uint32_t *tile_n0, uint32_t *hist,
+                   int64_t tile_blocks, void *sym_cols, uint32_t *coset_words, uint32_t *tile_n0, uint32_t *hist,
                    void *deq, int deq_dtype, float *q_out, const OutlierArgs &oa, uint32_t *err, void *stream) {
     if (n_chunks < 0 || n_heads < 0 || bph < 0) return LQ_ERR_INVALID;
     if (tile_blocks <= 0 || (tile_blocks % 32) != 0) return LQ_ERR_INVALID;
     if (n_chunks == 0 || n_heads * bph == 0) return LQ_OK;
-    if (!x || !scale_f32 || !sym_rows || !coset_words || !tile_n0 || !hist) return LQ_ERR_INVALID;
+    if (!x || !scale_f32 || !sym_cols || !coset_words || !tile_n0 || !hist) return LQ_ERR_INVALID;
     if ((reinterpret_cast<uintptr_t>(x) & 15) || (deq && (reinterpret_cast<uintptr_t>(deq) & 15)) ||
-        (reinterpret_cast<uintptr_t>(sym_rows) & 15) || (q_out && (reinterpret_cast<uintptr_t>(q_out) & 15)))
+        (reinterpret_cast<uintptr_t>(sym_cols) & 15) || (q_out && (reinterpret_cast<uintptr_t>(q_out) & 15)))
         return LQ_ERR_INVALID;
+    const SymCols sym_rows = sym_cols_view(sym_cols, n_chunks * ceil_div(n_heads * bph, tile_blocks), tile_blocks);
     if (n_chunks > 65535) return LQ_ERR_INVALID;
     if (n_heads * bph >= (int64_t)1 << 31) return LQ_ERR_INVALID;  // blocks per chunk are indexed in 32 bits
     cudaStream_t st = as_stream(stream);
@@ -337,16 +357,16 @@ __global__ void patch_outliers_kernel(const int32_t *__restrict__ rec, const uin
 }  // namespace lq
 
 extern "C" int lq_e8_quantize(const void *x, int dtype, int64_t n_chunks, int64_t n_heads, int64_t bph,
-                              const float *scale_f32, int64_t tile_blocks, int16_t *sym_rows, uint32_t *coset_words,
+                              const float *scale_f32, int64_t tile_blocks, void *sym_cols, uint32_t *coset_words,
                               uint32_t *tile_n0, uint32_t *hist, void *deq, int deq_dtype, float *q_out,
                               uint32_t *err, void *stream) {
     const lq::OutlierArgs off{0, 1, nullptr, nullptr, nullptr, 0};
-    return lq::quantize_entry(x, dtype, n_chunks, n_heads, bph, scale_f32, tile_blocks, sym_rows, coset_words, tile_n0,
+    return lq::quantize_entry(x, dtype, n_chunks, n_heads, bph, scale_f32, tile_blocks, sym_cols, coset_words, tile_n0,
                               hist, deq, deq_dtype, q_out, off, err, stream);
 }
 
 extern "C" int lq_e8_quantize_outliers(const void *x, int dtype, int64_t n_chunks, int64_t n_heads, int64_t bph,
-                                       const float *scale_f32, int64_t tile_blocks, int16_t *sym_rows,
+                                       const float *scale_f32, int64_t tile_blocks, void *sym_cols,
                                        uint32_t *coset_words, uint32_t *tile_n0, uint32_t *hist, void *deq,
                                        int deq_dtype, float *q_out, int limit, int blocks_per_token,
                                        uint32_t *outlier_words, int32_t *outlier_rec, uint32_t *outlier_count,
@@ -360,7 +380,7 @@ extern "C" int lq_e8_quantize_outliers(const void *x, int dtype, int64_t n_chunk
         return LQ_ERR_CUDA;
     const lq::OutlierArgs oa{limit, (uint32_t)blocks_per_token, outlier_words, outlier_rec, outlier_count,
                              (uint32_t)outlier_cap};
-    return lq::quantize_entry(x, dtype, n_chunks, n_heads, bph, scale_f32, tile_blocks, sym_rows, coset_words, tile_n0,
+    return lq::quantize_entry(x, dtype, n_chunks, n_heads, bph, scale_f32, tile_blocks, sym_cols, coset_words, tile_n0,
                               hist, deq, deq_dtype, q_out, oa, err, stream);
 }
 
@@ -398,4 +418,9 @@ extern "C" int lq_encode_e8(const float *x, int64_t n, float *out, int d8_only, 
     if (!x || !out) return LQ_ERR_INVALID;
     lq::encode_e8_kernel<<<(unsigned)lq::ceil_div(n, 256), 256, 0, lq::as_stream(stream)>>>(x, n, out, d8_only);
     return lq::check_launch();
+}
+
+extern "C" size_t lq_sym_cols_bytes(int64_t n_chunks, int64_t n_vectors, int64_t tile_blocks) {
+    if (n_chunks <= 0 || n_vectors <= 0 || tile_blocks <= 0 || (tile_blocks % 32) != 0) return 0;
+    return lq::sym_cols_bytes(n_chunks * lq::ceil_div(n_vectors, tile_blocks), tile_blocks);
 }

@@ -35,20 +35,29 @@ namespace {
 //
 // A CTA takes kEncTiles tiles of one chunk (16 lanes each) and stages the
 // chunk's 16 coder tables (64 KB) in shared memory.  Each lane reads its
-// symbols from its coordinate column of the tile (lq_e8_quantize's
+// symbols from its int8 coordinate column of the tile (lq_e8_quantize's
 // lane-major layout): coset-0 lanes walk the coset-0 prefix backward,
-// coset-1 lanes the coset-1 suffix forward, 8 symbols per 16-byte load once
-// aligned (a coset-0 lane reverses each loaded vector).
+// coset-1 lanes the coset-1 suffix forward, 8 symbols per 8-byte load once
+// aligned (a coset-0 lane reverses each loaded vector).  A tile flagged for
+// symbols outside [-127, 127] reads them one by one, taking a -128 from the
+// int16 plane.
 constexpr int kEncTiles = 32;
 constexpr size_t kEncSmem = (size_t)LQ_NSTREAMS * LQ_L * 4;
 
-__device__ __forceinline__ uint4 reverse8(uint4 u) {
-    return make_uint4(__byte_perm(u.w, 0, 0x1032), __byte_perm(u.z, 0, 0x1032), __byte_perm(u.y, 0, 0x1032),
-                      __byte_perm(u.x, 0, 0x1032));
+__device__ __forceinline__ uint2 reverse8(uint2 u) {
+    return make_uint2(__byte_perm(u.y, 0, 0x0123), __byte_perm(u.x, 0, 0x0123));
+}
+// byte k of w, sign-extended: prmt's default mode replicates the selected
+// byte's top bit where a selector nibble has bit 3 set
+template <int K>
+__device__ __forceinline__ int sbyte(uint32_t w) {
+    int r;
+    asm("prmt.b32 %0, %1, 0, %2;" : "=r"(r) : "r"(w), "n"(K | (8 | K) << 4 | (8 | K) << 8 | (8 | K) << 12));
+    return r;
 }
 
 __global__ void __launch_bounds__(16 * kEncTiles, 2) encode_lanes_kernel(
-    const int16_t *__restrict__ sym_lanes, const uint32_t *__restrict__ tile_n0, uint32_t n_tiles, uint32_t N,
+    SymCols symc, const uint32_t *__restrict__ tile_n0, uint32_t n_tiles, uint32_t N,
     uint32_t TB, const int32_t *__restrict__ tab_lo, const int32_t *__restrict__ tab_nsym,
     const uint32_t *__restrict__ enc_tab, uint32_t *__restrict__ scratch, uint32_t slot_words,
     uint32_t *__restrict__ lane_nbits, uint32_t *__restrict__ lane_state, uint32_t *__restrict__ lane_nwords,
@@ -82,7 +91,10 @@ __global__ void __launch_bounds__(16 * kEncTiles, 2) encode_lanes_kernel(
             return;
         }
         const uint32_t tab = smem_addr(etab) + s * (LQ_L * 4);
-        const int16_t *col = sym_lanes + ((size_t)chunk * n_tiles + tile) * TB * 8 + (size_t)idx * TB;
+        const size_t c0 = ((size_t)chunk * n_tiles + tile) * TB * 8 + (size_t)idx * TB;
+        const int8_t *col = symc.cols + c0;
+        const int16_t *colw = symc.wide + c0;
+        const bool esc = symc.esc[(size_t)chunk * n_tiles + tile] != 0u;
         uint32_t acc = 0, cnt = 0, simax = 0;  // simax: largest alphabet index seen (unsigned)
         uint32_t *const out_end = out;
         auto code = [&](int v) {
@@ -102,27 +114,33 @@ __global__ void __launch_bounds__(16 * kEncTiles, 2) encode_lanes_kernel(
             x = (x >> k) + (e >> 16);
         };
         // symbol j (coding order) sits at col[n0 + j] (coset 1) or col[n0 - 1 - j] (coset 0)
-        auto sym_at = [&](int j) { return (int)col[c ? (int)n0 + j : (int)n0 - 1 - j]; };
-        const int head = min(n, c ? (int)((8u - (n0 & 7u)) & 7u) : (int)(((n0 - 1u) & 7u) + 1u) & 7);
+        auto sym_at = [&](int j) {
+            const int p = c ? (int)n0 + j : (int)n0 - 1 - j;
+            const int v = col[p];
+            return v == -128 ? (int)colw[p] : v;
+        };
         int j = 0;
-        for (; j < head; ++j) code(sym_at(j));
-        if (j + 8 <= n) {
-            const uint4 *vp = reinterpret_cast<const uint4 *>(col + (c ? (int)n0 + j : (int)n0 - 1 - j - 7));
-            const int step = c ? 1 : -1;
-            uint4 cur = __ldg(vp);
-            for (; j + 8 <= n; j += 8) {
-                vp += step;
-                const uint4 nxt = (j + 16 <= n) ? __ldg(vp) : cur;
-                const uint4 u = c ? cur : reverse8(cur);
-                code((int16_t)(u.x & 0xffffu));
-                code((int16_t)(u.x >> 16));
-                code((int16_t)(u.y & 0xffffu));
-                code((int16_t)(u.y >> 16));
-                code((int16_t)(u.z & 0xffffu));
-                code((int16_t)(u.z >> 16));
-                code((int16_t)(u.w & 0xffffu));
-                code((int16_t)(u.w >> 16));
-                cur = nxt;
+        if (!esc) {  // uniform over the tile's 16 lanes
+            const int head = min(n, c ? (int)((8u - (n0 & 7u)) & 7u) : (int)(((n0 - 1u) & 7u) + 1u) & 7);
+            for (; j < head; ++j) code(sym_at(j));
+            if (j + 8 <= n) {
+                const uint2 *vp = reinterpret_cast<const uint2 *>(col + (c ? (int)n0 + j : (int)n0 - 1 - j - 7));
+                const int step = c ? 1 : -1;
+                uint2 cur = __ldg(vp);
+                for (; j + 8 <= n; j += 8) {
+                    vp += step;
+                    const uint2 nxt = (j + 16 <= n) ? __ldg(vp) : cur;
+                    const uint2 u = c ? cur : reverse8(cur);
+                    code(sbyte<0>(u.x));
+                    code(sbyte<1>(u.x));
+                    code(sbyte<2>(u.x));
+                    code(sbyte<3>(u.x));
+                    code(sbyte<0>(u.y));
+                    code(sbyte<1>(u.y));
+                    code(sbyte<2>(u.y));
+                    code(sbyte<3>(u.y));
+                    cur = nxt;
+                }
             }
         }
         for (; j < n; ++j) code(sym_at(j));
@@ -559,7 +577,7 @@ extern "C" size_t lq_rans_encode_workspace(int64_t n_chunks, int64_t n_vectors, 
     return b;
 }
 
-extern "C" int lq_rans_encode(const int16_t *sym_rows, const uint32_t *tile_n0, int64_t n_chunks, int64_t n_vectors,
+extern "C" int lq_rans_encode(const void *sym_cols, const uint32_t *tile_n0, int64_t n_chunks, int64_t n_vectors,
                               int64_t tile_blocks, const int32_t *tab_lo, const int32_t *tab_nsym,
                               const uint32_t *enc_tab, uint32_t *words, int64_t words_cap, uint32_t *lane_off,
                               uint32_t *lane_nbits, uint32_t *lane_state, void *workspace, size_t workspace_bytes,
@@ -572,10 +590,10 @@ extern "C" int lq_rans_encode(const int16_t *sym_rows, const uint32_t *tile_n0, 
         if (cudaMemsetAsync(lane_off, 0, sizeof(uint32_t), st) != cudaSuccess) return LQ_ERR_CUDA;
         return LQ_OK;
     }
-    if (!sym_rows || !tile_n0 || !tab_lo || !tab_nsym || !enc_tab || !words || !lane_nbits || !lane_state ||
+    if (!sym_cols || !tile_n0 || !tab_lo || !tab_nsym || !enc_tab || !words || !lane_nbits || !lane_state ||
         !workspace)
         return LQ_ERR_INVALID;
-    if (reinterpret_cast<uintptr_t>(sym_rows) & 15) return LQ_ERR_INVALID;  // 16-byte symbol loads
+    if (reinterpret_cast<uintptr_t>(sym_cols) & 15) return LQ_ERR_INVALID;  // vector symbol loads
     if (workspace_bytes < lq_rans_encode_workspace(n_chunks, n_vectors, tile_blocks)) return LQ_ERR_CAPACITY;
     const int64_t n_tiles = ceil_div(n_vectors, tile_blocks);
     const int64_t n_lanes = n_chunks * n_tiles * LQ_NSTREAMS;
@@ -590,7 +608,8 @@ extern "C" int lq_rans_encode(const int16_t *sym_rows, const uint32_t *tile_n0, 
         cudaSuccess)
         return LQ_ERR_CUDA;
     encode_lanes_kernel<<<dim3((unsigned)ceil_div(n_tiles, kEncTiles), (unsigned)n_chunks), 16 * kEncTiles, kEncSmem,
-                          st>>>(sym_rows, tile_n0, (uint32_t)n_tiles, (uint32_t)n_vectors, (uint32_t)tile_blocks,
+                          st>>>(sym_cols_view(const_cast<void *>(sym_cols), n_chunks * n_tiles, tile_blocks), tile_n0,
+                                (uint32_t)n_tiles, (uint32_t)n_vectors, (uint32_t)tile_blocks,
                                 tab_lo, tab_nsym, enc_tab, scratch, (uint32_t)sw, lane_nbits, lane_state, nwords, err);
     scan_reduce_kernel<<<(unsigned)nblk, kScanT, 0, st>>>(nwords, n_lanes, bsum);
     scan_blocks_kernel<<<1, kScanT, 0, st>>>(bsum, nblk);

@@ -6,6 +6,8 @@ is not correctly rounded on large tensors; ours is IEEE, as is the oracle's).
 """
 import ctypes
 
+import math
+
 import numpy as np
 import pytest
 import torch
@@ -329,3 +331,40 @@ def test_device_tables_match_oracle_rule(lq, case):
     assert int(lo.item()) == a - 512 and int(ns.item()) == len(counts)
     got = fr[0].cpu().numpy().view(np.uint16).astype(np.int32)[: len(counts)]
     assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("tile", [32, 1024])
+def test_wide_symbols_take_the_escape_plane(lq, tile):
+    """Symbols outside [-127, 127] (a few blocks ~60x the rest of their head)
+    do not fit the int8 symbol columns between the quantiser and the lane
+    encoder: they travel through the int16 plane of flagged tiles.  Lanes,
+    words and decode stay byte-identical to the oracle, and -128 itself (the
+    column's escape value) round-trips."""
+    _lib, codec = lq
+    g = torch.Generator().manual_seed(17)
+    b, h, s, d = 1, 2, 256, 128
+    x = torch.randn(b, h, s, d, generator=g)
+    x[0, 0, 5] *= 60.0
+    x[0, 1, 77] *= 60.0
+    # one block of -128 in units of its head's scale: with the block's own
+    # share in sigma^2, v^2 = c sigma^2 (c = 128^2 * 2 pi e / 4^4) and
+    # sigma^2 = (S + 8 v^2) / n give sigma^2 = S / (n - 8c)
+    hd = x[0, 1].double().clone()
+    hd[200, :8] = 0.0
+    c = 128.0 ** 2 * 2 * math.pi * math.e / 4 ** 4
+    x[0, 1, 200, :8] = -math.sqrt(c * float((hd ** 2).sum()) / (hd.numel() - 8 * c))
+    n_heads, bph = b * h, s * d // 8
+    chunk, _ = codec.compress(x.cuda(), 4, tile_blocks=tile)
+    ref = _oracle_chunk(x.numpy(), O.DT_F32, n_heads, bph, 4, chunk.geom.tile_blocks)
+    _, _, sym_ref, _ = O.quantize_chunk(x.numpy(), O.DT_F32, n_heads, bph, ref.scale_f32, out_dtype=O.DT_F32)
+    assert np.abs(sym_ref).max() > 127, "the case must hold symbols beyond the int8 range"
+    assert (sym_ref == -128).any(), "and the column's escape value itself"
+    assert np.array_equal(chunk.tab_lo.cpu().numpy(), ref.tab_lo)
+    assert np.array_equal(chunk.tab_nsym.cpu().numpy(), ref.tab_nsym)
+    assert chunk.n_words == ref.words.size
+    assert np.array_equal(_u32(chunk.lane_nbits.cpu().numpy()), ref.lane_nbits)
+    assert np.array_equal(_u32(chunk.lane_state.cpu().numpy()), ref.lane_state)
+    assert np.array_equal(_u32(chunk.words[: chunk.n_words].cpu().numpy()), ref.words)
+    out, sym = codec.decompress(chunk, want_symbols=True)
+    assert np.array_equal(sym.cpu().numpy(), sym_ref)
+    assert np.array_equal(_u32(out.reshape(-1).cpu().numpy()), _u32(O.decompress_chunk(ref, out_dtype=O.DT_F32).reshape(-1)))
