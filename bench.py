@@ -73,7 +73,7 @@ C4_LAYERS, C4_KV, C4_B, C4_S, C4_D, C4_G = 28, 4, 4, 131072, 128, 7
 # (dram__bytes_read.sum + dram__bytes_write.sum) on the 8-layer config-2 case
 # (decode: the full-size capture, whose bf16 output no longer fits L2) and
 # the full config-3 step; scaled to each launch for roofline.traffic.
-TRAFFIC_PER_BLOCK = {"scales": 16.0, "quantize": 30.6, "encode": 29.9, "decode": 20.2}
+TRAFFIC_PER_BLOCK = {"scales": 16.0, "quantize": 23.0, "encode": 20.6, "decode": 20.2}
 ATTN_TRAFFIC_PER_ALG_BYTE = 602.4 / 583.6
 
 

@@ -119,28 +119,28 @@ __global__ void __launch_bounds__(16 * kEncTiles, 2) encode_lanes_kernel(
             const int v = col[p];
             return v == -128 ? (int)colw[p] : v;
         };
+        const int head = min(n, c ? (int)((8u - (n0 & 7u)) & 7u) : (int)(((n0 - 1u) & 7u) + 1u) & 7);
         int j = 0;
-        if (!esc) {  // uniform over the tile's 16 lanes
-            const int head = min(n, c ? (int)((8u - (n0 & 7u)) & 7u) : (int)(((n0 - 1u) & 7u) + 1u) & 7);
-            for (; j < head; ++j) code(sym_at(j));
-            if (j + 8 <= n) {
-                const uint2 *vp = reinterpret_cast<const uint2 *>(col + (c ? (int)n0 + j : (int)n0 - 1 - j - 7));
-                const int step = c ? 1 : -1;
-                uint2 cur = __ldg(vp);
-                for (; j + 8 <= n; j += 8) {
-                    vp += step;
-                    const uint2 nxt = (j + 16 <= n) ? __ldg(vp) : cur;
-                    const uint2 u = c ? cur : reverse8(cur);
-                    code(sbyte<0>(u.x));
-                    code(sbyte<1>(u.x));
-                    code(sbyte<2>(u.x));
-                    code(sbyte<3>(u.x));
-                    code(sbyte<0>(u.y));
-                    code(sbyte<1>(u.y));
-                    code(sbyte<2>(u.y));
-                    code(sbyte<3>(u.y));
-                    cur = nxt;
+        for (; j < head; ++j) code(sym_at(j));
+        if (j + 8 <= n) {
+            const uint2 *vp = reinterpret_cast<const uint2 *>(col + (c ? (int)n0 + j : (int)n0 - 1 - j - 7));
+            const int step = c ? 1 : -1;
+            uint2 cur = __ldg(vp);
+            for (; j + 8 <= n; j += 8) {
+                vp += step;
+                const uint2 nxt = (j + 16 <= n) ? __ldg(vp) : cur;
+                const uint2 u = c ? cur : reverse8(cur);
+                int v[8] = {sbyte<0>(u.x), sbyte<1>(u.x), sbyte<2>(u.x), sbyte<3>(u.x),
+                            sbyte<0>(u.y), sbyte<1>(u.y), sbyte<2>(u.y), sbyte<3>(u.y)};
+                if (esc) {  // uniform over the tile's 16 lanes
+                    const int p = c ? (int)n0 + j : (int)n0 - 1 - j;
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                        if (v[k] == -128) v[k] = colw[c ? p + k : p - k];
                 }
+#pragma unroll
+                for (int k = 0; k < 8; ++k) code(v[k]);
+                cur = nxt;
             }
         }
         for (; j < n; ++j) code(sym_at(j));
