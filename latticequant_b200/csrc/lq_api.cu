@@ -159,8 +159,8 @@ __global__ void encode_streams_kernel(const int32_t *__restrict__ sym_idx, const
     for (int64_t j = n - 1; j >= 0; --j) {
         const int32_t si = min(max(p[j], 0), nsym - 1);
         const uint32_t e = __ldg(enc + si);
-        const uint32_t twof = e & 0xfffu, k0 = (e >> 12) & 0xfu;
-        const uint32_t k = k0 + ((x >> k0) >= twof ? 1u : 0u);
+        const uint32_t xmax = e & 0xfffu, k0 = (e >> 12) & 0xfu;  // lq_expand_tables' entry
+        const uint32_t k = k0 + (x >= xmax ? 1u : 0u);
         const uint32_t v = x & ~(0xffffffffu << k);
         acc |= v << cnt;
         const uint32_t tt = cnt + k;

@@ -28,8 +28,8 @@ namespace lq {
 namespace {
 
 // ---------------------------------------------------------------- encode
-// Table entry (lq_expand_tables): 2f | k0 << 12 | (L + cf - f) << 16.
-// From x in [L, 2L): k = k0 + (x >> k0 >= 2f) bits leave (the k low bits of
+// Table entry (lq_expand_tables): (2f << k0) | k0 << 12 | (L + cf - f) << 16.
+// From x in [L, 2L): k = k0 + (x >= 2f << k0) bits leave (the k low bits of
 // x), then x' = (x >> k) + L + cf - f.  The k bits are prepended to a 32-bit
 // accumulator; full words are written toward the front of the lane's slot.
 //
@@ -101,8 +101,8 @@ __global__ void __launch_bounds__(16 * kEncTiles, 2) encode_lanes_kernel(
             const uint32_t si = (uint32_t)(v - lo);
             simax = max(simax, si);
             const uint32_t e = lds_u32(tab + ((si & (LQ_L - 1)) << 2));
-            const uint32_t twof = e & 0xfffu, k0 = (e >> 12) & 0xfu;
-            const uint32_t k = k0 + ((x >> k0) >= twof ? 1u : 0u);
+            const uint32_t xmax = e & 0xfffu, k0 = (e >> 12) & 0xfu;
+            const uint32_t k = k0 + (x >= xmax ? 1u : 0u);
             const uint32_t w = x & ~(0xffffffffu << k);
             acc |= w << cnt;
             const uint32_t t = cnt + k;
@@ -501,11 +501,12 @@ __global__ void __launch_bounds__(1024, 1) decode_fused_kernel(ChunkDev a, FastD
             so[1] = make_int4(sym[4], sym[5], sym[6], sym[7]);
         }
         if constexpr (DO >= 0) {
-            float q[8];
-            ring_point(blk, q);
             const float sc = __half2float(__ushort_as_half(a.scale_f16[chunk * a.n_heads + bph_div.div(b)]));
+            unsigned long long q2[4];
+            ring_point_scaled2(blk, sc, q2);
+            float q[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) q[i] = __fmul_rn(q[i], sc);
+            for (int i = 0; i < 4; ++i) f2_unpack(q2[i], q[2 * i], q[2 * i + 1]);
             store_block8<DO>(out, gb, q);
         }
     };

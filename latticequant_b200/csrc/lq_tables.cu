@@ -221,9 +221,10 @@ __global__ void __launch_bounds__(kTT) build_tables_kernel(const uint32_t *__res
     for (int i = threadIdx.x; i < LQ_L; i += blockDim.x) fo[i] = (uint16_t)(i < n ? freq[i] : 0);
 }
 
-// enc entry: 2f | k0 << 12 | (L + cf - f) << 16, k0 = max(0, 9 - floor(log2 f)):
-// from a state x in [L, 2L) the encoder emits k = k0 + (x >> k0 >= 2f) bits and
-// moves to (x >> k) + L + cf - f.
+// enc entry: (2f << k0) | k0 << 12 | (L + cf - f) << 16, k0 = max(0, 9 -
+// floor(log2 f)): from a state x in [L, 2L) the encoder emits k = k0 +
+// (x >= 2f << k0) bits (the same test as x >> k0 >= 2f) and moves to
+// (x >> k) + L + cf - f.  2f << k0 lies in [L, 2L], so it fits 12 bits.
 // dec entry: si | nb << 10 | base << 14 for slot in [cf, cf+f):
 //   x' = f + slot - cf; nb = bits the decoder reads; base = x' << nb.
 __global__ void __launch_bounds__(kTT) expand_tables_kernel(const int32_t *__restrict__ tab_nsym,
@@ -279,7 +280,7 @@ __global__ void __launch_bounds__(kTT) expand_tables_kernel(const int32_t *__res
                 const int fi = f[i];
                 const int g = 31 - __clz(fi > 0 ? fi : 1);
                 const int k0 = max(0, 9 - g);
-                e = (uint32_t)(2 * fi) | ((uint32_t)k0 << 12) | ((uint32_t)(LQ_L + cf[i] - fi) << 16);
+                e = ((uint32_t)(2 * fi) << k0) | ((uint32_t)k0 << 12) | ((uint32_t)(LQ_L + cf[i] - fi) << 16);
             }
             enc[i] = e;
         }
