@@ -95,25 +95,17 @@ __device__ __forceinline__ void attn_partial_cta(const AttnArgs &a, uint32_t cx,
     const bool act0 = wact, act1 = wact && 2 * pair + 1 < a.tph;
     const uint32_t tile0 = head * a.tph + 2 * pair;
 
-    // query channels 8*dc .. 8*dc+7 of the G heads reading this kv head
+    // query channels 8*dc .. 8*dc+7 of the G heads reading this kv head, as
+    // packed channel pairs (2c, 2c+1) for fma.rn.f32x2 against the block's pairs
     const uint32_t b = head / a.n_kv_heads, kvh = head % a.n_kv_heads;
-    // as packed pairs of heads (g, g+1) for fma.rn.f32x2; an odd last head alone
-    constexpr int GH = G / 2;
-    unsigned long long q2[GH > 0 ? GH : 1][8];
-    float qlast[8];
+    unsigned long long q2[G][4];
 #pragma unroll
-    for (int g = 0; g < G; g += 2) {
+    for (int g = 0; g < G; ++g) {
         const int64_t row = (int64_t)b * a.n_kv_heads * G + (int64_t)kvh * G + g;
-        float x0[8], x1[8];
+        float x0[8];
         load_block8<QDT>(a.q, row * BPT + dc, x0);
-        if (g + 1 < G) {
-            load_block8<QDT>(a.q, (row + 1) * BPT + dc, x1);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) q2[g / 2][i] = f2_pack(x0[i], x1[i]);
-        } else {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) qlast[i] = x0[i];
-        }
+        for (int c = 0; c < 4; ++c) q2[g][c] = f2_pack(x0[2 * c], x0[2 * c + 1]);
     }
 
     // ---- phase K: scores
@@ -136,22 +128,19 @@ __device__ __forceinline__ void attn_partial_cta(const AttnArgs &a, uint32_t cx,
     if (bulk) mbar_wait(tbar, 0, a.err);
     if (wact) {
         auto epi_k = [&](bool ok, int t, uint32_t grp, uint32_t j, uint32_t cc, const uint4 blk) {
-            float kq[8];
-            ring_point(blk, kq);
-            // per-lane partial dots over its 8 channels, i in order, two heads per fma.rn.f32x2
+            unsigned long long k2[4];
+            ring_point2(blk, k2);
+            // per-lane partial dots over its 8 channels: the even and the odd
+            // channels as the two halves of fma.rn.f32x2, then their sum
             float dot[G];
 #pragma unroll
-            for (int g = 0; g + 1 < G; g += 2) {
-                unsigned long long s2 = f2_mul(q2[g / 2][0], f2_pack(kq[0], kq[0]));
+            for (int g = 0; g < G; ++g) {
+                unsigned long long s2 = f2_mul(q2[g][0], k2[0]);
 #pragma unroll
-                for (int i = 1; i < 8; ++i) s2 = f2_fma(q2[g / 2][i], f2_pack(kq[i], kq[i]), s2);
-                f2_unpack(s2, dot[g], dot[g + 1]);
-            }
-            if constexpr (G % 2) {
-                float s = __fmul_rn(qlast[0], kq[0]);
-#pragma unroll
-                for (int i = 1; i < 8; ++i) s = __fmaf_rn(qlast[i], kq[i], s);
-                dot[G - 1] = s;
+                for (int c = 1; c < 4; ++c) s2 = f2_fma(q2[g][c], k2[c], s2);
+                float lo, hi;
+                f2_unpack(s2, lo, hi);
+                dot[g] = lo + hi;
             }
 #pragma unroll
             for (int g = 0; g < G; ++g) dot[g] = ok ? dot[g] : 0.f;
@@ -271,8 +260,8 @@ __device__ __forceinline__ void attn_partial_cta(const AttnArgs &a, uint32_t cx,
     if (wact) {
         auto epi_v = [&](bool ok, int t, uint32_t grp, uint32_t j, uint32_t cc, const uint4 blk) {
             if (!ok) return;
-            float vq[8];
-            ring_point(blk, vq);
+            unsigned long long v2[4];
+            ring_point2(blk, v2);
             const uint32_t tok = grp * TPG + j / BPT;
             const float *pp = sc + ((uint32_t)t * a.tpt + tok) * GP;
             float p[GP];
@@ -284,9 +273,6 @@ __device__ __forceinline__ void attn_partial_cta(const AttnArgs &a, uint32_t cx,
                 p[g4 + 2] = f.z;
                 p[g4 + 3] = f.w;
             }
-            unsigned long long v2[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) v2[i] = f2_pack(vq[2 * i], vq[2 * i + 1]);
 #pragma unroll
             for (int g = 0; g < G; ++g) {
                 const unsigned long long pg = f2_pack(p[g], p[g]);

@@ -158,20 +158,26 @@ __device__ __forceinline__ void ring_point(const uint4 u, float q[8]) {
     q[7] = ring_value(u.w, true, __int_as_float(0x4AC08000 - 2 * (int)ring_parity(u)));
 }
 
-// ring_point scaled by s, as four packed fp32x2 pairs (channels 2i, 2i+1):
-// the point by packed subtractions, the product by packed multiplies, each
-// half rounded exactly as its scalar op (the subtraction is exact)
-__device__ __forceinline__ void ring_point_scaled2(const uint4 u, float s, unsigned long long q2[4]) {
+// ring_point as four packed fp32x2 pairs (channels 2i, 2i+1), by packed
+// subtractions (exact, as the scalar ones)
+__device__ __forceinline__ void ring_point2(const uint4 u, unsigned long long q2[4]) {
     constexpr float kOff = 6307840.0f;  // 1.5 * 2^22 + 2^15 / 2
     const float off7 = __int_as_float(0x4AC08000 - 2 * (int)ring_parity(u));
-    const unsigned long long off = f2_pack(kOff, kOff), ss = f2_pack(s, s);
+    const unsigned long long off = f2_pack(kOff, kOff);
     const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const unsigned long long raw = f2_pack(__int_as_float(__byte_perm(w[i], 0x4AC00000u, 0x7610u)),
                                                __int_as_float(__byte_perm(w[i], 0x4AC00000u, 0x7632u)));
-        q2[i] = f2_mul(f2_sub(raw, i == 3 ? f2_pack(kOff, off7) : off), ss);
+        q2[i] = f2_sub(raw, i == 3 ? f2_pack(kOff, off7) : off);
     }
+}
+// ring_point2 times s: packed multiplies, each half rounded as its scalar op
+__device__ __forceinline__ void ring_point_scaled2(const uint4 u, float s, unsigned long long q2[4]) {
+    ring_point2(u, q2);
+    const unsigned long long ss = f2_pack(s, s);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) q2[i] = f2_mul(q2[i], ss);
 }
 
 // the reference's integer symbols (entropy_coder.py:46-68) of a ring block
