@@ -368,6 +368,8 @@ class CompressedAttentionKVCache(CompressedKVCache):
             segs.append((st.tail_deq_k, st.tail_deq_v, self._graph_idx))
         elif st.n_tail:
             segs.append((st.tail_deq_k, st.tail_deq_v, st.n_tail))
+        if not P and not segs:
+            raise ValueError(f"layer {layer_idx} holds no tokens to attend over")
         H = st.parts[0].shape[1] if P else segs[0][0].shape[1]
         out = A.dense_merge_attention(q3, segs, po, pl, H, scaling)
         return out.view(B, Hq, 1, D)
