@@ -807,6 +807,7 @@ def bench_config5(dev, rank, world, args, barrier):
         e_dec1.record(st)
         torch.cuda.synchronize()
         captures = stepper.captures if stepper is not None else 0
+        capture_s = stepper.capture_s if stepper is not None else 0.0
         if stepper is not None:
             stepper.release()  # the graph holds collectives when sharded: gone before the process group
         # the attention of one layer (every compressed part, the exact tail and
@@ -872,8 +873,10 @@ def bench_config5(dev, rank, world, args, barrier):
                        "parallelism": f"KV-head-sharded cache over {world} GPUs (weights replicated, per-layer "
                                       "all-gather of attention heads)" if world > 1 else "single GPU",
                        "global_batch": B, "seq_len": P + T},
-            "decode": "eager" if args.c5_eager else f"CUDA graph replays ({captures} captures, re-captured "
-                                                     "after each tail flush, inside the timed region)",
+            "decode": "eager" if args.c5_eager else f"CUDA graph replays ({captures} captures; a tail flush "
+                                                     "that replaces a buffer the step reads is followed by a "
+                                                     "new capture, inside the timed region)",
+            "capture_s": capture_s,
             "prefill_s": prefill_s, "compressed_cache_GB_rank0": comp / 1e9,
             "max_memory_GB_rank0": mem / 1e9,
             "attention": {"layer_ms": layer_attn_ms, "share_of_step": L * layer_attn_ms / (ms / steps),

@@ -77,6 +77,13 @@ class _LayerState:
         self.tail_deq_k = self.tail_deq_v = None
         self.n_tail = 0
         self.seq = 0
+        # flushed tails kept dequantised, appended to one buffer that grows by
+        # doubling; its token count is also on the device (as the last valid
+        # index), where the attention reads it, so a captured decode step stays
+        # valid across flushes until the buffer has to grow
+        self.tail_dense_k = self.tail_dense_v = None
+        self.n_tail_dense = 0
+        self.tail_dense_last: Optional[torch.Tensor] = None
 
     # dense segments a decode step attends besides the open tail: at most
     # this many (consolidated into one tensor when the list reaches it)
@@ -92,6 +99,38 @@ class _LayerState:
         if len(self.dense_k) >= self.MAX_DENSE:
             self.dense_k = [torch.cat(self.dense_k, 2)]
             self.dense_v = [torch.cat(self.dense_v, 2)]
+
+    def reserve_tail_dense(self, like: torch.Tensor, tokens: int):
+        """Make the dense tail buffer hold at least `tokens` tokens shaped like
+        `like` (B, H, *, D) (a new, doubled buffer when it must grow)."""
+        old = self.tail_dense_k
+        if old is not None and old.shape[2] >= tokens:
+            return
+        B, H, _, D = like.shape
+        cap = max(tokens, 2 * old.shape[2] if old is not None else 0)
+        k = torch.empty(B, H, cap, D, dtype=like.dtype, device=like.device)
+        v = torch.empty_like(k)
+        if self.n_tail_dense:
+            k[:, :, :self.n_tail_dense].copy_(old[:, :, :self.n_tail_dense])
+            v[:, :, :self.n_tail_dense].copy_(self.tail_dense_v[:, :, :self.n_tail_dense])
+        self.tail_dense_k, self.tail_dense_v = k, v
+        if self.tail_dense_last is None:
+            self.tail_dense_last = torch.full((1,), self.n_tail_dense - 1, dtype=torch.int64, device=like.device)
+
+    def push_tail_dense(self, k: torch.Tensor, v: torch.Tensor):
+        """Append flushed tail tokens (B, H, n, D), kept dequantised."""
+        n = k.shape[2]
+        self.reserve_tail_dense(k, self.n_tail_dense + n)
+        self.tail_dense_k[:, :, self.n_tail_dense:self.n_tail_dense + n].copy_(k)
+        self.tail_dense_v[:, :, self.n_tail_dense:self.n_tail_dense + n].copy_(v)
+        self.n_tail_dense += n
+        self.tail_dense_last.fill_(self.n_tail_dense - 1)
+
+    def dense_tail_tokens(self):
+        """(K, V) of the flushed tails kept dequantised, or None."""
+        if not self.n_tail_dense:
+            return None
+        return self.tail_dense_k[:, :, :self.n_tail_dense], self.tail_dense_v[:, :, :self.n_tail_dense]
 
 
 class CompressedAttentionKVCache(CompressedKVCache):
@@ -236,6 +275,8 @@ class CompressedAttentionKVCache(CompressedKVCache):
             st.tail_raw_v = torch.zeros_like(st.tail_raw_k)
             st.tail_deq_k = torch.zeros_like(st.tail_raw_k)
             st.tail_deq_v = torch.zeros_like(st.tail_raw_k)
+            if self.layout == "compact":  # its flushed tails stay dequantised: room for four
+                st.reserve_tail_dense(st.tail_deq_k, 4 * T)
         # K and V of the token in one call: each (batch, head) row has its own
         # scale, so stacking them along the heads changes no value
         kvd = self._quantise_only(torch.cat([k, v], 1))
@@ -285,7 +326,7 @@ class CompressedAttentionKVCache(CompressedKVCache):
             else:
                 st.parts.append(_Part(ck.lanes, cv.lanes, (B, H, n, D), per_token=True, opt_k=ck, opt_v=cv))
         else:
-            st.push_dense(st.tail_deq_k[:, :, :n].clone(), st.tail_deq_v[:, :, :n].clone())
+            st.push_tail_dense(st.tail_deq_k[:, :, :n], st.tail_deq_v[:, :, :n])
         st.n_tail = 0
 
     def _merge_tail_parts(self, st, layer_idx, prev: "_Part", ck, cv, n_new: int):
@@ -338,6 +379,10 @@ class CompressedAttentionKVCache(CompressedKVCache):
             vs.append(codec.decompress(p.v, out_dtype=dt).view(p.shape))
         ks += [t.to(dt) for t in st.dense_k]
         vs += [t.to(dt) for t in st.dense_v]
+        td = st.dense_tail_tokens()
+        if td is not None:
+            ks.append(td[0].to(dt))
+            vs.append(td[1].to(dt))
         if st.n_tail:
             ks.append(st.tail_deq_k[:, :, :st.n_tail].to(dt))
             vs.append(st.tail_deq_v[:, :, :st.n_tail].to(dt))
@@ -364,6 +409,8 @@ class CompressedAttentionKVCache(CompressedKVCache):
             for i, p in enumerate(st.parts):
                 p.op(Hq // p.shape[1])(q3, po[i], pl[i], scaling)
         segs = [(k, v, k.shape[2]) for k, v in zip(st.dense_k, st.dense_v)]
+        if st.tail_dense_k is not None:  # length read on the device: valid across flushes in a captured step
+            segs.append((st.tail_dense_k, st.tail_dense_v, st.tail_dense_last))
         if self._graph_idx is not None:  # the whole tail; slots past the step's are not counted
             segs.append((st.tail_deq_k, st.tail_deq_v, self._graph_idx))
         elif st.n_tail:
@@ -403,6 +450,17 @@ class CompressedAttentionKVCache(CompressedKVCache):
 
     def tail_full(self) -> bool:
         return any(st.n_tail >= self.tail_tokens for st in self._state)
+
+    def graph_signature(self):
+        """The device buffers a captured decode step reads (parts, dense
+        segments, tails): a flush that leaves it unchanged leaves the captured
+        step valid (the tail slot restarts at 0)."""
+        def ptr(t):
+            return None if t is None else t.data_ptr()
+
+        return tuple((tuple(id(p) for p in st.parts), tuple(ptr(t) for t in st.dense_k + st.dense_v),
+                      ptr(st.tail_dense_k), ptr(st.tail_dense_v), ptr(st.tail_raw_k), ptr(st.tail_deq_k))
+                     for st in self._state)
 
     def flush_tails(self):
         """Encode every full tail (what an eager update does at the 64th token)."""
@@ -447,7 +505,8 @@ class CompressedAttentionKVCache(CompressedKVCache):
     def decompressed_resident_bytes(self):
         total = 0
         for st in self._state:
-            for t in st.dense_k + st.dense_v + [st.tail_raw_k, st.tail_raw_v, st.tail_deq_k, st.tail_deq_v]:
+            for t in st.dense_k + st.dense_v + [st.tail_raw_k, st.tail_raw_v, st.tail_deq_k, st.tail_deq_v,
+                                                st.tail_dense_k, st.tail_dense_v]:
                 if t is not None:
                     total += t.nelement() * t.element_size()
         return total

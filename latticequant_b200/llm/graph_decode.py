@@ -9,12 +9,16 @@ position ids and the cache's tail slot are static device tensors the captured
 step advances itself, and the cache's host bookkeeping runs after each replay
 (CompressedAttentionKVCache.enter_graph / graph_advance).  When the tails are
 full (every `tail_tokens` tokens) they are encoded eagerly, as an eager
-update() would, and the step is captured again (the cache then has one more
-part per layer).  The reference decodes eagerly (llm/e2e_eval.py:212); the
+update() would; the captured step is replayed on (its tail slot back at 0)
+when the flush left every buffer it reads in place (the compact layout's
+dequantised tails go to a buffer whose length the attention reads on the
+device), and captured again when it did not (a new or recoded part, a buffer
+that had to grow).  The reference decodes eagerly (llm/e2e_eval.py:212); the
 tokens are the same greedy tokens.
 """
 from __future__ import annotations
 
+import time
 from typing import Optional
 
 import torch
@@ -33,6 +37,7 @@ class GraphedDecodeStep:
         self.model, self.cache, self.keep_logits = model, cache, keep_logits
         self.graph: Optional[torch.cuda.CUDAGraph] = None
         self.captures = 0
+        self.capture_s = 0.0  # host wall time spent in captures (warm-up run included)
 
     def _body(self):
         out = self.model(self.s_ids, past_key_values=self.cache, position_ids=self.s_pos,
@@ -46,6 +51,7 @@ class GraphedDecodeStep:
         self.s_idx.add_(1)
 
     def _capture(self, ids: torch.Tensor):
+        t0 = time.perf_counter()
         c, dev = self.cache, ids.device
         B = ids.shape[0]
         pos = c.get_seq_length(0)
@@ -55,6 +61,7 @@ class GraphedDecodeStep:
         self.s_cpos = torch.tensor([pos], dtype=torch.long, device=dev)
         self.s_idx = torch.tensor([n_tail], dtype=torch.long, device=dev)
         self.s_out = torch.empty(B, 1, dtype=torch.long, device=dev)
+        self.sig = c.graph_signature()
         if self.keep_logits:
             self.logits = torch.empty(B, self.model.config.vocab_size, dtype=torch.float32, device=dev)
         c.enter_graph(self.s_idx)
@@ -73,6 +80,7 @@ class GraphedDecodeStep:
         with torch.cuda.graph(self.graph), torch.no_grad():
             self._body()
         self.captures += 1
+        self.capture_s += time.perf_counter() - t0
 
     def release(self):
         """Drop the captured graph (before destroy_process_group when the step
@@ -84,7 +92,11 @@ class GraphedDecodeStep:
     def step(self, ids: torch.Tensor) -> torch.Tensor:
         c = self.cache
         if self.graph is not None and c.tail_full():
-            self.release()
+            c.flush_tails()
+            if c.graph_signature() == self.sig:
+                self.s_idx.zero_()  # the same buffers: replay on from tail slot 0
+            else:
+                self.release()
         if self.graph is None:
             c.flush_tails()
             if any(st.tail_raw_k is None for st in c._state):  # the first decode step runs eagerly

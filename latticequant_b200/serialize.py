@@ -98,8 +98,8 @@ def cache_state(cache) -> Dict[str, Any]:
     if isinstance(cache, CompressedAttentionKVCache):
         d["tail_tokens"] = cache.tail_tokens
         d["attn"] = [{"parts": [[i, list(p.shape), p.per_token] for i, p in enumerate(st.parts)],
-                      "dense_k": [_tensor_or_none(t) for t in st.dense_k],
-                      "dense_v": [_tensor_or_none(t) for t in st.dense_v],
+                      "dense_k": [_tensor_or_none(t) for t in st.dense_k + _tail_dense(st, 0)],
+                      "dense_v": [_tensor_or_none(t) for t in st.dense_v + _tail_dense(st, 1)],
                       "tail": [_tensor_or_none(t) for t in (st.tail_raw_k, st.tail_raw_v, st.tail_deq_k,
                                                             st.tail_deq_v)],
                       "n_tail": st.n_tail, "seq": st.seq, "part_chunks": _part_chunk_index(cache, li)}
@@ -107,6 +107,12 @@ def cache_state(cache) -> Dict[str, Any]:
     else:
         d["resident"] = [None if t is None or t.numel() == 0 else "rebuild" for t in cache.key_cache]
     return d
+
+
+def _tail_dense(st, i: int) -> list:
+    """The layer's flushed tails kept dequantised (saved as one more dense segment)."""
+    td = st.dense_tail_tokens()
+    return [] if td is None else [td[i]]
 
 
 def _part_chunk_index(cache, li):

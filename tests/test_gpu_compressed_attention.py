@@ -126,7 +126,8 @@ def test_compact_layout_decode_attention(bits):
     assert worst <= 1e-3, worst
     st = cache._state[0]
     assert len(st.parts) == 1 and st.parts[0].layout == "compact"
-    assert len(st.dense_k) == 1 and st.n_tail == steps - 64
+    # the flushed tail is kept dequantised in the layer's growing tail buffer
+    assert not st.dense_k and st.n_tail_dense == 64 and st.n_tail == steps - 64
     assert cache.get_seq_length(0) == S0 + steps
     with pytest.raises(ValueError):
         from latticequant_b200 import serialize
