@@ -35,7 +35,10 @@ from ..codec import LaneChunk
 from .compressed_kv_cache import CompressedKVCache, CompressedKVLayer, OptimizedChunk
 
 ATTN_NAME = "lq_compressed"
-TAIL_MERGE_MAX = 1024  # tokens of one merged tail part
+# rANS layout: flushed tails are attended from their dequantised tokens up to
+# this many per layer, and beyond it from per-token-scale parts of at most
+# this many tokens each (recoded together as tails arrive)
+TAIL_MERGE_MAX = 1024
 
 
 def _attn_tile(bph: int, limit: int) -> Optional[int]:
@@ -275,8 +278,10 @@ class CompressedAttentionKVCache(CompressedKVCache):
             st.tail_raw_v = torch.zeros_like(st.tail_raw_k)
             st.tail_deq_k = torch.zeros_like(st.tail_raw_k)
             st.tail_deq_v = torch.zeros_like(st.tail_raw_k)
-            if self.layout == "compact":  # its flushed tails stay dequantised: room for four
-                st.reserve_tail_dense(st.tail_deq_k, 4 * T)
+            # flushed tails are attended dequantised (the first TAIL_MERGE_MAX
+            # tokens in the rANS layout, all in the compact one): room for up
+            # to four tails, at most a sixteenth of the context so far
+            st.reserve_tail_dense(st.tail_deq_k, T * min(4, max(1, st.seq // (16 * T))))
         # K and V of the token in one call: each (batch, head) row has its own
         # scale, so stacking them along the heads changes no value
         kvd = self._quantise_only(torch.cat([k, v], 1))
@@ -317,7 +322,11 @@ class CompressedAttentionKVCache(CompressedKVCache):
         self.total_vectors = saved  # counted when the tokens arrived
         self._comp_keys[layer_idx].append_chunk(ck)
         self._comp_values[layer_idx].append_chunk(cv)
-        if tile is not None and not force:
+        if tile is not None and not force and st.n_tail_dense + n <= TAIL_MERGE_MAX:
+            # stored encoded; attended from its dequantised tokens (update()'s
+            # values), which join the layer's dense tail buffer
+            st.push_tail_dense(st.tail_deq_k[:, :, :n], st.tail_deq_v[:, :, :n])
+        elif tile is not None and not force:
             prev = st.parts[-1] if st.parts and st.parts[-1].per_token and st.parts[-1].opt_k is not None else None
             # merged tails grow up to TAIL_MERGE_MAX tokens, then a new part starts
             # (a recode costs time in proportion to the part's tokens)

@@ -49,10 +49,8 @@ def test_decode_attention_over_chunks_and_tail(D, S0, steps):
     assert worst <= 1e-3, worst
     st = cache._state[0]
     assert st.seq == S0 + steps
-    # flushed tails are recoded into ONE per-token-scale part
-    assert len(st.parts) == 1 + min(1, steps // 64) and st.n_tail == steps % 64
-    if steps >= 64:
-        assert st.parts[-1].per_token and st.parts[-1].shape[2] == (steps // 64) * 64
+    # flushed tails are stored encoded and attended from the layer's dense tail
+    assert len(st.parts) == 1 and st.n_tail == steps % 64 and st.n_tail_dense == (steps // 64) * 64
     assert cache.get_seq_length(0) == S0 + steps
     # the tail chunks hold exactly the reference's per-token quantisation
     # resident: only the fixed-size tail buffers, vs. the reference's whole dequantised K/V
@@ -96,6 +94,38 @@ def test_tiny_llama_decode_through_hook():
     assert cache.flags() == 0
     assert cache.get_seq_length(0) == 128 + steps
     assert worst < 2e-2, worst
+
+
+def test_tails_past_the_dense_limit_become_encoded_parts(monkeypatch):
+    """rANS layout: flushed tails are attended from the dense tail buffer up to
+    TAIL_MERGE_MAX tokens per layer and from per-token-scale parts (recoded
+    together as they arrive) beyond it; the attention over all of them stays
+    within the bar of float64 attention over the same dequantised tokens."""
+    import latticequant_b200.llm.compressed_attention as CA
+
+    monkeypatch.setattr(CA, "TAIL_MERGE_MAX", 32)
+    torch.manual_seed(6)
+    B, H, G, S0, D, T = 2, 2, 4, 128, 128, 16
+    steps = 4 * T + 3
+    cache = CA.CompressedAttentionKVCache(4, tail_tokens=T)
+    cache.update(torch.randn(B, H, S0, D, device="cuda", dtype=torch.bfloat16),
+                 torch.randn(B, H, S0, D, device="cuda", dtype=torch.bfloat16), 0)
+    worst = 0.0
+    for _ in range(steps):
+        cache.update(torch.randn(B, H, 1, D, device="cuda", dtype=torch.bfloat16),
+                     torch.randn(B, H, 1, D, device="cuda", dtype=torch.bfloat16), 0)
+        q = torch.randn(B, H * G, 1, D, device="cuda", dtype=torch.float32) / math.sqrt(D)
+        o = cache.decode_attention(0, q)
+        kk, vv = cache._materialise(cache._state[0], torch.float32)
+        ref = _ref_attention(q, kk, vv, 1 / math.sqrt(D))
+        worst = max(worst, ((o.double() - ref).abs().amax(-1) / ref.abs().amax(-1)).max().item())
+    st = cache._state[0]
+    assert st.n_tail_dense == 2 * T and st.n_tail == 3
+    tails = [p for p in st.parts if p.per_token]
+    assert len(tails) == 1 and tails[0].shape == (B, H, 2 * T, D)
+    assert cache.get_seq_length(0) == S0 + steps
+    assert cache.flags() == 0
+    assert worst <= 1e-3, worst
 
 
 @pytest.mark.parametrize("bits", [4, 3])

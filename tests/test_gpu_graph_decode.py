@@ -1,10 +1,11 @@
 """CUDA-graph decode steps (llm.graph_decode.GraphedDecodeStep) against eager
 decoding through the same CompressedAttentionKVCache: a tiny Llama, teacher-
 forced on the eager run's greedy tokens for 150 steps (two tail flushes), for
-both cache layouts: the rANS layout captures again after each flush (a new,
-then a recoded tail part), the compact layout's step stays valid across both
-(its dequantised tails go to a buffer reserved for four, length on the
-device), so one capture serves all 150 steps.  The graphed step attends over the
+both cache layouts.  Flushed tails are attended from a dequantised buffer
+whose length the attention reads on the device, so the captured step stays
+valid across a flush while the buffer has room; at this 128-token context it
+is reserved for one tail, so the first flush keeps the capture and the
+second (the buffer doubles) takes a new one: two captures in all.  The graphed step attends over the
 whole tail with a mask where the eager one takes its filled slots, so fp32
 sums round differently and the bf16 model turns that into ulp-level changes:
 logits within 2e-2 of the eager step's (relative to the step's largest
@@ -48,7 +49,7 @@ def test_graphed_steps_match_eager(layout):
             worst = max(worst, ((g.logits - ref[t]).abs().amax() / ref[t].abs().amax()).item())
             same += int((g.logits.argmax(-1) == ref[t].argmax(-1)).sum())
         g.release()
-    assert g.captures == (3 if layout == "rans" else 1)
+    assert g.captures == 2
     assert cache.get_seq_length(0) == 128 + steps == eager.get_seq_length(0)
     assert cache.flags() == 0
     assert worst < 2e-2, worst

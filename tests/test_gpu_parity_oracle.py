@@ -159,8 +159,9 @@ def test_variable_rate_cache_matches_oracle():
 
 
 def test_compressed_attention_tails_match_oracle():
-    """Decode tokens: update()'s output, the per-token-scale tail chunks and the
-    attention over them, all against the oracle."""
+    """Decode tokens: update()'s output, the stored per-token-scale tail chunks,
+    the dequantised tail the attention reads and the attention itself, all
+    against the oracle."""
     from latticequant_b200 import codec
     from latticequant_b200.llm.compressed_attention import CompressedAttentionKVCache
 
@@ -181,9 +182,12 @@ def test_compressed_attention_tails_match_oracle():
         toks_k.append(kt)
         toks_v.append(vt)
     st = cache._state[0]
-    tails = [p for p in st.parts if p.per_token]
-    # the two flushed tails are recoded into one per-token-scale part of 2T tokens
-    assert len(tails) == 1 and tails[0].shape == (B, H, 2 * T, D) and st.n_tail == steps - 2 * T
+    # the two flushed tails: stored as per-token-scale chunks, attended from
+    # their dequantised tokens (update()'s values) in the layer's dense tail
+    assert not [p for p in st.parts if p.per_token]
+    assert st.n_tail_dense == 2 * T and st.n_tail == steps - 2 * T
+    stored_k, stored_v = cache._comp_keys[0].chunks[1:], cache._comp_values[0].chunks[1:]
+    assert len(stored_k) == len(stored_v) == 2
 
     def oracle_fp16_values(x):  # (B, H, S, D) -> q * fp16 scale per head, float64
         xb, q, s32, s16 = _oracle_update_values(x, 4)
@@ -191,33 +195,31 @@ def test_compressed_attention_tails_match_oracle():
         sc = s16.view(np.float16).astype(np.float64).reshape(b * h, 1, 1)
         return (q.astype(np.float64).reshape(b * h, s * d // 8, 8) * sc).reshape(b, h, s, d)
 
-    for p in tails:
-        kt = torch.cat(toks_k[:2 * T], 2)  # (B, H, 2T, D)
-        vt = torch.cat(toks_v[:2 * T], 2)
-        for chunk, x in ((p.k, kt), (p.v, vt)):
-            # the tail chunk holds the (B, H*2T, 1, D) view: one head per token
-            per_tok = x.reshape(B, H * 2 * T, 1, D)
+    for i in range(2):
+        for chunk, toks in ((stored_k[i].lanes, toks_k), (stored_v[i].lanes, toks_v)):
+            # a tail chunk holds the (B, H*T, 1, D) view: one head per token
+            per_tok = torch.cat(toks[i * T:(i + 1) * T], 2).reshape(B, H * T, 1, D)
             _, _, s32, s16 = _oracle_update_values(per_tok, 4)
             assert np.array_equal(_u32(chunk.scale_f32), s32.view(np.uint32))
             assert np.array_equal(chunk.scale_f16.cpu().numpy().view(np.uint16), s16)
             dec = codec.decompress(chunk, out_dtype=torch.float32).double().cpu().numpy()
             assert np.array_equal(dec.reshape(-1), oracle_fp16_values(per_tok).reshape(-1))
-    # attention against float64 attention over the oracle's values: prefill and
-    # flushed tails with their fp16 scales, the open tail with the fp32 scale
-    kk = [oracle_fp16_values(k0)] + [oracle_fp16_values(torch.cat(toks_k[i * T:(i + 1) * T], 2)
-                                                        .reshape(B, H * T, 1, D)).reshape(B, H, T, D)
-                                     for i in range(2)]
-    vv = [oracle_fp16_values(v0)] + [oracle_fp16_values(torch.cat(toks_v[i * T:(i + 1) * T], 2)
-                                                        .reshape(B, H * T, 1, D)).reshape(B, H, T, D)
-                                     for i in range(2)]
-    # the open tail: each token as its own update() quantised it (a scale per token, fp32)
-    n_open = steps - 2 * T
-    for toks, dst in ((toks_k, kk), (toks_v, vv)):
-        per_tok = torch.cat(toks[2 * T:], 2).reshape(B, H * n_open, 1, D)
-        bits = _oracle_update_values(per_tok, 4)[0].reshape(B, H, n_open, D)
-        dst.append(torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16).double().numpy())
-    K = np.concatenate(kk, 2)
-    V = np.concatenate(vv, 2)
+
+    def update_bits(toks):  # tokens as their own update() quantised them: bf16 bits (B, H, n, D)
+        n = len(toks)
+        per_tok = torch.cat(toks, 2).reshape(B, H * n, 1, D)
+        return _oracle_update_values(per_tok, 4)[0].reshape(B, H, n, D)
+
+    def update_values(toks):
+        return torch.from_numpy(update_bits(toks).view(np.int16)).view(torch.bfloat16).double().numpy()
+
+    # the dense tail holds exactly update()'s values of the flushed tokens
+    assert np.array_equal(_bf16_bits(st.tail_dense_k[:, :, :2 * T]), update_bits(toks_k[:2 * T]))
+    assert np.array_equal(_bf16_bits(st.tail_dense_v[:, :, :2 * T]), update_bits(toks_v[:2 * T]))
+    # attention against float64 attention over the oracle's values: the prefill
+    # with its fp16 scales, every decode token as update() returned it
+    K = np.concatenate([oracle_fp16_values(k0), update_values(toks_k)], 2)
+    V = np.concatenate([oracle_fp16_values(v0), update_values(toks_v)], 2)
     gq = torch.Generator().manual_seed(10)
     q = torch.randn(B, H * G, 1, D, generator=gq) / math.sqrt(D)  # fp32: the output is fp32 too
     o = cache.decode_attention(0, q.cuda()).cpu().numpy().reshape(B, H * G, D)
