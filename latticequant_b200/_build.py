@@ -21,7 +21,8 @@ OBJ = os.path.join(HERE, "_build")
 HEADER = os.path.join(HERE, "..", "include", "latticequant_b200.h")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CFLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC"]
-LFLAGS = ["-shared", "-cudart", "static"]
+MAP = os.path.join(CSRC, "liblq_b200.map")
+LFLAGS = ["-shared", "-cudart", "static", "-Xlinker", "--version-script=" + MAP]
 
 
 def sources():
@@ -44,7 +45,7 @@ def _stale(target: str, deps) -> bool:
 
 
 def needs_build() -> bool:
-    return _stale(LIB, sources() + _headers())
+    return _stale(LIB, sources() + _headers() + [MAP])
 
 
 def _compile(nvcc: str, src: str, verbose: bool):

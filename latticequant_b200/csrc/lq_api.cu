@@ -209,6 +209,7 @@ using namespace lq;
 static inline unsigned grid_for(int64_t n, int t = 256) { return (unsigned)ceil_div(n, t); }
 
 extern "C" int lq_quantize_e8(const float *x, int64_t n, float scale, float *q_out, float *xhat, void *stream) {
+    LQ_NVTX_RANGE();
     if (n < 0) return LQ_ERR_INVALID;
     if (n == 0) return LQ_OK;
     if (!x || (!q_out && !xhat)) return LQ_ERR_INVALID;
@@ -217,6 +218,7 @@ extern "C" int lq_quantize_e8(const float *x, int64_t n, float scale, float *q_o
 }
 
 extern "C" int lq_e8_to_symbols(const float *q, int64_t n, int32_t *coset, int32_t *sym, void *stream) {
+    LQ_NVTX_RANGE();
     if (n < 0) return LQ_ERR_INVALID;
     if (n == 0) return LQ_OK;
     if (!q || !coset || !sym) return LQ_ERR_INVALID;
@@ -225,6 +227,7 @@ extern "C" int lq_e8_to_symbols(const float *q, int64_t n, int32_t *coset, int32
 }
 
 extern "C" int lq_symbols_to_e8(const int32_t *coset, const int32_t *sym, int64_t n, float *q, void *stream) {
+    LQ_NVTX_RANGE();
     if (n < 0) return LQ_ERR_INVALID;
     if (n == 0) return LQ_OK;
     if (!coset || !sym || !q) return LQ_ERR_INVALID;
@@ -234,6 +237,7 @@ extern "C" int lq_symbols_to_e8(const int32_t *coset, const int32_t *sym, int64_
 
 extern "C" int lq_check_e8(const float *q, int64_t n, float atol, int bits, uint8_t *valid, uint8_t *coset,
                            uint8_t *in_range, void *stream) {
+    LQ_NVTX_RANGE();
     if (n < 0 || bits < 0 || bits > 30) return LQ_ERR_INVALID;
     if (n == 0) return LQ_OK;
     if (!q) return LQ_ERR_INVALID;
@@ -242,6 +246,7 @@ extern "C" int lq_check_e8(const float *q, int64_t n, float atol, int bits, uint
 }
 
 extern "C" int lq_pack_bits(const uint8_t *in, int64_t n, uint8_t *out, void *stream) {
+    LQ_NVTX_RANGE();
     if (n < 0) return LQ_ERR_INVALID;
     if (n == 0) return LQ_OK;
     if (!in || !out) return LQ_ERR_INVALID;
@@ -250,6 +255,7 @@ extern "C" int lq_pack_bits(const uint8_t *in, int64_t n, uint8_t *out, void *st
 }
 
 extern "C" int lq_unpack_bits(const uint8_t *in, int64_t n, uint8_t *out, void *stream) {
+    LQ_NVTX_RANGE();
     if (n < 0) return LQ_ERR_INVALID;
     if (n == 0) return LQ_OK;
     if (!in || !out) return LQ_ERR_INVALID;
@@ -259,6 +265,7 @@ extern "C" int lq_unpack_bits(const uint8_t *in, int64_t n, uint8_t *out, void *
 
 extern "C" int lq_map_symbols(const int64_t *sym, int64_t n, const int64_t *alphabet, int32_t n_alpha, int contiguous,
                               int32_t *out, void *stream) {
+    LQ_NVTX_RANGE();
     if (n < 0 || n_alpha <= 0) return LQ_ERR_INVALID;
     if (n == 0) return LQ_OK;
     if (!sym || !alphabet || !out) return LQ_ERR_INVALID;
@@ -270,6 +277,7 @@ extern "C" int lq_rans_encode_streams(const int32_t *sym_idx, const int64_t *sym
                                       const int32_t *table_id, const int32_t *tab_nsym, const uint32_t *enc_tab,
                                       int64_t n_streams, const int64_t *slot_off, uint32_t *slots, int64_t *nbits,
                                       uint32_t *state, uint32_t *err, void *stream) {
+    LQ_NVTX_RANGE();
     if (n_streams < 0) return LQ_ERR_INVALID;
     if (n_streams == 0) return LQ_OK;
     if (!sym_idx || !sym_off || !n_sym || !table_id || !tab_nsym || !enc_tab || !slot_off || !slots || !nbits ||
@@ -282,6 +290,7 @@ extern "C" int lq_rans_encode_streams(const int32_t *sym_idx, const int64_t *sym
 
 extern "C" int lq_rans_finish_streams(const uint32_t *slots, const int64_t *slot_off, const int64_t *nbits,
                                       int64_t n_streams, const int64_t *dst_off, uint32_t *dst, void *stream) {
+    LQ_NVTX_RANGE();
     if (n_streams < 0) return LQ_ERR_INVALID;
     if (n_streams == 0) return LQ_OK;
     if (!slots || !slot_off || !nbits || !dst_off || !dst) return LQ_ERR_INVALID;

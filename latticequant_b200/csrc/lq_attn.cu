@@ -460,6 +460,7 @@ extern "C" int lq_attn_decode(const lq_chunk_view *k, const lq_chunk_view *v, co
                               int head_dim, float sm_scale, void *out, int out_dtype, float *lse,
                               const uint32_t *tok_mask, void *workspace, size_t workspace_bytes, uint32_t *err,
                               void *stream) {
+    LQ_NVTX_RANGE();
     if (!view_ok(k) || !view_ok(v) || !q || !out || !workspace || batch <= 0 || n_kv_heads <= 0 || seq_len <= 0)
         return LQ_ERR_INVALID;
     if (k->n_heads != v->n_heads || k->bph != v->bph || k->tile_blocks != v->tile_blocks) return LQ_ERR_INVALID;
@@ -517,6 +518,7 @@ extern "C" int lq_attn_decode(const lq_chunk_view *k, const lq_chunk_view *v, co
 
 extern "C" int lq_stage_tables(const uint32_t *dec_tab, const int32_t *tab_lo, int64_t n_tables, uint32_t *staged,
                                void *stream) {
+    LQ_NVTX_RANGE();
     if (n_tables < 0 || n_tables > 0x7fffffff) return LQ_ERR_INVALID;
     if (n_tables == 0) return LQ_OK;
     if (!dec_tab || !tab_lo || !staged || (reinterpret_cast<uintptr_t>(staged) & 15)) return LQ_ERR_INVALID;

@@ -1197,6 +1197,7 @@ extern "C" int lq_attn_decode_compact(const lq_compact_view *k, const lq_compact
                                       int64_t batch, int64_t n_kv_heads, int64_t seq_len, int group, int head_dim,
                                       float sm_scale, void *out, int out_dtype, float *lse, void *workspace,
                                       size_t workspace_bytes, uint32_t *err, void *stream) {
+    LQ_NVTX_RANGE();
     if (!q || !out || !workspace || batch <= 0 || n_kv_heads <= 0 || seq_len <= 0) return LQ_ERR_INVALID;
     if (head_dim != 64 && head_dim != 128) return LQ_ERR_INVALID;
     const int64_t heads = batch * n_kv_heads, bph = seq_len * (head_dim / 8);

@@ -205,6 +205,7 @@ extern "C" int lq_attn_dense_merge(const void *q, int q_dtype, int n_seg, const 
                                    const int64_t *const *last_seg, int kv_dtype, const float *o_parts,
                                    const float *lse_parts, int64_t n_parts, int64_t batch, int64_t n_kv_heads,
                                    int group, int head_dim, float sm_scale, void *out, float *lse, void *stream) {
+    LQ_NVTX_RANGE();
     if (n_seg < 0 || n_seg > LQ_DENSE_MAX_SEGMENTS || n_parts < 0 || batch <= 0 || n_kv_heads <= 0 || group < 1 ||
         group > kDenseMaxG || (head_dim != 64 && head_dim != 128))
         return LQ_ERR_INVALID;

@@ -105,6 +105,7 @@ using namespace lq;
 
 extern "C" int lq_attn_merge(const float *o_parts, const float *lse_parts, int64_t n_parts, int64_t rows,
                              int head_dim, void *out, int out_dtype, float *lse, void *stream) {
+    LQ_NVTX_RANGE();
     if (n_parts < 0 || rows < 0 || head_dim <= 0 || head_dim > 1024) return LQ_ERR_INVALID;
     if (n_parts == 0 || rows == 0) return n_parts == 0 && rows > 0 ? LQ_ERR_INVALID : LQ_OK;
     if (!o_parts || !lse_parts || !out || rows > 0x7fffffff) return LQ_ERR_INVALID;
@@ -114,6 +115,7 @@ extern "C" int lq_attn_merge(const float *o_parts, const float *lse_parts, int64
 
 extern "C" int lq_attn_merge_packed(const float *parts, int64_t n_parts, int64_t rows, int head_dim, void *out,
                                     int out_dtype, float *lse, void *stream) {
+    LQ_NVTX_RANGE();
     if (n_parts < 0 || rows < 0 || head_dim <= 0 || head_dim > 1024) return LQ_ERR_INVALID;
     if (n_parts == 0 || rows == 0) return n_parts == 0 && rows > 0 ? LQ_ERR_INVALID : LQ_OK;
     if (!parts || !out || rows > 0x7fffffff) return LQ_ERR_INVALID;

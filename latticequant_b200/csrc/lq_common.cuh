@@ -4,6 +4,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 #include <stdint.h>
 
 #include "../../include/latticequant_b200.h"
@@ -23,6 +24,32 @@ inline int check_launch() {
 }
 
 inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// One NVTX range per C entry point that enqueues work, named after the
+// function, in the "latticequant_b200" domain: profilers (Nsight Systems,
+// ncu's NVTX filters) see which library call launched each kernel.  NVTX 3
+// is header-only; with no tool attached a push or pop is one indirect call
+// that returns at once.
+inline nvtxDomainHandle_t nvtx_domain() {
+    static nvtxDomainHandle_t d = nvtxDomainCreateA("latticequant_b200");
+    return d;
+}
+
+struct NvtxRange {
+    explicit NvtxRange(const char *name) {
+        nvtxEventAttributes_t e = {};
+        e.version = NVTX_VERSION;
+        e.size = NVTX_EVENT_ATTRIB_STRUCT_SIZE;
+        e.messageType = NVTX_MESSAGE_TYPE_ASCII;
+        e.message.ascii = name;
+        nvtxDomainRangePushEx(nvtx_domain(), &e);
+    }
+    ~NvtxRange() { nvtxDomainRangePop(nvtx_domain()); }
+    NvtxRange(const NvtxRange &) = delete;
+    NvtxRange &operator=(const NvtxRange &) = delete;
+};
+
+#define LQ_NVTX_RANGE() const ::lq::NvtxRange lq_nvtx_range_(__func__)
 
 __device__ inline void raise_flag(uint32_t *err, uint32_t f) {
     if (err) atomicOr(err, f);

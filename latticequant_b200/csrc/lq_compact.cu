@@ -177,6 +177,7 @@ __global__ void selftest_fastdiv_kernel(const uint32_t *__restrict__ num, int64_
 }  // namespace lq
 
 extern "C" int lq_selftest(int which, const void *a, const void *b, int64_t n, uint32_t d, void *out, void *stream) {
+    LQ_NVTX_RANGE();
     if (n < 0 || !out || !a) return LQ_ERR_INVALID;
     if (n == 0) return LQ_OK;
     const unsigned g = (unsigned)lq::ceil_div(n, 256);
@@ -210,6 +211,7 @@ extern "C" const char *lq_strerror(int status) {
 }
 
 extern "C" int lq_pack_e8(const float *q, int64_t n, int bits, uint8_t *out, uint32_t *n_bad, void *stream) {
+    LQ_NVTX_RANGE();
     if (n < 0 || bits < 3 || bits > 5) return LQ_ERR_INVALID;
     if (!n_bad) return LQ_ERR_INVALID;
     cudaStream_t st = lq::as_stream(stream);
@@ -222,6 +224,7 @@ extern "C" int lq_pack_e8(const float *q, int64_t n, int bits, uint8_t *out, uin
 
 extern "C" int lq_unpack_e8(const uint8_t *packed, int64_t n, int bits, const float *scales, const int32_t *head_idx,
                             float *q_out, uint16_t *f16_out, void *stream) {
+    LQ_NVTX_RANGE();
     if (n < 0 || bits < 3 || bits > 5) return LQ_ERR_INVALID;
     if (n == 0) return LQ_OK;
     if (!packed || (!q_out && !f16_out) || (f16_out && (!scales || !head_idx))) return LQ_ERR_INVALID;
@@ -235,6 +238,7 @@ extern "C" int lq_compact_merge(const uint8_t *packed, int64_t n_repr, int bits,
                                 const int32_t *repr_rank, const int32_t *fb_rank, const uint16_t *fallback,
                                 int64_t n_fallback, const float *scales, int64_t n_heads, int64_t bph, uint16_t *out,
                                 uint32_t *err, void *stream) {
+    LQ_NVTX_RANGE();
     if (n_heads < 0 || bph <= 0 || bits < 3 || bits > 5 || n_repr < 0 || n_fallback < 0) return LQ_ERR_INVALID;
     const int64_t n = n_heads * bph;
     if (n == 0) return LQ_OK;

@@ -360,6 +360,7 @@ extern "C" int lq_e8_quantize(const void *x, int dtype, int64_t n_chunks, int64_
                               const float *scale_f32, int64_t tile_blocks, void *sym_cols, uint32_t *coset_words,
                               uint32_t *tile_n0, uint32_t *hist, void *deq, int deq_dtype, float *q_out,
                               uint32_t *err, void *stream) {
+    LQ_NVTX_RANGE();
     const lq::OutlierArgs off{0, 1, nullptr, nullptr, nullptr, 0};
     return lq::quantize_entry(x, dtype, n_chunks, n_heads, bph, scale_f32, tile_blocks, sym_cols, coset_words, tile_n0,
                               hist, deq, deq_dtype, q_out, off, err, stream);
@@ -371,6 +372,7 @@ extern "C" int lq_e8_quantize_outliers(const void *x, int dtype, int64_t n_chunk
                                        int deq_dtype, float *q_out, int limit, int blocks_per_token,
                                        uint32_t *outlier_words, int32_t *outlier_rec, uint32_t *outlier_count,
                                        int64_t outlier_cap, uint32_t *err, void *stream) {
+    LQ_NVTX_RANGE();
     if (limit <= 0 || limit > 0x3fffffff || blocks_per_token <= 0 || blocks_per_token > 32 ||
         (blocks_per_token & (blocks_per_token - 1)) || (tile_blocks % blocks_per_token) || (bph % blocks_per_token) ||
         !outlier_rec || !outlier_count || outlier_cap < 0 || outlier_cap > 0x7fffffff)
@@ -387,6 +389,7 @@ extern "C" int lq_e8_quantize_outliers(const void *x, int dtype, int64_t n_chunk
 extern "C" int lq_patch_outliers(const int32_t *outlier_rec, const uint32_t *outlier_count, int64_t n_chunks,
                                  int64_t outlier_cap, int64_t n_heads, int64_t bph, const uint16_t *scale_f16,
                                  void *out, int out_dtype, int32_t *sym_out, uint32_t *err, void *stream) {
+    LQ_NVTX_RANGE();
     if (n_chunks < 0 || outlier_cap < 0 || n_heads < 0 || bph <= 0 || outlier_cap > 0x7fffffff) return LQ_ERR_INVALID;
     if (n_chunks == 0 || outlier_cap == 0 || n_heads == 0) return LQ_OK;
     if (!outlier_rec || !outlier_count || (!out && !sym_out) || (out && !scale_f16) || n_chunks > 65535 ||
@@ -413,6 +416,7 @@ extern "C" int lq_patch_outliers(const int32_t *outlier_rec, const uint32_t *out
 }
 
 extern "C" int lq_encode_e8(const float *x, int64_t n, float *out, int d8_only, void *stream) {
+    LQ_NVTX_RANGE();
     if (n < 0) return LQ_ERR_INVALID;
     if (n == 0) return LQ_OK;
     if (!x || !out) return LQ_ERR_INVALID;

@@ -583,6 +583,7 @@ extern "C" int lq_rans_encode(const void *sym_cols, const uint32_t *tile_n0, int
                               const uint32_t *enc_tab, uint32_t *words, int64_t words_cap, uint32_t *lane_off,
                               uint32_t *lane_nbits, uint32_t *lane_state, void *workspace, size_t workspace_bytes,
                               uint32_t *err, void *stream) {
+    LQ_NVTX_RANGE();
     if (n_chunks < 0 || n_vectors < 0 || tile_blocks <= 0 || (tile_blocks % 32) != 0 || words_cap < 0)
         return LQ_ERR_INVALID;
     if (!lane_off) return LQ_ERR_INVALID;
@@ -635,6 +636,7 @@ extern "C" int lq_rans_decode(const uint32_t *words, int64_t n_words, const uint
                                  const uint16_t *tab_freq, const uint32_t *dec_tab, const uint16_t *scale_f16,
                                  void *out, int out_dtype, int32_t *sym_out, void *workspace, size_t workspace_bytes,
                                  uint32_t *err, void *stream) {
+    LQ_NVTX_RANGE();
     if (n_chunks < 0 || n_heads < 0 || bph < 0 || tile_blocks <= 0 || (tile_blocks % 32) != 0 || n_words < 0)
         return LQ_ERR_INVALID;
     const int64_t N = n_heads * bph;
@@ -708,6 +710,7 @@ extern "C" int lq_rans_decode_streams(const uint32_t *bitstream, int64_t n_words
                                       const int32_t *alphabet, const int32_t *table_id, int64_t max_sym,
                                       int64_t n_streams, int64_t *out, const int64_t *out_offsets, uint32_t *err,
                                       void *stream) {
+    LQ_NVTX_RANGE();
     if (n_streams < 0 || max_sym < 0 || n_words < 0) return LQ_ERR_INVALID;
     if (n_streams == 0) return LQ_OK;
     if (!bitstream || !bit_offsets || !n_bits || !init_states || !n_decode || !lookup || !freqs || !cumfreqs ||

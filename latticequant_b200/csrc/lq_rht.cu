@@ -44,6 +44,7 @@ __global__ void fwht_kernel(const float *__restrict__ x, int d, int log2d, const
 
 extern "C" int lq_fwht(const float *x, int64_t n_vec, int d, const float *pre_signs, const float *post_signs,
                        float *out, void *stream) {
+    LQ_NVTX_RANGE();
     if (n_vec < 0 || d < 2 || d > 4096 || (d & (d - 1)) != 0) return LQ_ERR_INVALID;
     if (n_vec == 0) return LQ_OK;
     if (!x || !out || n_vec > 0x7fffffff) return LQ_ERR_INVALID;

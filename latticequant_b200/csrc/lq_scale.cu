@@ -281,6 +281,7 @@ extern "C" size_t lq_head_scales_workspace(int64_t n_heads_total, int64_t elems_
 extern "C" int lq_head_scales(const void *x, int dtype, int64_t n_heads_total, int64_t elems_per_head,
                               float vol_mult, float *sigma2, float *scale_f32, uint16_t *scale_f16, void *workspace,
                               size_t workspace_bytes, void *stream) {
+    LQ_NVTX_RANGE();
     if (n_heads_total < 0 || elems_per_head < 0) return LQ_ERR_INVALID;
     if (n_heads_total == 0) return LQ_OK;
     if (x == nullptr || elems_per_head == 0) return LQ_ERR_INVALID;
@@ -358,6 +359,7 @@ int static_scratch_for_current_device(float **out) {
 extern "C" int lq_head_scales_static(const void *x, int dtype, int64_t n_heads_total, int64_t elems_per_head,
                                      float vol_mult, float *sigma2, float *scale_f32, uint16_t *scale_f16,
                                      void *stream) {
+    LQ_NVTX_RANGE();
     if (n_heads_total < 0 || elems_per_head < 0) return LQ_ERR_INVALID;
     if (n_heads_total == 0) return LQ_OK;
     if (x == nullptr || elems_per_head == 0) return LQ_ERR_INVALID;

@@ -303,6 +303,7 @@ __global__ void __launch_bounds__(kTT) expand_tables_kernel(const int32_t *__res
 
 extern "C" int lq_build_tables(const uint32_t *hist, int64_t n_tables, int32_t *tab_lo, int32_t *tab_nsym,
                                uint16_t *tab_freq, uint32_t *err, void *stream) {
+    LQ_NVTX_RANGE();
     if (n_tables < 0) return LQ_ERR_INVALID;
     if (n_tables == 0) return LQ_OK;
     if (!hist || !tab_lo || !tab_nsym || !tab_freq) return LQ_ERR_INVALID;
@@ -313,6 +314,7 @@ extern "C" int lq_build_tables(const uint32_t *hist, int64_t n_tables, int32_t *
 
 extern "C" int lq_expand_tables(const int32_t *tab_nsym, const uint16_t *tab_freq, int64_t n_tables,
                                 uint32_t *enc_tab, uint32_t *dec_tab, uint32_t *err, void *stream) {
+    LQ_NVTX_RANGE();
     if (n_tables < 0) return LQ_ERR_INVALID;
     if (n_tables == 0) return LQ_OK;
     if (!tab_nsym || !tab_freq || (!enc_tab && !dec_tab)) return LQ_ERR_INVALID;
