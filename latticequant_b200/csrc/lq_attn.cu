@@ -56,12 +56,6 @@ __host__ __device__ constexpr int attn_threads() {
     return G <= 2 ? 768 : G <= 4 ? 640 : 512;
 }
 
-// Fused attention partial of CTA `cx` of head `head`.  BPT = blocks per
-// token = head_dim / 8.  CHECKED = false decodes optimistically and records
-// in a.redo whether a lane read past its bits (only a malformed stream
-// does); attn_redo_kernel then recomputes those CTAs with CHECKED = true.
-// Keeping the exact decode out of the main kernel keeps that kernel to one
-// copy of the decoder and within its registers.
 // The 16 tables of a chunk in their shared-memory form (smem_entry), so a
 // CTA can fill its table region with one bulk copy.
 __global__ void staged_tables_kernel(const uint32_t *__restrict__ dec_tab, const int32_t *__restrict__ tab_lo,
@@ -74,6 +68,47 @@ __global__ void staged_tables_kernel(const uint32_t *__restrict__ dec_tab, const
         out[(size_t)t * LQ_L + i] = smem_entry(dec_tab[(size_t)t * LQ_L + i], lo, c, mul);
 }
 
+// Per-head sums of the G partial dots a token's BPT lanes hold, transposed
+// on the way: with H (G rounded up to a power of two, H <= BPT) values per
+// lane, each of the first log2(H) butterfly steps keeps half of the heads
+// the lane carries and sends its partner the other half, so those steps
+// move H/2, H/4, ..., 1 values instead of G each; the rest is a plain
+// butterfly.  Lane jc ends with head jc / (BPT / H) summed over all BPT
+// lanes (heads G..H-1 are zero padding).
+template <int G>
+__host__ __device__ constexpr int pow2_heads() {
+    return G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8;
+}
+
+template <int G, int BPT>
+__device__ __forceinline__ float head_sums_transposed(const float (&dot)[G], uint32_t jc) {
+    constexpr int H = pow2_heads<G>();
+    static_assert(H <= BPT, "one lane per head at least");
+    float a[H];
+#pragma unroll
+    for (int i = 0; i < H; ++i) a[i] = i < G ? dot[i < G ? i : 0] : 0.0f;
+#pragma unroll
+    for (int n = H, o = BPT / 2; n > 1; n >>= 1, o >>= 1) {
+        const bool up = (jc & (uint32_t)o) != 0u;
+#pragma unroll
+        for (int i = 0; i < n / 2; ++i) {
+            const float keep = up ? a[n / 2 + i] : a[i];
+            const float send = up ? a[i] : a[n / 2 + i];
+            a[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+    }
+    float s = a[0];
+#pragma unroll
+    for (int o = BPT / (2 * H); o >= 1; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    return s;
+}
+
+// Fused attention partial of CTA `cx` of head `head`.  BPT = blocks per
+// token = head_dim / 8.  CHECKED = false decodes optimistically and records
+// in a.redo whether a lane read past its bits (only a malformed stream
+// does); attn_redo_kernel then recomputes those CTAs with CHECKED = true.
+// Keeping the exact decode out of the main kernel keeps that kernel to one
+// copy of the decoder and within its registers.
 template <int G, int BPT, int QDT, bool CHECKED>
 __device__ __forceinline__ void attn_partial_cta(const AttnArgs &a, uint32_t cx, uint32_t head) {
     static_assert(BPT == 8 || BPT == 16, "head_dim 64 or 128");
@@ -147,33 +182,9 @@ __device__ __forceinline__ void attn_partial_cta(const AttnArgs &a, uint32_t cx,
             const uint32_t jc = j % BPT;
             const uint32_t tok = grp * TPG + j / BPT;
             float *row = sc + ((uint32_t)t * a.tpt + tok) * GP;
-            if constexpr (G == 4 && BPT == 16) {
-                // transposing reduction over the token's 16 lanes: halve the
-                // heads a lane carries at each of the first two steps
-                const bool h8 = (jc & 8u) != 0, h4 = (jc & 4u) != 0;
-                float a0 = h8 ? dot[2] : dot[0], a1 = h8 ? dot[3] : dot[1];
-                const float s0 = h8 ? dot[0] : dot[2], s1 = h8 ? dot[1] : dot[3];
-                a0 += __shfl_xor_sync(0xffffffffu, s0, 8);
-                a1 += __shfl_xor_sync(0xffffffffu, s1, 8);
-                float bsum = h4 ? a1 : a0;
-                bsum += __shfl_xor_sync(0xffffffffu, h4 ? a0 : a1, 4);
-                bsum += __shfl_xor_sync(0xffffffffu, bsum, 2);
-                bsum += __shfl_xor_sync(0xffffffffu, bsum, 1);
-                // lane jc holds head (jc >> 2) & 3 (bit 3 picked heads 2-3, bit 2 the odd one)
-                if (ok && (jc & 3u) == 0) row[jc >> 2] = bsum;
-            } else {
-#pragma unroll
-                for (int off = BPT / 2; off >= 1; off >>= 1) {
-#pragma unroll
-                    for (int g = 0; g < G; ++g) dot[g] += __shfl_xor_sync(0xffffffffu, dot[g], off);
-                }
-                if (ok && jc < (uint32_t)G) {
-                    float v = dot[0];
-#pragma unroll
-                    for (int g = 1; g < G; ++g) v = (jc == (uint32_t)g) ? dot[g] : v;
-                    row[jc] = v;
-                }
-            }
+            constexpr uint32_t LPH = BPT / pow2_heads<G>();  // lanes per head after the transposing steps
+            const float hs = head_sums_transposed<G, BPT>(dot, jc);
+            if (ok && jc % LPH == 0u && jc / LPH < (uint32_t)G) row[jc / LPH] = hs;
         };
         if (decode_two_tiles_ordered<kAttnRing, CHECKED>(a.k, 0, tile0, act0, act1, dta, ring, epi_k, a.err))
             s_overrun = 1u;
