@@ -471,11 +471,16 @@ __global__ void __launch_bounds__(kCompactThreads, G <= 4 ? 2 : 1) attn_compact_
 // per group of 16 tokens: A = V^T (rows channels, columns tokens); lane
 // (g, t) decodes blocks 2g and 2g+1 of tokens 2t, 2t+1, 2t+8, 2t+9 and pairs
 // their channels across tokens with byte permutes; B = p^T.
-constexpr int kMThreads = 256;
-constexpr int kMWarps = kMThreads / 32;  // 8 warps: 16 tokens each per stage
-constexpr int kMStageTok = 128;          // tokens per stage
-constexpr int kMRing = 4;                // stage buffers: three in flight while one is read
-constexpr int kMFbCap = 768;             // fallback rows a stage buffer holds (3/8 of its blocks)
+// Four CTAs of 4 warps per SM (128 registers a thread, 47 KB of shared memory
+// a CTA): a stage barrier holds 4 warps, not 8.  Against two CTAs of 8 warps
+// with 128-token stages and three stages in flight, config 3 went from 0.557
+// to 0.510 ms; 2-warp CTAs with 32-token stages (eight per SM) and 4-warp
+// CTAs over 512 tokens with three 64-token stages in flight were no faster.
+constexpr int kMThreads = 128;
+constexpr int kMWarps = kMThreads / 32;  // 4 warps: 16 tokens each per stage
+constexpr int kMStageTok = 64;           // tokens per stage
+constexpr int kMRing = 3;                // stage buffers: two in flight while one is read
+constexpr int kMFbCap = 384;             // fallback rows a stage buffer holds (3/8 of its blocks)
 constexpr int kMTokPerCta = 1024;
 
 template <bool B4>
@@ -773,7 +778,7 @@ __device__ __forceinline__ void mblock_fast(int bits, uint32_t cw, uint32_t fw, 
 }
 
 template <int G, int QDT, bool B4>
-__global__ void __launch_bounds__(kMThreads, 2) attn_compact_mma_kernel(CompactArgs a) {
+__global__ void __launch_bounds__(kMThreads, 4) attn_compact_mma_kernel(CompactArgs a) {
     static_assert(G >= 1 && G <= 4, "query groups of up to 4 heads");
     using S = MStage<B4>;
     constexpr int D = 128, GP = 4;
@@ -828,7 +833,7 @@ __global__ void __launch_bounds__(kMThreads, 2) attn_compact_mma_kernel(CompactA
     __syncthreads();
 
     // the stages of both phases stream through a ring of kMRing buffers: K
-    // stages 0..nst-1, then V stages, three ahead of the one being read
+    // stages 0..nst-1, then V stages, two ahead of the one being read
     const uint32_t n_seq = 2 * nst;
     auto issue = [&](uint32_t q) {
         if (q < n_seq) {
@@ -853,7 +858,6 @@ __global__ void __launch_bounds__(kMThreads, 2) attn_compact_mma_kernel(CompactA
     };
     issue(0);
     issue(1);
-    issue(2);
 
     const float fk_score = mk.u * a.qk_log2;
     float m_[G], l_[G];
@@ -873,7 +877,7 @@ __global__ void __launch_bounds__(kMThreads, 2) attn_compact_mma_kernel(CompactA
         const CStageSpan s = spans[ph][st];
         const CompactDev &c = ph ? a.v : a.k;
         const uint32_t buf = bufs + (q % kMRing) * S::kBytes;
-        cp_async_wait<2>();
+        cp_async_wait<1>();
         // a copy that never completes leaves the flag raised and stale data,
         // which every index below stays inside
         mbar_wait(smem_addr(&s_bar[q % kMRing]), (q / kMRing) & 1u, a.err);
@@ -924,7 +928,7 @@ __global__ void __launch_bounds__(kMThreads, 2) attn_compact_mma_kernel(CompactA
             __syncwarp();
         }
         __syncthreads();
-        issue(q + 3);  // into the buffer read in the previous iteration
+        issue(q + 2);  // into the buffer read in the previous iteration
 
         const uint32_t tw = st * kMStageTok + (uint32_t)warp * 16;  // the warp's first token, CTA-relative
         const uint32_t b0 = stage_b0(st);
@@ -1078,15 +1082,16 @@ struct CompactPlan {
     uint32_t nct, tok_per_cta;
     size_t smem, part_floats;
     bool cuda_cores;  // force the CUDA-core kernel (LQ_ATTN_CUDA_CORES set)
+    bool mma;         // the tensor-core kernel runs (head_dim 128, up to 4 query heads per KV head)
 };
 
 int compact_plan(int64_t n_heads, int64_t seq, int G, int D, CompactPlan *p) {
     if (n_heads <= 0 || seq <= 0 || G < 1 || G > 8 || (D != 64 && D != 128)) return LQ_ERR_INVALID;
     const int bpt = D / 8;
     if ((seq * bpt) % 32 != 0 || n_heads > 65535 || n_heads * seq * bpt >= ((int64_t)1 << 31)) return LQ_ERR_INVALID;
-    static_assert(kCTokPerCta == kMTokPerCta, "both kernels write the same partials");
-    p->tok_per_cta = kCTokPerCta;
     p->cuda_cores = getenv("LQ_ATTN_CUDA_CORES") != nullptr;
+    p->mma = D == 128 && G <= 4 && !p->cuda_cores;
+    p->tok_per_cta = p->mma ? kMTokPerCta : kCTokPerCta;
     p->nct = (uint32_t)ceil_div(seq, p->tok_per_cta);
     const size_t gp = (size_t)((G + 3) & ~3);
     const size_t stages = 2 * (size_t)(bpt == 16 ? CStage<16>::kBytes : CStage<8>::kBytes);
@@ -1149,11 +1154,12 @@ int launch_mma_q(const CompactArgs &a, const CompactPlan &p, uint32_t n_heads, i
 }
 
 // head_dim 128 with up to 4 query heads per KV head takes the tensor-core
-// kernel; other shapes the CUDA-core kernel.  Both write the same partials.
+// kernel; other shapes the CUDA-core kernel.  Both write partials in the same
+// layout, [heads][tok_per_cta slices][G][D + 2], each with its own tok_per_cta.
 template <int G>
 int launch_compact_g(const CompactArgs &a, const CompactPlan &p, uint32_t n_heads, int q_dtype, int D, cudaStream_t st) {
     if constexpr (G <= 4) {
-        if (D == 128 && !p.cuda_cores) return launch_mma_q<G>(a, p, n_heads, q_dtype, st);
+        if (p.mma) return launch_mma_q<G>(a, p, n_heads, q_dtype, st);
     }
     return D == 128 ? launch_compact_q<G, 16>(a, p, n_heads, q_dtype, st)
                     : launch_compact_q<G, 8>(a, p, n_heads, q_dtype, st);
