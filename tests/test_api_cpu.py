@@ -38,6 +38,19 @@ def test_library_exports_every_declared_symbol(cabi):
         assert hasattr(cabi, n), n
 
 
+def test_library_exports_only_the_declared_abi(cabi):
+    """The export map keeps internal C++ helpers and the static CUDA runtime
+    local: the dynamic symbol table holds exactly the header's lq_* names."""
+    import shutil
+    import subprocess
+
+    if shutil.which("nm") is None:
+        pytest.skip("nm not available")
+    out = subprocess.run(["nm", "-D", "--defined-only", LIB], capture_output=True, text=True, check=True).stdout
+    exported = {ln.split()[-1] for ln in out.splitlines() if len(ln.split()) == 3}
+    assert exported == set(_declared()), sorted(exported ^ set(_declared()))
+
+
 def test_host_only_entry_points(cabi):
     cabi.lq_version.restype = ctypes.c_int
     cabi.lq_strerror.restype = ctypes.c_char_p
