@@ -72,9 +72,12 @@ C4_LAYERS, C4_KV, C4_B, C4_S, C4_D, C4_G = 28, 4, 4, 131072, 128, 7
 # compressed byte of the attention kernel, measured with ncu
 # (dram__bytes_read.sum + dram__bytes_write.sum) on the 8-layer config-2 case
 # (decode: the full-size capture, whose bf16 output no longer fits L2) and
-# the full config-3 step; scaled to each launch for roofline.traffic.
+# the full config-3 step (rANS lanes; compact layout: 943.4 MB read + 13.8 MB
+# written against 937.0 MB algorithmic); scaled to each launch for
+# roofline.traffic.
 TRAFFIC_PER_BLOCK = {"scales": 16.0, "quantize": 23.0, "encode": 20.6, "decode": 20.2}
 ATTN_TRAFFIC_PER_ALG_BYTE = 602.4 / 583.6
+COMPACT_TRAFFIC_PER_ALG_BYTE = (943.4 + 13.8) / 937.0
 
 
 def make_cache(gen_device, seed, n_layers=N_LAYERS):
@@ -452,9 +455,11 @@ def bench_attention_compact(dev, rank, world, steps, warmup, barrier):
             "layout": "compact fixed-rate, 4 bits: 4-byte codes + fp16 fallback rows "
                       "(llm/fused_triton_merge.py format)",
             "fallback_share": oor2 / (2 * world), "bytes_per_step_GB": tot_bytes / 1e9,
-            "roofline": {"bound": "hbm", "kernel": "attn_compact_kernel + attn_combine_kernel",
+            "roofline": {"bound": "hbm", "kernel": "attn_compact_mma_kernel + attn_combine_kernel",
                          "achieved": gbps / world, "peak": peak, "unit": "GB/s per GPU",
-                         "frac": gbps / world / peak, "peak_kind": peak_kind},
+                         "frac": gbps / world / peak, "peak_kind": peak_kind,
+                         "traffic": tot_bytes / world * COMPACT_TRAFFIC_PER_ALG_BYTE / 1e9,
+                         "traffic_unit": "GB per launch", "algorithmic_GB": tot_bytes / world / 1e9},
             "gpu_launches": steps * 2}
 
 
